@@ -1,0 +1,68 @@
+"""The C restatement (full-size oracle) against the numpy restatement at small dims."""
+import numpy as np
+import pytest
+
+from oracle import corc
+from oracle import ref_np as R
+from oracle import synth_np as sy
+
+SMALL = R.Dims(H=256, M=384, NH=8, NKV=2, HD=32, L=2, V=300)
+
+
+@pytest.mark.parametrize("seed,tid,start,n,sigma", [(0, 0, 0, 1000, 0.02), (7, 0x7001, 12345, 777, 1.0),
+                                                     (2**40 + 3, 31 * 16 + 6, 2**33, 64, 0.02)])
+def test_gauss_bits_c_equals_numpy(seed, tid, start, n, sigma):
+    a = corc.gauss_bf16_bits(seed, tid, n, sigma, start)
+    b = sy.gauss_bf16_bits(seed, tid, n, sigma, start)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_gauss_distribution():
+    x = sy.bf16_bits_to_f32(sy.gauss_bf16_bits(3, 9, 200000, 0.02))
+    assert abs(x.mean()) < 2e-4 and abs(x.std() - 0.02) < 2e-4
+
+
+def _np_lane_cache(d, S, B, seeds, lens):
+    Ks = [np.zeros((B, d.NKV, d.HD, S), np.float32) for _ in range(d.L)]
+    Vs = [np.zeros((B, d.NKV, S, d.HD), np.float32) for _ in range(d.L)]
+    for b in range(B):
+        K, V = R.synth_kv(d, S, seeds[b], lens[b])
+        for l in range(d.L):
+            Ks[l][b], Vs[l][b] = K[l], V[l]
+    return Ks, Vs
+
+
+def test_decode_steps_c_equals_numpy():
+    d, S, B = SMALL, 16, 3
+    seeds, lens = [101, 102, 103], [4, 9, 1]
+    m = R.SynthModel(d, seed=0)
+    cm = corc.CModel(d, seed=0)
+    Kc, Vc = cm.new_cache(B, S)
+    for b in range(B):
+        cm.fill_lane(Kc, Vc, b, seeds[b], lens[b])
+    Ks, Vs = _np_lane_cache(d, S, B, seeds, lens)
+    np.testing.assert_array_equal(sy.bf16_bits_to_f32(Kc).transpose(0, 1, 2, 4, 3), np.stack(Ks))
+    toks, pos = [5, 299, 17], list(lens)
+    for _ in range(3):
+        nxt, lg, _ = cm.decode_step(toks, pos, Kc, Vc)
+        lg_ref = R.decode_step(m, toks, pos, Ks, Vs, S, kv_bf16=True)
+        np.testing.assert_allclose(lg, lg_ref, rtol=1e-4, atol=1e-4)
+        assert list(nxt) == R.greedy(lg_ref)
+        toks, pos = list(nxt), [p + 1 for p in pos]
+    Kn = sy.bf16_bits_to_f32(Kc).transpose(0, 1, 2, 4, 3)
+    np.testing.assert_allclose(Kn, np.stack(Ks), rtol=1e-2, atol=1e-2)
+    cm.close()
+
+
+def test_prefill_c_equals_numpy():
+    d, S = SMALL, 16
+    toks = [7, 3, 250, 11, 42, 0, 299]
+    m = R.SynthModel(d, seed=4)
+    cm = corc.CModel(d, seed=4)
+    K, V, lg, nxt, _ = cm.prefill(toks, S)
+    Kr, Vr, lgr = R.prefill(m, toks, S, kv_bf16=True)
+    np.testing.assert_allclose(sy.bf16_bits_to_f32(K), Kr, rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(sy.bf16_bits_to_f32(V), Vr, rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(lg, lgr, rtol=1e-4, atol=1e-4)
+    assert nxt == int(np.argmax(lgr))
+    cm.close()
