@@ -1,0 +1,128 @@
+/* rngd_b200.h — C ABI of the B200 kernels behind rngd-pd's hot path.
+ *
+ * Plain pointers, sizes and a stream handle; no torch or Python types.  The
+ * Python package rngd_pd (engines/, connector/, nvlink.py) binds these with
+ * ctypes; a C/C++/Go/Rust host can bind them the same way.
+ *
+ * Every function returns an int status: RNGD_OK (0) or a negative code, and
+ * records a message that rngd_last_error() copies out.  Device-side waits are
+ * bounded and come back as RNGD_ERR_TIMEOUT; nothing traps.  All launches are
+ * stream-ordered on the given stream (NULL = the legacy default stream).
+ *
+ * Reference interfaces each group replaces are cited per declaration
+ * (paths relative to the rngd-pd repository).
+ */
+#ifndef RNGD_B200_H
+#define RNGD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RNGD_OK 0
+#define RNGD_ERR_ARG (-1)         /* bad argument: shape, pointer, bound */
+#define RNGD_ERR_CUDA (-2)        /* a CUDA call or launch failed */
+#define RNGD_ERR_TIMEOUT (-3)     /* a bounded device/host wait ran out */
+#define RNGD_ERR_UNSUPPORTED (-4) /* a shape outside what the kernels are built for */
+
+typedef void* rngd_stream_t; /* cudaStream_t */
+
+/* ---------------------------------------------------------------- runtime */
+/* Copies the last error message of the calling thread (NUL-terminated). */
+int rngd_last_error(char* buf, size_t n);
+/* ABI version of this library (bumped when a struct below changes). */
+int rngd_abi_version(void);
+
+/* ------------------------------------------------------- synthetic inputs
+ * The reference serves a real checkpoint (src/rngd_pd/engines/decode_batch.py:
+ * 456-462 loads it with transformers); this build measures on seeded synthetic
+ * weights and KV instead.  Integer-only recipe, bit-identical to the CPU
+ * generator of the test oracle: splitmix64 hash of (seed, tid, index), sum of
+ * its four 16-bit fields (Irwin-Hall n=4) times `scale`, rounded to bf16. */
+int rngd_synth_gauss_bf16(void* dst, uint64_t n, uint64_t seed, uint64_t tid, uint64_t start,
+                          float scale, rngd_stream_t stream);
+/* dst[i] = (hash(seed, tid, start+i) >> 32) % hi as int32 (token ids, lengths). */
+int rngd_synth_uniform_i32(int32_t* dst, uint64_t n, uint64_t seed, uint64_t tid, uint64_t start,
+                           uint32_t hi, rngd_stream_t stream);
+
+/* ---------------------------------------------------------- model + decode
+ * Weights as the engine lays them out in HBM (bf16, K-major rows, i.e. the HF
+ * [out, in] layout), one contiguous block per kind over all layers. */
+typedef struct rngd_model {
+  int32_t H, M, NH, NKV, HD, L, V;
+  float eps;
+  const void* wqkv;      /* bf16 [L][(NH+2*NKV)*HD][H]: q rows, then k, then v */
+  const void* wo;        /* bf16 [L][H][NH*HD] */
+  const void* wgu;       /* bf16 [L][2*M][H]: gate/up interleaved in 64-row blocks */
+  const void* wd;        /* bf16 [L][H][M] */
+  const float* n1;       /* fp32 [L][H] input_layernorm */
+  const float* n2;       /* fp32 [L][H] post_attention_layernorm */
+  const float* norm;     /* fp32 [H] final norm */
+  const void* embed;     /* bf16 [V][H] */
+  const void* lm;        /* bf16 [V][H] */
+  const float* inv_freq; /* fp32 [HD/2] RoPE inverse frequencies (device) */
+} rngd_model_t;
+
+/* Per-engine decode state.  Lanes 0..B-1 of the resident cache are the B
+ * streams of the step; each has its own position (engines/decode_batch.py:422-442). */
+typedef struct rngd_decode_io {
+  int32_t B;            /* streams stepped (<= 16) */
+  int32_t Bcap;         /* lanes of the resident cache */
+  int32_t S;            /* cache width in positions (multiple of 128, <= 8192) */
+  int32_t kv_layers;    /* layers held by kcache/vcache (a layer group's block) */
+  void* kcache;         /* bf16 [kv_layers][Bcap][NKV][S][HD], first layer = layer0 of the call */
+  void* vcache;         /* bf16 [kv_layers][Bcap][NKV][S][HD] */
+  const int32_t* toks;  /* device [B] token ids of this step */
+  const int32_t* pos;   /* device [B] position each token is written at */
+  float* x;             /* fp32 [16][H] residual stream */
+  float* h;             /* fp32 [16][max(H, M)] normalised / gated activations */
+  float* qkv;           /* fp32 [16][(NH+2*NKV)*HD] */
+  float* q;             /* fp32 [16][NH*HD] rotated queries */
+  float* ao;            /* fp32 [16][NH*HD] attention output */
+  float* gu;            /* fp32 [16][2*M] */
+  float* logits;        /* fp32 [B][V] */
+  float* attn_part;     /* fp32 scratch [B][NH][S/128][HD+2] */
+  int32_t* next;        /* device [B] greedy next tokens */
+} rngd_decode_io_t;
+
+/* x = embed[toks] (engines/decode_batch.py:432). */
+int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream);
+/* Layers [layer0, layer1) of the batched decode step, updating the cache at
+ * pos[b]; io->kcache/vcache hold exactly those layers (layer1 - layer0 <=
+ * io->kv_layers), like the per-group cache of the reference (replaces DecodeModel.forward over one layer group,
+ * kernels/decode_batch.py:73-109, called from engines/decode_batch.py:436-439). */
+int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, int layer1,
+                       rngd_stream_t stream);
+/* Final norm + lm_head + first-max argmax into io->next; logits kept in
+ * io->logits (engines/decode_batch.py:440 and greedy_tokens 162-171). */
+int rngd_decode_lmhead(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream);
+
+/* toks[b] = next[b]; pos[b] += 1 for b < B: feeds a greedy step's output back as
+ * the next step's input on the device, so multi-step decoding needs no host
+ * round trip (the reference loops step() through the host,
+ * src/rngd_pd/serving/cluster.py:1374-1380). */
+int rngd_decode_advance(const rngd_decode_io_t* io, rngd_stream_t stream);
+
+/* ------------------------------------------------------ kernel-level ops
+ * Exposed for the parity tests and for hosts that build their own step. */
+/* Y[b][n] (+)= sum_k W[n][k] * X[b][k]; W bf16 [N][K] row-major, X/Y fp32,
+ * b < B <= 16, K % 8 == 0 (CUDA-core path, fp32 accumulation). */
+int rngd_gemv_bf16(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy,
+                   int accumulate, rngd_stream_t stream);
+/* out[r][k] = x[r][k] / sqrt(mean_k x^2 + eps) * w[k] (kernels/decode_batch.py:130). */
+int rngd_rmsnorm_f32(const float* x, int R, int H, const float* w, float eps, float* out,
+                     rngd_stream_t stream);
+/* Split-S decode attention for one layer: q fp32 [B][NH*HD] (already rotated),
+ * caches bf16 [Bcap][NKV][S][HD] of that layer, positions [B] -> ao fp32
+ * [B][NH*HD] (kernels/decode_batch.py:83-85 with the mask of :153). */
+int rngd_attn_decode(const float* q, const void* kc, const void* vc, const int32_t* pos, int B,
+                     int Bcap, int NH, int NKV, int HD, int S, float* part, float* ao,
+                     rngd_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RNGD_B200_H */

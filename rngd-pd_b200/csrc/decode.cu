@@ -1,0 +1,466 @@
+// Batched decode step for B <= 16 streams at independent positions.
+//
+// Replaces the reference's compiled decode graph (DecodeLayer.forward,
+// src/rngd_pd/kernels/decode_batch.py:73-91) and its lm_head + host argmax
+// (src/rngd_pd/engines/decode_batch.py:103-171).  The residual stream and all
+// accumulations stay fp32; only weights and the KV cache are bf16 (the cache
+// is written rounded to nearest even, exactly as the test oracle models it).
+//
+// Per layer:  rmsnorm -> QKV GEMV -> RoPE + KV append -> split-S attention
+//             -> O GEMV (+= residual) -> rmsnorm -> gate/up GEMV -> SwiGLU
+//             -> down GEMV (+= residual)
+// HBM-bound: the GEMVs stream 436 MB of weights per layer; activations are a
+// few hundred KB and stay in L1/L2.
+#include "common.cuh"
+
+namespace rngd {
+
+// ------------------------------------------------------------------ GEMV
+// One warp owns R consecutive rows; each lane streams 16-byte vectors of every
+// row at k = lane*8 + 256*i and keeps R*BT fp32 partial sums, reduced across
+// the warp at the end.  Activation rows are read through L1 (shared by the
+// CTA's 8 warps); weights bypass L1 (read once).
+template <int BT, int R>
+__global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ W, int N, int K,
+                                                   const float* __restrict__ X, int ldx, int B,
+                                                   float* __restrict__ Y, int ldy, int accumulate) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows_per_cta = 8 * R;
+  for (int n0 = blockIdx.x * rows_per_cta + warp * R; n0 < N; n0 += gridDim.x * rows_per_cta) {
+    float acc[R][BT];
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int b = 0; b < BT; b++) acc[r][b] = 0.f;
+#pragma unroll 2
+    for (int k = lane * 8; k < K; k += 256) {
+      float w[R][8];
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (n0 + r < N) v = ldg_nc_v4(W + (size_t)(n0 + r) * K + k);
+        unpack8(v, w[r]);
+      }
+#pragma unroll
+      for (int b = 0; b < BT; b++) {
+        if (b >= B) break;  // rows past B are neither read nor written
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(X + (size_t)b * ldx + k));
+        const float4 x1 = __ldg(reinterpret_cast<const float4*>(X + (size_t)b * ldx + k + 4));
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          float a = acc[r][b];
+          a = fmaf(w[r][0], x0.x, a); a = fmaf(w[r][1], x0.y, a);
+          a = fmaf(w[r][2], x0.z, a); a = fmaf(w[r][3], x0.w, a);
+          a = fmaf(w[r][4], x1.x, a); a = fmaf(w[r][5], x1.y, a);
+          a = fmaf(w[r][6], x1.z, a); a = fmaf(w[r][7], x1.w, a);
+          acc[r][b] = a;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int b = 0; b < BT; b++) {
+        float v = warp_sum(acc[r][b]);
+        // spread the stores over the lanes of the warp
+        if (lane == ((r * BT + b) & 31) && n0 + r < N && b < B) {
+          float* y = Y + (size_t)b * ldy + n0 + r;
+          *y = accumulate ? *y + v : v;
+        }
+      }
+  }
+}
+
+template <int BT>
+static int launch_gemv_bt(const uint16_t* W, int N, int K, const float* X, int ldx, int B, float* Y,
+                          int ldy, int accumulate, cudaStream_t s) {
+  constexpr int R = BT >= 8 ? 2 : 4;
+  int rows = 8 * R;
+  int blocks = (N + rows - 1) / rows;
+  gemv_kernel<BT, R><<<blocks, 256, 0, s>>>(W, N, K, X, ldx, B, Y, ldy, accumulate);
+  return check_launch("gemv_kernel");
+}
+
+int launch_gemv(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy,
+                int accumulate, cudaStream_t s) {
+  RNGD_REQUIRE(W && X && Y, "gemv: null pointer");
+  RNGD_REQUIRE(N > 0 && K > 0 && K % 8 == 0, "gemv: need N > 0 and K %% 8 == 0 (N=%d K=%d)", N, K);
+  RNGD_REQUIRE(B >= 1 && B <= 16, "gemv: batch %d outside 1..16", B);
+  RNGD_REQUIRE(ldx % 4 == 0 && ldx >= K, "gemv: ldx %d must be >= K and a multiple of 4", ldx);
+  const uint16_t* w = (const uint16_t*)W;
+  if (B <= 1) return launch_gemv_bt<1>(w, N, K, X, ldx, B, Y, ldy, accumulate, s);
+  if (B <= 2) return launch_gemv_bt<2>(w, N, K, X, ldx, B, Y, ldy, accumulate, s);
+  if (B <= 4) return launch_gemv_bt<4>(w, N, K, X, ldx, B, Y, ldy, accumulate, s);
+  if (B <= 8) return launch_gemv_bt<8>(w, N, K, X, ldx, B, Y, ldy, accumulate, s);
+  return launch_gemv_bt<16>(w, N, K, X, ldx, B, Y, ldy, accumulate, s);
+}
+
+// -------------------------------------------------------------- rmsnorm
+// out = x * (1 / sqrt(mean(x^2) + eps)) * w   (kernels/decode_batch.py:130)
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, int H,
+                                                      const float* __restrict__ w, float eps,
+                                                      float* __restrict__ out) {
+  __shared__ float red[8];
+  const float* xr = x + (size_t)blockIdx.x * H;
+  float s = 0.f;
+  for (int k = threadIdx.x; k < H; k += 256) s = fmaf(xr[k], xr[k], s);
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = 1.0f / sqrtf(t / (float)H + eps);
+  }
+  __syncthreads();
+  const float inv = red[0];
+  float* o = out + (size_t)blockIdx.x * H;
+  for (int k = threadIdx.x; k < H; k += 256) o[k] = xr[k] * inv * w[k];
+}
+
+int launch_rmsnorm(const float* x, int R, int H, const float* w, float eps, float* out, cudaStream_t s) {
+  RNGD_REQUIRE(x && w && out && R > 0 && H > 0, "rmsnorm: bad arguments");
+  rmsnorm_kernel<<<R, 256, 0, s>>>(x, H, w, eps, out);
+  return check_launch("rmsnorm_kernel");
+}
+
+// ------------------------------------------------------ RoPE + KV append
+// HF rotate-half on q and k at pos[b] (kernels/decode_batch.py:133-142), angles
+// fp32 = float(pos) * inv_freq (engines/decode_batch.py:248-253); k and v are
+// rounded to bf16 and written into lane b at pos[b] (the one-hot injection of
+// kernels/decode_batch.py:81-82, as a store).
+// grid (B, NH + 2*NKV), block HD/2.
+__global__ void rope_kv_kernel(const float* __restrict__ qkv, int ldqkv, const int32_t* __restrict__ pos,
+                               const float* __restrict__ inv, float* __restrict__ q, int ldq,
+                               uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int NH, int NKV,
+                               int HD, int S) {
+  const int b = blockIdx.x, hd = blockIdx.y, i = threadIdx.x, half = HD >> 1;
+  const int p = pos[b];
+  if (p < 0 || p >= S) return;  // the host validates positions; never write outside the lane
+  const float* src = qkv + (size_t)b * ldqkv + (size_t)hd * HD;
+  const float a = src[i], c = src[i + half];
+  if (hd < NH + NKV) {
+    const float ang = (float)p * inv[i];
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    const float r0 = a * cs - c * sn, r1 = c * cs + a * sn;
+    if (hd < NH) {
+      float* dq = q + (size_t)b * ldq + (size_t)hd * HD;
+      dq[i] = r0;
+      dq[i + half] = r1;
+    } else {
+      uint16_t* dk = kc + (((size_t)b * NKV + (hd - NH)) * S + p) * HD;
+      dk[i] = f2bf_bits(r0);
+      dk[i + half] = f2bf_bits(r1);
+    }
+  } else {
+    uint16_t* dv = vc + (((size_t)b * NKV + (hd - NH - NKV)) * S + p) * HD;
+    dv[i] = f2bf_bits(a);
+    dv[i + half] = f2bf_bits(c);
+  }
+}
+
+// ------------------------------------------------------------ attention
+// Split-S flash decoding with a fixed 128-position chunk (independent of B and
+// of the other lanes, so a stream's result does not depend on who it is
+// batched with).  One CTA = (chunk, kv head, stream) and the G=4 query heads
+// that share the kv head.  Positions > pos[b] are skipped; the reference masks
+// them with -1e4 (kernels/decode_batch.py:153), which gives them probability
+// exactly 0 in fp32 as well.
+constexpr int kChunk = 128;
+constexpr int kG = 4;
+constexpr int kHD = 128;
+
+__global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restrict__ q, int ldq,
+                                                           const uint16_t* __restrict__ kc,
+                                                           const uint16_t* __restrict__ vc,
+                                                           const int32_t* __restrict__ pos, int NH,
+                                                           int NKV, int S, float* __restrict__ part) {
+  const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
+  const int nchunk = gridDim.x;
+  const int P = min(pos[b] + 1, S);
+  const int s0 = c * kChunk;
+  const int PS = kHD + 2;  // partial record: o[HD], m, l
+  __shared__ float qs[kG][kHD];
+  __shared__ float ps[kG][kChunk];
+  __shared__ float red[kG][4];
+  float* rec0 = part + (((size_t)b * NH + kvh * kG) * nchunk + c) * PS;
+  if (s0 >= P) {
+    if (t < kG) {
+      float* rec = rec0 + (size_t)t * nchunk * PS;
+      rec[kHD] = -INFINITY;
+      rec[kHD + 1] = 0.f;
+    }
+    return;
+  }
+  const float scale = 0.08838834764831845f;  // 1/sqrt(128) in fp32
+  for (int i = t; i < kG * kHD; i += 128)
+    qs[i / kHD][i % kHD] = q[(size_t)b * ldq + (size_t)(kvh * kG + i / kHD) * kHD + i % kHD];
+  __syncthreads();
+  const int s = s0 + t;
+  const bool valid = s < P;
+  const size_t head_base = ((size_t)b * NKV + kvh) * (size_t)S * kHD;
+  float sc[kG] = {0.f, 0.f, 0.f, 0.f};
+  if (valid) {
+    const uint16_t* krow = kc + head_base + (size_t)s * kHD;
+#pragma unroll 4
+    for (int d = 0; d < kHD; d += 8) {
+      float kf[8];
+      unpack8(*reinterpret_cast<const uint4*>(krow + d), kf);
+#pragma unroll
+      for (int g = 0; g < kG; g++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) sc[g] = fmaf(qs[g][d + j], kf[j], sc[g]);
+    }
+  }
+  const int warp = t >> 5, lane = t & 31;
+  float mx[kG], sum[kG];
+#pragma unroll
+  for (int g = 0; g < kG; g++) {
+    sc[g] = valid ? sc[g] * scale : -INFINITY;
+    float m = warp_max(sc[g]);
+    if (lane == 0) red[g][warp] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < kG; g++) mx[g] = fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]));
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < kG; g++) {
+    float p = valid ? expf(sc[g] - mx[g]) : 0.f;
+    ps[g][t] = p;
+    float ssum = warp_sum(p);
+    if (lane == 0) red[g][warp] = ssum;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < kG; g++) sum[g] = (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
+  // P.V: thread t owns output dimension t for the 4 heads
+  const int n = min(kChunk, P - s0);
+  float o[kG] = {0.f, 0.f, 0.f, 0.f};
+  const uint16_t* vcol = vc + head_base + (size_t)s0 * kHD + t;
+  for (int j = 0; j < n; j++) {
+    const float vv = bf2f(vcol[(size_t)j * kHD]);
+#pragma unroll
+    for (int g = 0; g < kG; g++) o[g] = fmaf(ps[g][j], vv, o[g]);
+  }
+#pragma unroll
+  for (int g = 0; g < kG; g++) {
+    float* rec = rec0 + (size_t)g * nchunk * PS;
+    rec[t] = o[g];
+    if (t == 0) {
+      rec[kHD] = mx[g];
+      rec[kHD + 1] = sum[g];
+    }
+  }
+}
+
+// Combines the chunk partials of one (stream, head) in chunk order.
+// grid (NH, B), block HD.
+__global__ void attn_combine_kernel(const float* __restrict__ part, int nchunk, float* __restrict__ ao,
+                                    int ldao, int NH) {
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const int PS = kHD + 2;
+  const float* rec = part + ((size_t)b * NH + h) * nchunk * PS;
+  float M = -INFINITY;
+  for (int c = 0; c < nchunk; c++) M = fmaxf(M, rec[(size_t)c * PS + kHD]);
+  float L = 0.f, O = 0.f;
+  for (int c = 0; c < nchunk; c++) {
+    const float m = rec[(size_t)c * PS + kHD];
+    if (m == -INFINITY) continue;
+    const float f = expf(m - M);
+    L = fmaf(rec[(size_t)c * PS + kHD + 1], f, L);
+    O = fmaf(rec[(size_t)c * PS + d], f, O);
+  }
+  ao[(size_t)b * ldao + (size_t)h * kHD + d] = O / L;
+}
+
+int launch_attn_decode(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B,
+                       int NH, int NKV, int HD, int S, float* part, float* ao, int ldao, cudaStream_t s) {
+  RNGD_REQUIRE(q && kc && vc && pos && part && ao, "attn_decode: null pointer");
+  RNGD_REQUIRE(HD == kHD && NH == kG * NKV, "attn_decode: built for HD=128 and 4 query heads per kv head");
+  RNGD_REQUIRE(S % kChunk == 0 && S > 0 && S <= 8192, "attn_decode: S=%d must be a multiple of 128", S);
+  RNGD_REQUIRE(B >= 1, "attn_decode: B=%d", B);
+  const int nchunk = S / kChunk;
+  attn_partial_kernel<<<dim3(nchunk, NKV, B), 128, 0, s>>>(q, ldq, (const uint16_t*)kc, (const uint16_t*)vc,
+                                                          pos, NH, NKV, S, part);
+  RNGD_TRY(check_launch("attn_partial_kernel"));
+  attn_combine_kernel<<<dim3(NH, B), kHD, 0, s>>>(part, nchunk, ao, ldao, NH);
+  return check_launch("attn_combine_kernel");
+}
+
+// ----------------------------------------------------------- SwiGLU
+// act[b][f] = silu(g) * u with g, u from the 64-row interleaved gate/up output
+// (kernels/decode_batch.py:159-161: g / (1 + exp(-g)) * u).
+__global__ void swiglu_kernel(const float* __restrict__ gu, int ldgu, int Mi, float* __restrict__ act,
+                              int ldact) {
+  const int b = blockIdx.y;
+  for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < Mi; f += gridDim.x * blockDim.x) {
+    const int blk = f >> 6, j = f & 63;
+    const float g = gu[(size_t)b * ldgu + blk * 128 + j];
+    const float u = gu[(size_t)b * ldgu + blk * 128 + 64 + j];
+    act[(size_t)b * ldact + f] = g / (1.0f + expf(-g)) * u;
+  }
+}
+
+// ------------------------------------------------------------ embedding
+__global__ void embed_kernel(const uint16_t* __restrict__ emb, const int32_t* __restrict__ toks, int H,
+                             int V, float* __restrict__ x) {
+  const int b = blockIdx.x;
+  int t = toks[b];
+  t = t < 0 ? 0 : (t >= V ? V - 1 : t);
+  const uint16_t* row = emb + (size_t)t * H;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) x[(size_t)b * H + k] = bf2f(row[k]);
+}
+
+// --------------------------------------------------------------- argmax
+// First maximum of each row (torch.argmax / numpy argmax tie rule,
+// engines/decode_batch.py:162-171).  One CTA per row.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V,
+                                                      int32_t* __restrict__ out) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const float* row = logits + (size_t)blockIdx.x * V;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = row[i];
+    if (v > best) { best = v; idx = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = best; bi[threadIdx.x >> 5] = idx; }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = bv[threadIdx.x];
+    idx = bi[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = idx;
+  }
+}
+
+__global__ void advance_kernel(int32_t* __restrict__ toks, int32_t* __restrict__ pos,
+                               const int32_t* __restrict__ next, int B) {
+  const int b = threadIdx.x;
+  if (b < B) {
+    toks[b] = next[b];
+    pos[b] += 1;
+  }
+}
+
+static int check_model(const rngd_model_t* m) {
+  RNGD_REQUIRE(m != nullptr, "null model");
+  RNGD_REQUIRE(m->HD == kHD && m->NH == kG * m->NKV, "model: kernels are built for HD=128, NH=4*NKV");
+  RNGD_REQUIRE(m->H % 128 == 0 && m->M % 64 == 0 && m->L > 0 && m->V > 0,
+               "model: need H %% 128 == 0 and M %% 64 == 0");
+  RNGD_REQUIRE(m->wqkv && m->wo && m->wgu && m->wd && m->n1 && m->n2 && m->norm && m->embed && m->lm &&
+                   m->inv_freq,
+               "model: null weight pointer");
+  return RNGD_OK;
+}
+
+static int check_io(const rngd_model_t* m, const rngd_decode_io_t* io) {
+  RNGD_REQUIRE(io != nullptr, "null decode io");
+  RNGD_REQUIRE(io->B >= 1 && io->B <= 16 && io->B <= io->Bcap, "decode: B=%d outside 1..min(16, Bcap=%d)",
+               io->B, io->Bcap);
+  RNGD_REQUIRE(io->S % kChunk == 0 && io->S > 0 && io->S <= 8192, "decode: S=%d must be a multiple of 128",
+               io->S);
+  RNGD_REQUIRE(io->kcache && io->vcache && io->toks && io->pos && io->x && io->h && io->qkv && io->q &&
+                   io->ao && io->gu && io->logits && io->attn_part && io->next,
+               "decode: null buffer");
+  (void)m;
+  return RNGD_OK;
+}
+
+}  // namespace rngd
+
+using namespace rngd;
+
+extern "C" int rngd_gemv_bf16(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy,
+                              int accumulate, rngd_stream_t stream) {
+  return launch_gemv(W, N, K, X, ldx, B, Y, ldy, accumulate, (cudaStream_t)stream);
+}
+
+extern "C" int rngd_rmsnorm_f32(const float* x, int R, int H, const float* w, float eps, float* out,
+                                rngd_stream_t stream) {
+  return launch_rmsnorm(x, R, H, w, eps, out, (cudaStream_t)stream);
+}
+
+extern "C" int rngd_attn_decode(const float* q, const void* kc, const void* vc, const int32_t* pos, int B,
+                                int Bcap, int NH, int NKV, int HD, int S, float* part, float* ao,
+                                rngd_stream_t stream) {
+  RNGD_REQUIRE(B <= Bcap, "attn_decode: B=%d > Bcap=%d", B, Bcap);
+  return launch_attn_decode(q, NH * HD, kc, vc, pos, B, NH, NKV, HD, S, part, ao, NH * HD,
+                            (cudaStream_t)stream);
+}
+
+extern "C" int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream) {
+  RNGD_TRY(check_model(m));
+  RNGD_TRY(check_io(m, io));
+  embed_kernel<<<io->B, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)m->embed, io->toks, m->H, m->V, io->x);
+  return check_launch("embed_kernel");
+}
+
+extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, int layer1,
+                                  rngd_stream_t stream) {
+  RNGD_TRY(check_model(m));
+  RNGD_TRY(check_io(m, io));
+  RNGD_REQUIRE(0 <= layer0 && layer0 <= layer1 && layer1 <= m->L, "decode: layers [%d, %d) outside [0, %d)",
+               layer0, layer1, m->L);
+  RNGD_REQUIRE(layer1 - layer0 <= io->kv_layers, "decode: %d layers requested but the cache block holds %d",
+               layer1 - layer0, io->kv_layers);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int H = m->H, Mi = m->M, QN = m->NH * m->HD, KN = m->NKV * m->HD, NQKV = QN + 2 * KN;
+  const int B = io->B;
+  const size_t lane_elems = (size_t)m->NKV * io->S * m->HD;
+  const int ldh = H > Mi ? H : Mi;
+  for (int l = layer0; l < layer1; l++) {
+    const uint16_t* wqkv = (const uint16_t*)m->wqkv + (size_t)l * NQKV * H;
+    const uint16_t* wo = (const uint16_t*)m->wo + (size_t)l * H * QN;
+    const uint16_t* wgu = (const uint16_t*)m->wgu + (size_t)l * 2 * Mi * H;
+    const uint16_t* wd = (const uint16_t*)m->wd + (size_t)l * H * Mi;
+    // the cache block passed in starts at layer0 (one layer group's cache)
+    uint16_t* kc = (uint16_t*)io->kcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
+    uint16_t* vc = (uint16_t*)io->vcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
+    RNGD_TRY(launch_rmsnorm(io->x, B, H, m->n1 + (size_t)l * H, m->eps, io->h, s));
+    RNGD_TRY(launch_gemv(wqkv, NQKV, H, io->h, H, B, io->qkv, NQKV, 0, s));
+    rope_kv_kernel<<<dim3(B, m->NH + 2 * m->NKV), m->HD / 2, 0, s>>>(io->qkv, NQKV, io->pos, m->inv_freq, io->q,
+                                                                       QN, kc, vc, m->NH, m->NKV, m->HD, io->S);
+    RNGD_TRY(check_launch("rope_kv_kernel"));
+    RNGD_TRY(launch_attn_decode(io->q, QN, kc, vc, io->pos, B, m->NH, m->NKV, m->HD, io->S, io->attn_part,
+                                io->ao, QN, s));
+    RNGD_TRY(launch_gemv(wo, H, QN, io->ao, QN, B, io->x, H, 1, s));
+    RNGD_TRY(launch_rmsnorm(io->x, B, H, m->n2 + (size_t)l * H, m->eps, io->h, s));
+    RNGD_TRY(launch_gemv(wgu, 2 * Mi, H, io->h, H, B, io->gu, 2 * Mi, 0, s));
+    swiglu_kernel<<<dim3((Mi + 255) / 256, B), 256, 0, s>>>(io->gu, 2 * Mi, Mi, io->h, ldh);
+    RNGD_TRY(check_launch("swiglu_kernel"));
+    RNGD_TRY(launch_gemv(wd, H, Mi, io->h, ldh, B, io->x, H, 1, s));
+  }
+  return RNGD_OK;
+}
+
+extern "C" int rngd_decode_lmhead(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream) {
+  RNGD_TRY(check_model(m));
+  RNGD_TRY(check_io(m, io));
+  cudaStream_t s = (cudaStream_t)stream;
+  RNGD_TRY(launch_rmsnorm(io->x, io->B, m->H, m->norm, m->eps, io->h, s));
+  RNGD_TRY(launch_gemv(m->lm, m->V, m->H, io->h, m->H, io->B, io->logits, m->V, 0, s));
+  argmax_kernel<<<io->B, 1024, 0, s>>>(io->logits, m->V, io->next);
+  return check_launch("argmax_kernel");
+}
+
+extern "C" int rngd_decode_advance(const rngd_decode_io_t* io, rngd_stream_t stream) {
+  RNGD_REQUIRE(io && io->toks && io->pos && io->next && io->B >= 1 && io->B <= 1024, "advance: bad io");
+  advance_kernel<<<1, 32 * ((io->B + 31) / 32), 0, (cudaStream_t)stream>>>((int32_t*)io->toks, (int32_t*)io->pos,
+                                                                          io->next, io->B);
+  return check_launch("advance_kernel");
+}

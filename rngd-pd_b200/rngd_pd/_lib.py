@@ -1,0 +1,115 @@
+"""ctypes binding of the C ABI in include/rngd_b200.h (the B200 kernels).
+
+The product has no CPU or library fallback: importing this module without the
+built ``_rngd_b200.so`` raises, and every call that returns a negative status
+raises ``RngdError`` with the library's own message.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_rngd_b200.so")
+
+RNGD_OK = 0
+RNGD_ERR_ARG = -1
+RNGD_ERR_CUDA = -2
+RNGD_ERR_TIMEOUT = -3
+RNGD_ERR_UNSUPPORTED = -4
+
+
+class RngdError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"rngd status {status}: {msg}")
+        self.status = status
+
+
+class RngdTimeout(RngdError, TimeoutError):
+    pass
+
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C rngd-pd_b200/csrc` "
+                      "(or __graft_entry__.build()); there is no fallback path")
+
+lib = ctypes.CDLL(LIB_PATH)
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_f32p = ctypes.POINTER(ctypes.c_float)
+
+
+class Model(ctypes.Structure):
+    """rngd_model_t"""
+    _fields_ = [("H", _i32), ("M", _i32), ("NH", _i32), ("NKV", _i32), ("HD", _i32), ("L", _i32),
+                ("V", _i32), ("eps", ctypes.c_float), ("wqkv", _vp), ("wo", _vp), ("wgu", _vp),
+                ("wd", _vp), ("n1", _vp), ("n2", _vp), ("norm", _vp), ("embed", _vp), ("lm", _vp),
+                ("inv_freq", _vp)]
+
+
+class DecodeIO(ctypes.Structure):
+    """rngd_decode_io_t"""
+    _fields_ = [("B", _i32), ("Bcap", _i32), ("S", _i32), ("kv_layers", _i32), ("kcache", _vp), ("vcache", _vp),
+                ("toks", _vp), ("pos", _vp), ("x", _vp), ("h", _vp), ("qkv", _vp), ("q", _vp),
+                ("ao", _vp), ("gu", _vp), ("logits", _vp), ("attn_part", _vp), ("next", _vp)]
+
+
+def _sig(name, *args):
+    f = getattr(lib, name)
+    f.argtypes = list(args)
+    f.restype = ctypes.c_int
+    return f
+
+
+_sig("rngd_last_error", ctypes.c_char_p, ctypes.c_size_t)
+_sig("rngd_abi_version")
+_sig("rngd_synth_gauss_bf16", _vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
+     ctypes.c_float, _vp)
+_sig("rngd_synth_uniform_i32", _vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
+     ctypes.c_uint32, _vp)
+_MP = ctypes.POINTER(Model)
+_IOP = ctypes.POINTER(DecodeIO)
+_sig("rngd_decode_embed", _MP, _IOP, _vp)
+_sig("rngd_decode_layers", _MP, _IOP, ctypes.c_int, ctypes.c_int, _vp)
+_sig("rngd_decode_lmhead", _MP, _IOP, _vp)
+_sig("rngd_decode_advance", _IOP, _vp)
+_sig("rngd_gemv_bf16", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
+     ctypes.c_int, _vp)
+_sig("rngd_rmsnorm_f32", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_float, _vp, _vp)
+_sig("rngd_attn_decode", _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+     ctypes.c_int, ctypes.c_int, _vp, _vp, _vp)
+
+
+def last_error():
+    buf = ctypes.create_string_buffer(512)
+    lib.rngd_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def check(status):
+    if status != RNGD_OK:
+        msg = last_error()
+        if status == RNGD_ERR_TIMEOUT:
+            raise RngdTimeout(status, msg)
+        raise RngdError(status, msg)
+    return status
+
+
+def call(name, *args):
+    return check(getattr(lib, name)(*args))
+
+
+def stream_handle(stream=None):
+    """Raw cudaStream_t of a torch stream (the current one by default)."""
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def ptr(t):
+    """Device pointer of a torch tensor (None -> NULL)."""
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def exported_symbols():
+    """Names declared in include/rngd_b200.h, for the ABI completeness test."""
+    return [n for n in dir(lib) if n.startswith("rngd_")]
