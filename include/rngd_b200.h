@@ -67,7 +67,10 @@ typedef struct rngd_model {
 } rngd_model_t;
 
 /* Per-engine decode state.  Lanes 0..B-1 of the resident cache are the B
- * streams of the step; each has its own position (engines/decode_batch.py:422-442). */
+ * streams of the step; each has its own position (engines/decode_batch.py:422-442).
+ * Activation operands of the tensor-core GEMMs are 32 bf16 rows: rows 0..15
+ * hold bf16(h) of each stream, rows 16..31 bf16(h - bf16(h)); rows of streams
+ * >= B stay zero (allocate zeroed). */
 typedef struct rngd_decode_io {
   int32_t B;            /* streams stepped (<= 16) */
   int32_t Bcap;         /* lanes of the resident cache */
@@ -78,15 +81,22 @@ typedef struct rngd_decode_io {
   const int32_t* toks;  /* device [B] token ids of this step */
   const int32_t* pos;   /* device [B] position each token is written at */
   float* x;             /* fp32 [16][H] residual stream */
-  float* h;             /* fp32 [16][max(H, M)] normalised / gated activations */
-  float* qkv;           /* fp32 [16][(NH+2*NKV)*HD] */
   float* q;             /* fp32 [16][NH*HD] rotated queries */
-  float* ao;            /* fp32 [16][NH*HD] attention output */
-  float* gu;            /* fp32 [16][2*M] */
+  void* act;            /* bf16 [32][max(H, NH*HD)] GEMM operand (zeroed at allocation) */
+  void* act2;           /* bf16 [32][M] down-projection operand (zeroed at allocation) */
   float* logits;        /* fp32 [B][V] */
   float* attn_part;     /* fp32 scratch [B][NH][S/128][HD+2] */
+  float* partial;       /* fp32 split-K scratch, rngd_decode_workspace() floats */
+  int32_t* counters;    /* int32 tile counters, rngd_decode_workspace() entries, zeroed once */
+  uint64_t* best;       /* [16] argmax keys */
   int32_t* next;        /* device [B] greedy next tokens */
 } rngd_decode_io_t;
+
+/* Sizes of the decode scratch buffers for a model (shape-only; independent of B). */
+int rngd_decode_workspace(const rngd_model_t* m, int S, size_t* partial_floats, size_t* counters,
+                          size_t* act_cols, size_t* act2_cols);
+/* Device status word of the bounded waits (0 = none timed out); reset clears it. */
+int rngd_device_status(int* status, int reset);
 
 /* x = embed[toks] (engines/decode_batch.py:432). */
 int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream);
@@ -97,7 +107,8 @@ int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_st
 int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, int layer1,
                        rngd_stream_t stream);
 /* Final norm + lm_head + first-max argmax into io->next; logits kept in
- * io->logits (engines/decode_batch.py:440 and greedy_tokens 162-171). */
+ * io->logits (engines/decode_batch.py:440 and greedy_tokens 162-171).
+ * The layer GEMMs and the lm_head run on tcgen05 tensor cores. */
 int rngd_decode_lmhead(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream);
 
 /* toks[b] = next[b]; pos[b] += 1 for b < B: feeds a greedy step's output back as
@@ -112,6 +123,14 @@ int rngd_decode_advance(const rngd_decode_io_t* io, rngd_stream_t stream);
  * b < B <= 16, K % 8 == 0 (CUDA-core path, fp32 accumulation). */
 int rngd_gemv_bf16(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy,
                    int accumulate, rngd_stream_t stream);
+/* Tensor-core form of the same op (the one the decode step uses): Y[b][n] +=
+ * sum_k W[n][k] * X[b][k] through tcgen05 with the fp32 X split into bf16
+ * hi + lo operand rows.  act: zeroed bf16 scratch [32][K]; partial/counters:
+ * split-K scratch of rngd_tc_gemv_workspace() (counters zeroed once).
+ * N % 128 == 0, K % 64 == 0, B <= 16. */
+int rngd_tc_gemv(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy, void* act,
+                 float* partial, int32_t* counters, rngd_stream_t stream);
+int rngd_tc_gemv_workspace(int N, int K, size_t* partial_floats, size_t* counters);
 /* out[r][k] = x[r][k] / sqrt(mean_k x^2 + eps) * w[k] (kernels/decode_batch.py:130). */
 int rngd_rmsnorm_f32(const float* x, int R, int H, const float* w, float eps, float* out,
                      rngd_stream_t stream);

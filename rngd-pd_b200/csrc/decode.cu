@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
 // Combines the chunk partials of one (stream, head) in chunk order.
 // grid (NH, B), block HD.
 __global__ void attn_combine_kernel(const float* __restrict__ part, int nchunk, float* __restrict__ ao,
-                                    int ldao, int NH) {
+                                    int ldao, int NH, uint16_t* __restrict__ act, int ld_act) {
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int PS = kHD + 2;
   const float* rec = part + ((size_t)b * NH + h) * nchunk * PS;
@@ -272,12 +272,21 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int nchunk, 
     L = fmaf(rec[(size_t)c * PS + kHD + 1], f, L);
     O = fmaf(rec[(size_t)c * PS + d], f, O);
   }
-  ao[(size_t)b * ldao + (size_t)h * kHD + d] = O / L;
+  const float o = O / L;
+  const size_t col = (size_t)h * kHD + d;
+  if (act != nullptr) {  // hi/lo bf16 operand of the O-projection GEMM
+    const uint16_t hi = f2bf_bits(o);
+    act[(size_t)b * ld_act + col] = hi;
+    act[(size_t)(16 + b) * ld_act + col] = f2bf_bits(o - bf2f(hi));
+  } else {
+    ao[(size_t)b * ldao + col] = o;
+  }
 }
 
-int launch_attn_decode(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B,
-                       int NH, int NKV, int HD, int S, float* part, float* ao, int ldao, cudaStream_t s) {
-  RNGD_REQUIRE(q && kc && vc && pos && part && ao, "attn_decode: null pointer");
+static int launch_attn(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B, int NH,
+                       int NKV, int HD, int S, float* part, float* ao, int ldao, uint16_t* act, int ld_act,
+                       cudaStream_t s) {
+  RNGD_REQUIRE(q && kc && vc && pos && part && (ao || act), "attn_decode: null pointer");
   RNGD_REQUIRE(HD == kHD && NH == kG * NKV, "attn_decode: built for HD=128 and 4 query heads per kv head");
   RNGD_REQUIRE(S % kChunk == 0 && S > 0 && S <= 8192, "attn_decode: S=%d must be a multiple of 128", S);
   RNGD_REQUIRE(B >= 1, "attn_decode: B=%d", B);
@@ -285,8 +294,18 @@ int launch_attn_decode(const float* q, int ldq, const void* kc, const void* vc, 
   attn_partial_kernel<<<dim3(nchunk, NKV, B), 128, 0, s>>>(q, ldq, (const uint16_t*)kc, (const uint16_t*)vc,
                                                           pos, NH, NKV, S, part);
   RNGD_TRY(check_launch("attn_partial_kernel"));
-  attn_combine_kernel<<<dim3(NH, B), kHD, 0, s>>>(part, nchunk, ao, ldao, NH);
+  attn_combine_kernel<<<dim3(NH, B), kHD, 0, s>>>(part, nchunk, ao, ldao, NH, act, ld_act);
   return check_launch("attn_combine_kernel");
+}
+
+int launch_attn_decode(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B, int NH,
+                       int NKV, int HD, int S, float* part, float* ao, int ldao, cudaStream_t s) {
+  return launch_attn(q, ldq, kc, vc, pos, B, NH, NKV, HD, S, part, ao, ldao, nullptr, 0, s);
+}
+
+int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B,
+                           int NH, int NKV, int HD, int S, float* part, void* act, int ld_act, cudaStream_t s) {
+  return launch_attn(q, ldq, kc, vc, pos, B, NH, NKV, HD, S, part, nullptr, 0, (uint16_t*)act, ld_act, s);
 }
 
 // ----------------------------------------------------------- SwiGLU
@@ -357,30 +376,6 @@ __global__ void advance_kernel(int32_t* __restrict__ toks, int32_t* __restrict__
   }
 }
 
-static int check_model(const rngd_model_t* m) {
-  RNGD_REQUIRE(m != nullptr, "null model");
-  RNGD_REQUIRE(m->HD == kHD && m->NH == kG * m->NKV, "model: kernels are built for HD=128, NH=4*NKV");
-  RNGD_REQUIRE(m->H % 128 == 0 && m->M % 64 == 0 && m->L > 0 && m->V > 0,
-               "model: need H %% 128 == 0 and M %% 64 == 0");
-  RNGD_REQUIRE(m->wqkv && m->wo && m->wgu && m->wd && m->n1 && m->n2 && m->norm && m->embed && m->lm &&
-                   m->inv_freq,
-               "model: null weight pointer");
-  return RNGD_OK;
-}
-
-static int check_io(const rngd_model_t* m, const rngd_decode_io_t* io) {
-  RNGD_REQUIRE(io != nullptr, "null decode io");
-  RNGD_REQUIRE(io->B >= 1 && io->B <= 16 && io->B <= io->Bcap, "decode: B=%d outside 1..min(16, Bcap=%d)",
-               io->B, io->Bcap);
-  RNGD_REQUIRE(io->S % kChunk == 0 && io->S > 0 && io->S <= 8192, "decode: S=%d must be a multiple of 128",
-               io->S);
-  RNGD_REQUIRE(io->kcache && io->vcache && io->toks && io->pos && io->x && io->h && io->qkv && io->q &&
-                   io->ao && io->gu && io->logits && io->attn_part && io->next,
-               "decode: null buffer");
-  (void)m;
-  return RNGD_OK;
-}
-
 }  // namespace rngd
 
 using namespace rngd;
@@ -404,58 +399,10 @@ extern "C" int rngd_attn_decode(const float* q, const void* kc, const void* vc, 
 }
 
 extern "C" int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream) {
-  RNGD_TRY(check_model(m));
-  RNGD_TRY(check_io(m, io));
+  RNGD_REQUIRE(m && io && m->embed && io->toks && io->x, "decode_embed: null argument");
+  RNGD_REQUIRE(io->B >= 1 && io->B <= 16, "decode_embed: B=%d outside 1..16", io->B);
   embed_kernel<<<io->B, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)m->embed, io->toks, m->H, m->V, io->x);
   return check_launch("embed_kernel");
-}
-
-extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, int layer1,
-                                  rngd_stream_t stream) {
-  RNGD_TRY(check_model(m));
-  RNGD_TRY(check_io(m, io));
-  RNGD_REQUIRE(0 <= layer0 && layer0 <= layer1 && layer1 <= m->L, "decode: layers [%d, %d) outside [0, %d)",
-               layer0, layer1, m->L);
-  RNGD_REQUIRE(layer1 - layer0 <= io->kv_layers, "decode: %d layers requested but the cache block holds %d",
-               layer1 - layer0, io->kv_layers);
-  cudaStream_t s = (cudaStream_t)stream;
-  const int H = m->H, Mi = m->M, QN = m->NH * m->HD, KN = m->NKV * m->HD, NQKV = QN + 2 * KN;
-  const int B = io->B;
-  const size_t lane_elems = (size_t)m->NKV * io->S * m->HD;
-  const int ldh = H > Mi ? H : Mi;
-  for (int l = layer0; l < layer1; l++) {
-    const uint16_t* wqkv = (const uint16_t*)m->wqkv + (size_t)l * NQKV * H;
-    const uint16_t* wo = (const uint16_t*)m->wo + (size_t)l * H * QN;
-    const uint16_t* wgu = (const uint16_t*)m->wgu + (size_t)l * 2 * Mi * H;
-    const uint16_t* wd = (const uint16_t*)m->wd + (size_t)l * H * Mi;
-    // the cache block passed in starts at layer0 (one layer group's cache)
-    uint16_t* kc = (uint16_t*)io->kcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
-    uint16_t* vc = (uint16_t*)io->vcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
-    RNGD_TRY(launch_rmsnorm(io->x, B, H, m->n1 + (size_t)l * H, m->eps, io->h, s));
-    RNGD_TRY(launch_gemv(wqkv, NQKV, H, io->h, H, B, io->qkv, NQKV, 0, s));
-    rope_kv_kernel<<<dim3(B, m->NH + 2 * m->NKV), m->HD / 2, 0, s>>>(io->qkv, NQKV, io->pos, m->inv_freq, io->q,
-                                                                       QN, kc, vc, m->NH, m->NKV, m->HD, io->S);
-    RNGD_TRY(check_launch("rope_kv_kernel"));
-    RNGD_TRY(launch_attn_decode(io->q, QN, kc, vc, io->pos, B, m->NH, m->NKV, m->HD, io->S, io->attn_part,
-                                io->ao, QN, s));
-    RNGD_TRY(launch_gemv(wo, H, QN, io->ao, QN, B, io->x, H, 1, s));
-    RNGD_TRY(launch_rmsnorm(io->x, B, H, m->n2 + (size_t)l * H, m->eps, io->h, s));
-    RNGD_TRY(launch_gemv(wgu, 2 * Mi, H, io->h, H, B, io->gu, 2 * Mi, 0, s));
-    swiglu_kernel<<<dim3((Mi + 255) / 256, B), 256, 0, s>>>(io->gu, 2 * Mi, Mi, io->h, ldh);
-    RNGD_TRY(check_launch("swiglu_kernel"));
-    RNGD_TRY(launch_gemv(wd, H, Mi, io->h, ldh, B, io->x, H, 1, s));
-  }
-  return RNGD_OK;
-}
-
-extern "C" int rngd_decode_lmhead(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream) {
-  RNGD_TRY(check_model(m));
-  RNGD_TRY(check_io(m, io));
-  cudaStream_t s = (cudaStream_t)stream;
-  RNGD_TRY(launch_rmsnorm(io->x, io->B, m->H, m->norm, m->eps, io->h, s));
-  RNGD_TRY(launch_gemv(m->lm, m->V, m->H, io->h, m->H, io->B, io->logits, m->V, 0, s));
-  argmax_kernel<<<io->B, 1024, 0, s>>>(io->logits, m->V, io->next);
-  return check_launch("argmax_kernel");
 }
 
 extern "C" int rngd_decode_advance(const rngd_decode_io_t* io, rngd_stream_t stream) {

@@ -49,8 +49,9 @@ class Model(ctypes.Structure):
 class DecodeIO(ctypes.Structure):
     """rngd_decode_io_t"""
     _fields_ = [("B", _i32), ("Bcap", _i32), ("S", _i32), ("kv_layers", _i32), ("kcache", _vp), ("vcache", _vp),
-                ("toks", _vp), ("pos", _vp), ("x", _vp), ("h", _vp), ("qkv", _vp), ("q", _vp),
-                ("ao", _vp), ("gu", _vp), ("logits", _vp), ("attn_part", _vp), ("next", _vp)]
+                ("toks", _vp), ("pos", _vp), ("x", _vp), ("q", _vp), ("act", _vp), ("act2", _vp),
+                ("logits", _vp), ("attn_part", _vp), ("partial", _vp), ("counters", _vp), ("best", _vp),
+                ("next", _vp)]
 
 
 def _sig(name, *args):
@@ -72,6 +73,12 @@ _sig("rngd_decode_embed", _MP, _IOP, _vp)
 _sig("rngd_decode_layers", _MP, _IOP, ctypes.c_int, ctypes.c_int, _vp)
 _sig("rngd_decode_lmhead", _MP, _IOP, _vp)
 _sig("rngd_decode_advance", _IOP, _vp)
+_szp = ctypes.POINTER(ctypes.c_size_t)
+_sig("rngd_decode_workspace", _MP, ctypes.c_int, _szp, _szp, _szp, _szp)
+_sig("rngd_tc_gemv", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp,
+     _vp, _vp, _vp)
+_sig("rngd_tc_gemv_workspace", ctypes.c_int, ctypes.c_int, _szp, _szp)
+_sig("rngd_device_status", ctypes.POINTER(ctypes.c_int), ctypes.c_int)
 _sig("rngd_gemv_bf16", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
      ctypes.c_int, _vp)
 _sig("rngd_rmsnorm_f32", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_float, _vp, _vp)
@@ -108,6 +115,19 @@ def stream_handle(stream=None):
 def ptr(t):
     """Device pointer of a torch tensor (None -> NULL)."""
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def device_status(reset=True):
+    """Status word of the kernels' bounded waits: 0, or the code of the first wait that timed out."""
+    st = ctypes.c_int(0)
+    call("rngd_device_status", ctypes.byref(st), 1 if reset else 0)
+    return st.value
+
+
+def decode_workspace(model, S):
+    out = [ctypes.c_size_t(0) for _ in range(4)]
+    call("rngd_decode_workspace", ctypes.byref(model), S, *[ctypes.byref(o) for o in out])
+    return [o.value for o in out]
 
 
 def exported_symbols():

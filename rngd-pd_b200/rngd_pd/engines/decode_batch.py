@@ -80,14 +80,17 @@ class BatchDecodeEngine:
         H, M = c.hidden, c.inter
         QN, KN = c.n_heads * c.head_dim, c.n_kv * c.head_dim
         f32 = dict(dtype=torch.float32, device=d)
+        partial_floats, counters, act_cols, act2_cols = _lib.decode_workspace(self._m, S)
         self._x = torch.zeros((MAXB, H), **f32)
-        self._h = torch.zeros((MAXB, max(H, M)), **f32)
-        self._qkv = torch.zeros((MAXB, QN + 2 * KN), **f32)
         self._q = torch.zeros((MAXB, QN), **f32)
-        self._ao = torch.zeros((MAXB, QN), **f32)
-        self._gu = torch.zeros((MAXB, 2 * M), **f32)
+        # hi/lo bf16 GEMM operands: rows of streams >= B must stay zero
+        self._act = torch.zeros((2 * MAXB, act_cols), dtype=BF, device=d)
+        self._act2 = torch.zeros((2 * MAXB, act2_cols), dtype=BF, device=d)
         self._logits = torch.zeros((B, self.V), **f32)
         self._part = torch.zeros((B, c.n_heads, S // ATTN_CHUNK, c.head_dim + 2), **f32)
+        self._partial = torch.zeros(max(partial_floats, 1), **f32)
+        self._counters = torch.zeros(max(counters, 1), dtype=torch.int32, device=d)
+        self._best = torch.zeros(MAXB, dtype=torch.int64, device=d)
         self._toks = torch.zeros(B, dtype=torch.int32, device=d)
         self._pos = torch.zeros(B, dtype=torch.int32, device=d)
         self._next = torch.zeros(B, dtype=torch.int32, device=d)
@@ -97,18 +100,18 @@ class BatchDecodeEngine:
         self.use_graph = os.environ.get("RNGD_CUDA_GRAPH", "1") != "0"
         self._graphs = {}
         self._copied = torch.cuda.Event()
-        # embed; per layer rms, qkv, rope+kv, attn partial, attn combine, o, rms, gate/up, swiglu, down;
-        # lm_head rms, gemv, argmax
-        self.launches_per_step = 1 + self.nl * 10 + 3 + 1   # + advance
+        # embed; per layer: prep, QKV gemm, attn partial, attn combine, O gemm, prep, gate/up gemm,
+        # down gemm; lm_head: prep, gemm, argmax finalize; advance
+        self.launches_per_step = 1 + self.nl * 8 + 3 + 1
 
     # ------------------------------------------------------------ buffers
     def _io(self, Kg, Vg):
-        return _lib.DecodeIO(B=self.B, Bcap=self.B, S=self.S, kv_layers=self.NG, kcache=Kg.data_ptr(),
-                             vcache=Vg.data_ptr(),
-                             toks=self._toks.data_ptr(), pos=self._pos.data_ptr(), x=self._x.data_ptr(),
-                             h=self._h.data_ptr(), qkv=self._qkv.data_ptr(), q=self._q.data_ptr(),
-                             ao=self._ao.data_ptr(), gu=self._gu.data_ptr(), logits=self._logits.data_ptr(),
-                             attn_part=self._part.data_ptr(), next=self._next.data_ptr())
+        p = lambda t: t.data_ptr()
+        return _lib.DecodeIO(B=self.B, Bcap=self.B, S=self.S, kv_layers=self.NG, kcache=p(Kg), vcache=p(Vg),
+                             toks=p(self._toks), pos=p(self._pos), x=p(self._x), q=p(self._q),
+                             act=p(self._act), act2=p(self._act2), logits=p(self._logits),
+                             attn_part=p(self._part), partial=p(self._partial), counters=p(self._counters),
+                             best=p(self._best), next=p(self._next))
 
     def _check_cache(self, Kd, Vd):
         c = self.cfg

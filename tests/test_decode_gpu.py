@@ -56,6 +56,36 @@ def test_gemv_matches_fp32(B, N, K):
         np.testing.assert_allclose(Yd.cpu().numpy(), want.numpy(), rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("B,N,K", [(1, 128, 64), (4, 256, 512), (16, 384, 4096), (16, 4096, 14336),
+                                   (3, 28672, 4096)])
+def test_tc_gemv_matches_fp32(B, N, K):
+    """tcgen05 GEMV (hi/lo bf16 operand, TMEM fp32 accumulation, split-K) vs fp32 matmul."""
+    import ctypes
+    from rngd_pd import _lib
+    g = torch.Generator().manual_seed(N + K + B)
+    W = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    X = torch.randn(B, K, generator=g)
+    Y0 = torch.randn(B, N, generator=g)
+    want = (W.double() @ X.double().T).T + Y0.double()
+    pf, ct = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    _lib.call("rngd_tc_gemv_workspace", N, K, ctypes.byref(pf), ctypes.byref(ct))
+    act = torch.zeros(32, K, dtype=torch.bfloat16, device="cuda")
+    part = torch.zeros(max(pf.value, 1), device="cuda")
+    cnt = torch.zeros(max(ct.value, 1), dtype=torch.int32, device="cuda")
+    Wd, Xd = W.cuda(), X.cuda()
+    for rep in range(2):                     # the second run reuses the self-resetting counters
+        Yd = Y0.clone().cuda()
+        _lib.call("rngd_tc_gemv", _lib.ptr(Wd), N, K, _lib.ptr(Xd), K, B, _lib.ptr(Yd), N, _lib.ptr(act),
+                  _lib.ptr(part), _lib.ptr(cnt), _lib.stream_handle())
+        torch.cuda.synchronize()
+        assert _lib.device_status() == 0
+        got = Yd.cpu().double()
+        scale = (W.double().abs() @ X.double().abs().T).T.max().item()
+        err = (got - want).abs().max().item()
+        assert err <= 2e-6 * scale + 1e-6, f"max err {err} (scale {scale})"
+        assert int(cnt.sum().item()) == 0
+
+
 def test_rmsnorm_matches_reference_formula():
     from rngd_pd import _lib
     x = torch.randn(5, 4096) * 3
