@@ -130,36 +130,147 @@ def run_reference(args):
     }), flush=True)
 
 
-def gemv_roofline(eng, reps=20):
-    """Dominant kernel (the decode GEMV) timed alone with CUDA events on its stream."""
+class TcGemm:
+    """One decode GEMM shape through rngd_tc_gemv: weights [L][N][K], the hi/lo operand prepared once."""
+
+    def __init__(self, weights, N, K, dev):
+        import ctypes
+        import torch
+        from rngd_pd import _lib
+        self.W, self.N, self.K = weights, N, K
+        pf, ct = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _lib.call("rngd_tc_gemv_workspace", N, K, ctypes.byref(pf), ctypes.byref(ct))
+        self.X = torch.randn(B, K, device=dev)
+        self.Y = torch.zeros(B, N, device=dev)
+        self.act = torch.zeros(32, K, dtype=torch.bfloat16, device=dev)
+        self.part = torch.zeros(max(pf.value, 1), device=dev)
+        self.cnt = torch.zeros(max(ct.value, 1), dtype=torch.int32, device=dev)
+        self.run(0, prep=1)
+        self.nbytes = N * K * 2 + 32 * K * 2 + B * N * 4 * 2   # weights + operand + y read/write
+
+    def run(self, layer, prep=0, stream=None):
+        from rngd_pd import _lib
+        _lib.call("rngd_tc_gemv", _lib.ptr(self.W[layer]), self.N, self.K, _lib.ptr(self.X), self.K, B,
+                  _lib.ptr(self.Y), self.N, _lib.ptr(self.act), _lib.ptr(self.part), _lib.ptr(self.cnt), prep,
+                  _lib.stream_handle(stream))
+
+    def time(self, reps, stream, trace=None):
+        """Mean launch duration (ms) over `reps` back-to-back launches (captured in a CUDA graph so host
+        launch cost does not gate short kernels), rotating through the layers so weights are cold.
+        trace: optional int64 device buffer [reps][1024][5] for per-launch CTA timelines."""
+        import torch
+        from rngd_pd import _lib
+        L = len(self.W)
+        side = torch.cuda.Stream(device=self.X.device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for i in range(3):
+                self.run(i % L, stream=side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                for i in range(reps):
+                    if trace is not None:
+                        _lib.call("rngd_tc_gemv_trace", _lib.ptr(trace[i]))
+                    self.run(i % L, stream=side)
+            if trace is not None:
+                _lib.call("rngd_tc_gemv_trace", None)
+            g.replay()                                   # warm
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(side)
+            g.replay()
+            e1.record(side)
+        e1.synchronize()
+        stream.wait_stream(side)
+        return e0.elapsed_time(e1) / reps
+
+
+def gemm_roofline(eng, reps=32):
+    """The dominant kernel (the tcgen05 decode GEMM, wsgemm_kernel) per weight shape, CUDA events on its stream."""
+    import torch
+    w, c = eng.w, eng.cfg
+    H, M = c.hidden, c.inter
+    s = torch.cuda.current_stream(eng.dev)
+    out = {}
+    for name, W, N, K in (("gate_up", w.wgu, 2 * M, H), ("qkv", w.wqkv, w.NQKV, H), ("o", w.wo, H, H),
+                          ("down", w.wd, H, M)):
+        g = TcGemm(W, N, K, eng.dev)
+        ms = g.time(reps, s)
+        out[name] = {"ms": ms, "bytes": g.nbytes, "gbs": g.nbytes / ms / 1e6}
+        del g
+    return out
+
+
+def run_micro_attn(args):
+    """The decode attention (split-S partials + combine) for one layer at config 4's lengths."""
     import torch
     from rngd_pd import _lib
-    w = eng.w
-    c = eng.cfg
-    H, M = c.hidden, c.inter
-    shapes = {"gate_up": (w.wgu[0], 2 * M, H), "qkv": (w.wqkv[0], w.NQKV, H), "o": (w.wo[0], H, H),
-              "down": (w.wd[0], H, M)}
-    X = torch.randn(B, max(H, M), device=eng.dev)
-    Y = torch.empty(B, 2 * M, device=eng.dev)
-    s = torch.cuda.current_stream(eng.dev)
-    h = _lib.stream_handle(s)
-    out = {}
-    for name, (Wt, N, K) in shapes.items():
-        Wl = [eng.w.wgu[l] if name == "gate_up" else (eng.w.wqkv[l] if name == "qkv" else
-              (eng.w.wo[l] if name == "o" else eng.w.wd[l])) for l in range(c.n_layers)]
-        for i in range(3):
-            _lib.call("rngd_gemv_bf16", _lib.ptr(Wl[i]), N, K, _lib.ptr(X), max(H, M), B, _lib.ptr(Y), N, 0, h)
+    dev = torch.device("cuda", 0)
+    NH, NKV, HD = 32, 8, 128
+    lens, _ = lengths_and_tokens()
+    pos = torch.tensor([l + 64 for l in lens], dtype=torch.int32, device=dev)
+    layers = 8                                       # rotate layers: 8 x 33.5 MB of cache > L2
+    K = torch.randn(layers, B, NKV, S, HD, device=dev).to(torch.bfloat16)
+    V = torch.randn(layers, B, NKV, S, HD, device=dev).to(torch.bfloat16)
+    q = torch.randn(B, NH * HD, device=dev)
+    part = torch.empty(B, NH, S // 128, HD + 2, device=dev)
+    ao = torch.empty(B, NH * HD, device=dev)
+    side = torch.cuda.Stream(device=dev)
+    def run(l, st):
+        _lib.call("rngd_attn_decode", _lib.ptr(q), _lib.ptr(K[l]), _lib.ptr(V[l]), _lib.ptr(pos), B, B, NH, NKV, HD,
+                  S, _lib.ptr(part), _lib.ptr(ao), _lib.stream_handle(st))
+    with torch.cuda.stream(side):
+        for l in range(3):
+            run(l, side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(args.steps):
+                run(i % layers, side)
+        g.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(s)
-        for i in range(reps):   # rotate layers: each launch reads cold weights
-            _lib.call("rngd_gemv_bf16", _lib.ptr(Wl[i % c.n_layers]), N, K, _lib.ptr(X), max(H, M), B,
-                      _lib.ptr(Y), N, 0, h)
-        e1.record(s)
-        e1.synchronize()
-        ms = e0.elapsed_time(e1) / reps
-        nbytes = N * K * 2 + B * K * 4 + B * N * 4
-        out[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6}
-    return out
+        e0.record(side)
+        g.replay()
+        e1.record(side)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = sum(int(p) + 1 for p in pos.tolist()) * NKV * HD * 2 * 2
+    print(json.dumps({"micro": "attn", "B": B, "S": S, "ms": ms, "kv_bytes": nbytes, "gbs": nbytes / ms / 1e6}),
+          flush=True)
+
+
+def run_micro(args):
+    """One decode GEMM shape alone (small device footprint; for ncu captures of skgemm_kernel)."""
+    import torch
+    from rngd_pd import synth
+    if args.micro == "attn":
+        return run_micro_attn(args)
+    shapes = {"gate_up": (28672, 4096), "qkv": (6144, 4096), "o": (4096, 4096), "down": (4096, 14336),
+              "lm": (128256, 4096)}
+    N, K = shapes[args.micro]
+    dev = torch.device("cuda", 0)
+    W = torch.empty((2, N, K), dtype=torch.bfloat16, device=dev)   # two layers' worth: > L2, alternated
+    synth.fill_gauss(W, 0, 4, 0.02)
+    g = TcGemm(W, N, K, dev)
+    ms = g.time(args.steps, torch.cuda.current_stream(dev))
+    # traced graph of 4 launches: per launch, CTA stamps relative to launch 0's earliest start (us)
+    tr = torch.zeros((4, 1024, 5), dtype=torch.int64, device=dev)
+    g.time(4, torch.cuda.current_stream(dev), trace=tr)
+    t = tr.cpu().double()
+    t0 = t[0, :, 0][t[0, :, 0] > 0].min()
+    timeline = []
+    for i in range(4):
+        ti = t[i][t[i, :, 0] > 0]
+        rel = (ti - t0) / 1e3
+        q = lambda col: [round(float(rel[:, col].min()), 2), round(float(rel[:, col].max()), 2)]
+        timeline.append({"start": q(0), "operand": q(1), "last_tma": q(2), "last_acc": q(3), "end": q(4)})
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    print(json.dumps({"micro": args.micro, "N": N, "K": K, "B": B, "ms": ms, "bytes": g.nbytes,
+                      "gbs": g.nbytes / ms / 1e6, "frac_hbm": g.nbytes / ms / 1e6 / hbm,
+                      "pdl": os.environ.get("RNGD_PDL", "1"), "timeline_us_min_max": timeline}), flush=True)
 
 
 def run_ours(args):
@@ -231,7 +342,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_s = float(t.item())
 
-    roof = gemv_roofline(eng) if rank == 0 else None
+    roof = gemm_roofline(eng) if rank == 0 else None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -248,7 +359,7 @@ def run_ours(args):
     dom = roof["gate_up"]
     traffic = None
     try:
-        traffic = _j.load(open(os.path.join(REPO, "profiles", "traffic.json"))).get("gemv_gate_up")
+        traffic = _j.load(open(os.path.join(REPO, "profiles", "traffic.json"))).get("wsgemm_gate_up")
     except (OSError, ValueError):
         pass
     cpu = None
@@ -266,7 +377,7 @@ def run_ours(args):
         "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes,
                           "achieved": step_bytes / (ms_step / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
                           "frac": step_bytes / (ms_step / 1e3) / 1e9 / hbm, "peak_kind": peak_kind},
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel (gate/up 28672x4096, B=16)",
+        "roofline": {"bound": "hbm", "kernel": "skgemm_kernel (tcgen05 stream-K, gate/up 28672x4096, B=16)",
                      "achieved": dom["gbs"], "peak": hbm, "unit": "GB/s", "frac": dom["gbs"] / hbm,
                      "traffic": traffic, "peak_kind": peak_kind,
                      "per_shape": {k: round(v["gbs"], 1) for k, v in roof.items()}},
@@ -286,10 +397,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn"],
+                    help="time one decode GEMM shape alone (small footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.micro:
+        run_micro(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

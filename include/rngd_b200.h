@@ -82,8 +82,10 @@ typedef struct rngd_decode_io {
   const int32_t* pos;   /* device [B] position each token is written at */
   float* x;             /* fp32 [16][H] residual stream */
   float* q;             /* fp32 [16][NH*HD] rotated queries */
-  void* act;            /* bf16 [32][max(H, NH*HD)] GEMM operand (zeroed at allocation) */
+  void* act;            /* bf16 [32][max(H, NH*HD)] operand of x * norm weight (zeroed at allocation) */
+  void* act_o;          /* bf16 [32][NH*HD] attention-output operand (zeroed at allocation) */
   void* act2;           /* bf16 [32][M] down-projection operand (zeroed at allocation) */
+  float* ss;            /* fp32 [H/128][16] per-128-column sums of squares of x (RMSNorm) */
   float* logits;        /* fp32 [B][V] */
   float* attn_part;     /* fp32 scratch [B][NH][S/128][HD+2] */
   float* partial;       /* fp32 split-K scratch, rngd_decode_workspace() floats */
@@ -98,7 +100,8 @@ int rngd_decode_workspace(const rngd_model_t* m, int S, size_t* partial_floats, 
 /* Device status word of the bounded waits (0 = none timed out); reset clears it. */
 int rngd_device_status(int* status, int reset);
 
-/* x = embed[toks] (engines/decode_batch.py:432). */
+/* x = embed[toks] (engines/decode_batch.py:432), plus the first layer's
+ * operand x * n1[0] and its sums of squares; clears the argmax keys. */
 int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream);
 /* Layers [layer0, layer1) of the batched decode step, updating the cache at
  * pos[b]; io->kcache/vcache hold exactly those layers (layer1 - layer0 <=
@@ -127,10 +130,15 @@ int rngd_gemv_bf16(const void* W, int N, int K, const float* X, int ldx, int B, 
  * sum_k W[n][k] * X[b][k] through tcgen05 with the fp32 X split into bf16
  * hi + lo operand rows.  act: zeroed bf16 scratch [32][K]; partial/counters:
  * split-K scratch of rngd_tc_gemv_workspace() (counters zeroed once).
+ * prep = 0 reuses the operand already in act (X is not read).
  * N % 128 == 0, K % 64 == 0, B <= 16. */
 int rngd_tc_gemv(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy, void* act,
-                 float* partial, int32_t* counters, rngd_stream_t stream);
+                 float* partial, int32_t* counters, int prep, rngd_stream_t stream);
 int rngd_tc_gemv_workspace(int N, int K, size_t* partial_floats, size_t* counters);
+/* Diagnostics: when trace != NULL, later rngd_tc_gemv launches record per CTA five
+ * %globaltimer stamps [start, operand ready, last TMA issued, last accumulator
+ * ready, end] into trace[cta*5 ..] (device memory, >= 5 * SM count entries). */
+int rngd_tc_gemv_trace(uint64_t* trace);
 /* out[r][k] = x[r][k] / sqrt(mean_k x^2 + eps) * w[k] (kernels/decode_batch.py:130). */
 int rngd_rmsnorm_f32(const float* x, int R, int H, const float* w, float eps, float* out,
                      rngd_stream_t stream);

@@ -11,7 +11,7 @@
 //             -> down GEMV (+= residual)
 // HBM-bound: the GEMVs stream 436 MB of weights per layer; activations are a
 // few hundred KB and stay in L1/L2.
-#include "common.cuh"
+#include "tc.cuh"
 
 namespace rngd {
 
@@ -177,13 +177,17 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
                                                            const int32_t* __restrict__ pos, int NH,
                                                            int NKV, int S, float* __restrict__ part) {
   const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31;
   const int nchunk = gridDim.x;
-  const int P = min(pos[b] + 1, S);
-  const int s0 = c * kChunk;
   const int PS = kHD + 2;  // partial record: o[HD], m, l
-  __shared__ float qs[kG][kHD];
+  __shared__ __align__(16) float qs[kG][kHD];
   __shared__ float ps[kG][kChunk];
   __shared__ float red[kG][4];
+  __shared__ __align__(16) float ored[8][kG][kHD];   // P.V partials of the 8 position groups
+  grid_dep_wait();
+  grid_dep_launch();  // every CTA of this grid is running: the next kernel may start its prologue
+  const int P = min(pos[b] + 1, S);
+  const int s0 = c * kChunk;
   float* rec0 = part + (((size_t)b * NH + kvh * kG) * nchunk + c) * PS;
   if (s0 >= P) {
     if (t < kG) {
@@ -193,64 +197,107 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
     }
     return;
   }
+  const int n = min(kChunk, P - s0);
   const float scale = 0.08838834764831845f;  // 1/sqrt(128) in fp32
   for (int i = t; i < kG * kHD; i += 128)
     qs[i / kHD][i % kHD] = q[(size_t)b * ldq + (size_t)(kvh * kG + i / kHD) * kHD + i % kHD];
   __syncthreads();
-  const int s = s0 + t;
-  const bool valid = s < P;
   const size_t head_base = ((size_t)b * NKV + kvh) * (size_t)S * kHD;
-  float sc[kG] = {0.f, 0.f, 0.f, 0.f};
-  if (valid) {
-    const uint16_t* krow = kc + head_base + (size_t)s * kHD;
-#pragma unroll 4
-    for (int d = 0; d < kHD; d += 8) {
-      float kf[8];
-      unpack8(*reinterpret_cast<const uint4*>(krow + d), kf);
+  const uint16_t* kbase = kc + head_base + (size_t)s0 * kHD;
+  const uint16_t* vbase = vc + head_base + (size_t)s0 * kHD;
+
+  // scores: 4 lanes per position (32 dims each), 8 positions per warp pass, 4 passes per warp
+  const int sub = lane >> 2, part4 = lane & 3;
+  float sc[4][kG];
 #pragma unroll
-      for (int g = 0; g < kG; g++)
+  for (int it = 0; it < 4; it++) {
+    const int j = warp * 32 + it * 8 + sub;   // position within the chunk
+    float acc[kG] = {0.f, 0.f, 0.f, 0.f};
+    if (j < n) {
+      const uint16_t* krow = kbase + (size_t)j * kHD + part4 * 32;
 #pragma unroll
-        for (int j = 0; j < 8; j++) sc[g] = fmaf(qs[g][d + j], kf[j], sc[g]);
+      for (int v4 = 0; v4 < 4; v4++) {
+        float kf[8];
+        unpack8(*reinterpret_cast<const uint4*>(krow + v4 * 8), kf);
+#pragma unroll
+        for (int g = 0; g < kG; g++) {
+          const float4 qa = *reinterpret_cast<const float4*>(&qs[g][part4 * 32 + v4 * 8]);
+          const float4 qb = *reinterpret_cast<const float4*>(&qs[g][part4 * 32 + v4 * 8 + 4]);
+          acc[g] = fmaf(qa.x, kf[0], acc[g]); acc[g] = fmaf(qa.y, kf[1], acc[g]);
+          acc[g] = fmaf(qa.z, kf[2], acc[g]); acc[g] = fmaf(qa.w, kf[3], acc[g]);
+          acc[g] = fmaf(qb.x, kf[4], acc[g]); acc[g] = fmaf(qb.y, kf[5], acc[g]);
+          acc[g] = fmaf(qb.z, kf[6], acc[g]); acc[g] = fmaf(qb.w, kf[7], acc[g]);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kG; g++) {
+      float v = acc[g];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      sc[it][g] = j < n ? v * scale : -INFINITY;
     }
   }
-  const int warp = t >> 5, lane = t & 31;
-  float mx[kG], sum[kG];
+  // softmax statistics of the chunk (per head)
 #pragma unroll
   for (int g = 0; g < kG; g++) {
-    sc[g] = valid ? sc[g] * scale : -INFINITY;
-    float m = warp_max(sc[g]);
+    float m = fmaxf(fmaxf(sc[0][g], sc[1][g]), fmaxf(sc[2][g], sc[3][g]));
+    m = warp_max(m);
     if (lane == 0) red[g][warp] = m;
   }
   __syncthreads();
+  float mx[kG];
 #pragma unroll
   for (int g = 0; g < kG; g++) mx[g] = fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]));
   __syncthreads();
 #pragma unroll
   for (int g = 0; g < kG; g++) {
-    float p = valid ? expf(sc[g] - mx[g]) : 0.f;
-    ps[g][t] = p;
-    float ssum = warp_sum(p);
+    float ssum = 0.f;
+#pragma unroll
+    for (int it = 0; it < 4; it++) {
+      const int j = warp * 32 + it * 8 + sub;
+      const float p = j < n ? expf(sc[it][g] - mx[g]) : 0.f;
+      if (part4 == 0) ps[g][j] = p;
+      ssum += part4 == 0 ? p : 0.f;
+    }
+    ssum = warp_sum(ssum);
     if (lane == 0) red[g][warp] = ssum;
   }
   __syncthreads();
+  // P.V: thread t owns dims dg*8..dg*8+7 for positions pg, pg+8, ...; partials reduced over pg
+  const int dg = t & 15, pg = t >> 4;
+  float o[kG][8];
 #pragma unroll
-  for (int g = 0; g < kG; g++) sum[g] = (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
-  // P.V: thread t owns output dimension t for the 4 heads
-  const int n = min(kChunk, P - s0);
-  float o[kG] = {0.f, 0.f, 0.f, 0.f};
-  const uint16_t* vcol = vc + head_base + (size_t)s0 * kHD + t;
-  for (int j = 0; j < n; j++) {
-    const float vv = bf2f(vcol[(size_t)j * kHD]);
+  for (int g = 0; g < kG; g++)
 #pragma unroll
-    for (int g = 0; g < kG; g++) o[g] = fmaf(ps[g][j], vv, o[g]);
+    for (int d = 0; d < 8; d++) o[g][d] = 0.f;
+#pragma unroll 4
+  for (int j = pg; j < n; j += 8) {
+    float vf[8];
+    unpack8(*reinterpret_cast<const uint4*>(vbase + (size_t)j * kHD + dg * 8), vf);
+#pragma unroll
+    for (int g = 0; g < kG; g++) {
+      const float p = ps[g][j];
+#pragma unroll
+      for (int d = 0; d < 8; d++) o[g][d] = fmaf(p, vf[d], o[g][d]);
+    }
   }
 #pragma unroll
   for (int g = 0; g < kG; g++) {
+    *reinterpret_cast<float4*>(&ored[pg][g][dg * 8]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+    *reinterpret_cast<float4*>(&ored[pg][g][dg * 8 + 4]) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < kG; g++) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) acc += ored[k][g][t];
     float* rec = rec0 + (size_t)g * nchunk * PS;
-    rec[t] = o[g];
+    rec[t] = acc;
     if (t == 0) {
       rec[kHD] = mx[g];
-      rec[kHD + 1] = sum[g];
+      rec[kHD + 1] = (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
     }
   }
 }
@@ -259,6 +306,8 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
 // grid (NH, B), block HD.
 __global__ void attn_combine_kernel(const float* __restrict__ part, int nchunk, float* __restrict__ ao,
                                     int ldao, int NH, uint16_t* __restrict__ act, int ld_act) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int PS = kHD + 2;
   const float* rec = part + ((size_t)b * NH + h) * nchunk * PS;
@@ -291,11 +340,10 @@ static int launch_attn(const float* q, int ldq, const void* kc, const void* vc, 
   RNGD_REQUIRE(S % kChunk == 0 && S > 0 && S <= 8192, "attn_decode: S=%d must be a multiple of 128", S);
   RNGD_REQUIRE(B >= 1, "attn_decode: B=%d", B);
   const int nchunk = S / kChunk;
-  attn_partial_kernel<<<dim3(nchunk, NKV, B), 128, 0, s>>>(q, ldq, (const uint16_t*)kc, (const uint16_t*)vc,
-                                                          pos, NH, NKV, S, part);
-  RNGD_TRY(check_launch("attn_partial_kernel"));
-  attn_combine_kernel<<<dim3(NH, B), kHD, 0, s>>>(part, nchunk, ao, ldao, NH, act, ld_act);
-  return check_launch("attn_combine_kernel");
+  RNGD_TRY(launch_pdl(attn_partial_kernel, dim3(nchunk, NKV, B), dim3(128), 0, s, "attn_partial_kernel", q, ldq,
+                      (const uint16_t*)kc, (const uint16_t*)vc, pos, NH, NKV, S, part));
+  return launch_pdl(attn_combine_kernel, dim3(NH, B), dim3(kHD), 0, s, "attn_combine_kernel", (const float*)part,
+                    nchunk, ao, ldao, NH, act, ld_act);
 }
 
 int launch_attn_decode(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B, int NH,
@@ -325,6 +373,8 @@ __global__ void swiglu_kernel(const float* __restrict__ gu, int ldgu, int Mi, fl
 // ------------------------------------------------------------ embedding
 __global__ void embed_kernel(const uint16_t* __restrict__ emb, const int32_t* __restrict__ toks, int H,
                              int V, float* __restrict__ x) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int b = blockIdx.x;
   int t = toks[b];
   t = t < 0 ? 0 : (t >= V ? V - 1 : t);
@@ -376,6 +426,10 @@ __global__ void advance_kernel(int32_t* __restrict__ toks, int32_t* __restrict__
   }
 }
 
+int launch_embed(const void* emb, const int32_t* toks, int H, int V, float* x, int B, cudaStream_t s) {
+  return launch_pdl(embed_kernel, dim3(B), dim3(256), 0, s, "embed_kernel", (const uint16_t*)emb, toks, H, V, x);
+}
+
 }  // namespace rngd
 
 using namespace rngd;
@@ -396,13 +450,6 @@ extern "C" int rngd_attn_decode(const float* q, const void* kc, const void* vc, 
   RNGD_REQUIRE(B <= Bcap, "attn_decode: B=%d > Bcap=%d", B, Bcap);
   return launch_attn_decode(q, NH * HD, kc, vc, pos, B, NH, NKV, HD, S, part, ao, NH * HD,
                             (cudaStream_t)stream);
-}
-
-extern "C" int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream) {
-  RNGD_REQUIRE(m && io && m->embed && io->toks && io->x, "decode_embed: null argument");
-  RNGD_REQUIRE(io->B >= 1 && io->B <= 16, "decode_embed: B=%d outside 1..16", io->B);
-  embed_kernel<<<io->B, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)m->embed, io->toks, m->H, m->V, io->x);
-  return check_launch("embed_kernel");
 }
 
 extern "C" int rngd_decode_advance(const rngd_decode_io_t* io, rngd_stream_t stream) {

@@ -1,4 +1,4 @@
-// Tensor-core decode step: weight-streaming tcgen05 GEMMs with fused epilogues.
+// Tensor-core decode step: persistent stream-K tcgen05 GEMMs with fused epilogues.
 //
 // A decode GEMM is Y[b][n] = sum_k W[n][k] * h[b][k] with W bf16 (HBM, read
 // once per step) and h fp32.  It runs on tcgen05 as D = A * B^T with
@@ -6,17 +6,31 @@
 //   B = the activation operand: 32 bf16 rows = 16 streams x {hi, lo}, where
 //       hi = bf16(h) and lo = bf16(h - hi), so hi + lo carries ~16 mantissa
 //       bits of the fp32 activation and W*hi + W*lo (fp32 accumulation in
-//       TMEM) stays at fp32-level accuracy,
-//   D = 128 x 32 fp32 accumulators in tensor memory.
-// Work unit = (128-row tile, K split).  Split decisions depend only on the
-// matrix shape (never on B), and the last CTA to finish a tile sums the split
-// partials in split order, so every stream's result is deterministic and
-// independent of which other streams share the batch.
+//       TMEM) keeps fp32-level accuracy,
+//   D = 128 x 32 fp32 accumulators in tensor memory (double-buffered).
 //
-// Epilogues (run by the CTA that completes a tile):
+// Scheduling (stream-K).  One CTA per SM.  The GEMM's tiles x K-blocks are laid
+// end to end and cut into one equal contiguous range per CTA, so every SM
+// streams the same number of weight bytes and the TMA ring never drains between
+// tiles.  A tile cut between CTAs leaves one fp32 partial per piece; the CTA
+// that finishes a tile's last piece sums the pieces in K order.  The cut
+// depends only on (N, K, CTA count), never on B, so a stream's result is
+// deterministic and independent of what else is batched with it.
+//
+// Programmatic dependent launch.  The producer issues the first weight tiles
+// BEFORE griddepcontrol.wait (weights do not depend on the previous kernel),
+// so each GEMM's HBM stream starts while the previous kernel finishes.
+//
+// RMSNorm is folded in: rms(x) * w @ W^T = (x * w) @ W^T / sqrt(mean(x^2) + eps).
+// The producer of x (embedding, residual epilogues) writes the operand of
+// x * w_next and per-128-column sums of squares; the consumer's epilogue
+// scales each stream's row by 1 / sqrt(sum / H + eps).
+//
+// Epilogues (run for a tile once all its K pieces are in):
 //   QKV     RoPE (rotate-half, fp32 angles) on q and k; q -> fp32 buffer,
-//           k and v -> bf16 cache at pos[b]      (kernels/decode_batch.py:77-82)
-//   RESID   x[b][n] += y                          (zipadd, kernels/decode_batch.py:87,91)
+//           k and v -> bf16 cache at pos[b]      (kernels/decode_batch.py:76-82)
+//   RESID   x[b][n] += y, plus the next GEMM's operand and its sums of squares
+//                                                 (zipadd + rms, kernels/decode_batch.py:87-88,91)
 //   SWIGLU  silu(gate) * up for the tile's 64 features -> hi/lo operand of the
 //           down GEMM                             (kernels/decode_batch.py:88-90)
 //   LOGITS  logits[b][n] = y and a first-max argmax key per stream
@@ -33,15 +47,21 @@ __device__ int g_status_decode = 0;  // this file's bounded-wait status word
 constexpr int BM = 128, BK = 64, BNC = 32, MAXB = 16;
 constexpr int A_BYTES = BM * BK * 2;   // 16 KB weight tile per stage
 constexpr int B_BYTES = BNC * BK * 2;  // 4 KB activation tile per stage
-constexpr int STAGES = 4;
+constexpr int STAGES = 5;
 constexpr int YS_LD = 17;
+constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int TMEM_COLS = 64;          // two 32-column accumulators
 
 enum Epi : int { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
 
 struct GemmArgs {
-  int N, K, nkb, nsplit, layer, B;
-  float* partial;
-  int* counters;
+  int N, K, nkb, tiles, total, maxseg, layer, B;
+  float* partial;   // [tiles][maxseg][128][16]
+  int* counters;    // [tiles]
+  // rms scale of the result (QKV, SWIGLU, LOGITS); ss_in == nullptr -> no scaling
+  const float* ss_in;  // [ss_tiles][16] per-128-column sums of squares of x
+  int ss_tiles;
+  float eps, inv_h;
   // QKV
   const int32_t* pos;
   const float* inv;
@@ -50,9 +70,13 @@ struct GemmArgs {
   uint16_t* kc;
   uint16_t* vc;
   int NH, NKV, S;
-  // RESID
+  // RESID: x += y; act_next = hi/lo(x * w_next); ss_out = per-tile sums of squares of x
   float* x;
   int ldx;
+  const float* w_next;
+  uint16_t* act_next;
+  int ld_next;
+  float* ss_out;
   // SWIGLU
   uint16_t* act_out;
   int ld_act;
@@ -60,48 +84,70 @@ struct GemmArgs {
   float* logits;
   unsigned long long* best;
   int V;
+  // optional per-CTA timeline (ns, %globaltimer): [cta][start, operand ready, last TMA issued,
+  // last accumulator ready, end]; nullptr = off
+  unsigned long long* trace;
 };
 
-constexpr size_t kSmemBytes = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + 3 * STAGES * 8 + 64 +
-                              BM * YS_LD * 4 + 64;
+// smem: stages | barriers (2*STAGES + 4) + tmem slot/flags (64 B) | scale (64 B) | ys | s_red
+constexpr size_t kBarBytes = (2 * STAGES + 4) * 8;
+constexpr size_t kSmemBytes = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + kBarBytes + 64 + 64 +
+                              BM * YS_LD * 4 + 4 * MAXB * 8;
 
 __device__ __forceinline__ uint32_t orderable(float f) {
   uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// CTA owning flattened K-block f under the equal split of `total` over `grid` CTAs.
+__host__ __device__ __forceinline__ int owner_of(long f, long total, int grid) {
+  return (int)(((f + 1) * grid - 1) / total);
+}
+
 template <int EPI>
-__global__ void __launch_bounds__(128) wsgemm_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                     const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                            const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = base;
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint64_t* full = (uint64_t*)(sB + STAGES * B_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = (uint32_t*)(accum + 1);
+  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + kBarBytes);
   int* s_last = (int*)(tmem_slot + 1);
-  float* ys = (float*)(base + STAGES * (A_BYTES + B_BYTES) + 3 * STAGES * 8 + 64);
+  float* s_scale = (float*)((uint8_t*)full + kBarBytes + 64);  // [16]
+  float* ys = (float*)((uint8_t*)full + kBarBytes + 128);
+  unsigned long long* s_red = (unsigned long long*)(ys + BM * YS_LD);  // [4][16]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int unit = blockIdx.x;
-  const int tile = unit / a.nsplit, split = unit - tile * a.nsplit;
-  const int kb0 = (int)((long)split * a.nkb / a.nsplit), kb1 = (int)((long)(split + 1) * a.nkb / a.nsplit);
-  const int nk = kb1 - kb0;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const long f0 = (long)cta * a.total / G, f1 = (long)(cta + 1) * a.total / G;
+  unsigned long long* tr = a.trace != nullptr ? a.trace + (size_t)cta * 5 : nullptr;
+  if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
   }
-  if (warp == 2) {
-    tmem_alloc(tmem_slot, 32);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -109,180 +155,275 @@ __global__ void __launch_bounds__(128) wsgemm_kernel(const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // TMA producer: weight tile + activation tile per 64-wide K block
-    for (int i = 0; i < nk; i++) {
-      const int s = i % STAGES;
-      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-      if (!mbar_wait(&empty[s], ph ^ 1u, ST_TMA_WAIT, &g_status_decode)) break;
-      mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
-      const int k = (kb0 + i) * BK;
-      tma_load_3d(sA + s * A_BYTES, &tmW, &full[s], k, tile * BM, a.layer);
-      tma_load_2d(sB + s * B_BYTES, &tmX, &full[s], k, 0);
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      const long nk = f1 - f0;
+      const long pre = nk < STAGES ? nk : STAGES;
+      // weights do not depend on the previous kernel: start streaming them now
+      for (long i = 0; i < pre; i++) {
+        const long f = f0 + i;
+        const int tile = (int)(f / a.nkb), kb = (int)(f - (long)tile * a.nkb);
+        mbar_arrive_expect_tx(&full[i], A_BYTES + B_BYTES);
+        tma_load_3d(sA + i * A_BYTES, &tmW, &full[i], kb * BK, tile * BM, a.layer);
+      }
+      grid_dep_wait();  // the activation operand is written by the previous kernel
+      if (tr != nullptr) tr[1] = globaltimer();
+      for (long i = 0; i < pre; i++) {
+        const long f = f0 + i;
+        const int kb = (int)(f % a.nkb);
+        tma_load_2d(sB + i * B_BYTES, &tmX, &full[i], kb * BK, 0);
+      }
+      for (long i = pre; i < nk; i++) {
+        const int s = (int)(i % STAGES);
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, ST_TMA_WAIT, &g_status_decode)) break;
+        const long f = f0 + i;
+        const int tile = (int)(f / a.nkb), kb = (int)(f - (long)tile * a.nkb);
+        mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+        tma_load_3d(sA + s * A_BYTES, &tmW, &full[s], kb * BK, tile * BM, a.layer);
+        tma_load_2d(sB + s * B_BYTES, &tmX, &full[s], kb * BK, 0);
+      }
+      if (tr != nullptr) tr[2] = globaltimer();
+      grid_dep_launch();  // all weight reads issued: the next kernel may start prefetching
     }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer: 4 x (128x32x16) per stage, accumulating in TMEM
-    const uint32_t idesc = idesc_bf16_f32(BM, BNC);
-    bool ok = true;
-    for (int i = 0; i < nk && ok; i++) {
-      const int s = i % STAGES;
-      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-      ok = mbar_wait(&full[s], ph, ST_MMA_WAIT, &g_status_decode);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t aBase = smem_u32(sA + s * A_BYTES), bBase = smem_u32(sB + s * B_BYTES);
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer: 4 x (128x32x16) per K block into the segment's accumulator
+      const uint32_t idesc = idesc_bf16_f32(BM, BNC);
+      long i = 0;
+      int seg = 0;
+      bool ok = true;
+      for (long f = f0; f < f1 && ok; seg++) {
+        const int tile = (int)(f / a.nkb);
+        const long fend = ((long)tile + 1) * a.nkb < f1 ? ((long)tile + 1) * a.nkb : f1;
+        const int buf = seg & 1;
+        const uint32_t aph = (uint32_t)(seg >> 1) & 1u;
+        ok = mbar_wait(&acc_empty[buf], aph ^ 1u, ST_MMA_WAIT, &g_status_decode);
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BNC);
+        for (long g = f; g < fend && ok; g++, i++) {
+          const int s = (int)(i % STAGES);
+          const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+          ok = mbar_wait(&full[s], ph, ST_MMA_WAIT, &g_status_decode);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t aBase = smem_u32(sA + s * A_BYTES), bBase = smem_u32(sB + s * B_BYTES);
 #pragma unroll
-      for (int kk = 0; kk < BK / 16; kk++)
-        umma_bf16(tmem, sw128_kmajor_desc(aBase + kk * 32), sw128_kmajor_desc(bBase + kk * 32), idesc,
-                  (i | kk) != 0);
-      umma_commit(&empty[s]);
-    }
-    umma_commit(accum);
-  }
-  __syncwarp();
-
-  // ---- accumulators -> registers (thread r owns row r of the tile)
-  mbar_wait(accum, 0, ST_EPI_WAIT, &g_status_decode);
-  tc_fence_after();
-  float v[32];
-  tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16), v);
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) tmem_dealloc(tmem, 32);
-
-  const int r = threadIdx.x;
-  const int n = tile * BM + r;
-  float y[MAXB];
-#pragma unroll
-  for (int b = 0; b < MAXB; b++) y[b] = v[b] + v[MAXB + b];
-
-  if (a.nsplit > 1) {
-    float4* dst = reinterpret_cast<float4*>(a.partial + ((size_t)split * a.N + n) * MAXB);
-#pragma unroll
-    for (int j = 0; j < 4; j++) __stcg(dst + j, make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]));
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) *s_last = (atomicAdd(&a.counters[tile], 1) == a.nsplit - 1);
-    __syncthreads();
-    if (!*s_last) return;
-    __threadfence();
-#pragma unroll
-    for (int b = 0; b < MAXB; b++) y[b] = 0.f;
-    for (int s = 0; s < a.nsplit; s++) {
-      const float4* src = reinterpret_cast<const float4*>(a.partial + ((size_t)s * a.N + n) * MAXB);
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float4 t = __ldcg(src + j);
-        y[4 * j] += t.x; y[4 * j + 1] += t.y; y[4 * j + 2] += t.z; y[4 * j + 3] += t.w;
+          for (int kk = 0; kk < BK / 16; kk++)
+            umma_bf16(d, sw128_kmajor_desc(aBase + kk * 32), sw128_kmajor_desc(bBase + kk * 32), idesc,
+                      (g != f || kk != 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[buf]);
+        f = fend;
       }
     }
-    if (threadIdx.x == 0) a.counters[tile] = 0;  // ready for the next launch
-  }
-
-  if constexpr (EPI == EPI_RESID) {
-    for (int b = 0; b < a.B; b++) a.x[(size_t)b * a.ldx + n] += y[b];
-  } else if constexpr (EPI == EPI_QKV) {
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps 2..5: thread r owns row r of the tile (TMEM lane r)
+    grid_dep_wait();
+    const int r = ((warp & 3) << 5) | lane;
+    const int et = threadIdx.x - 64;  // 0..127 index among the epilogue threads
+    int seg = 0;
+    for (long f = f0; f < f1; seg++) {
+      const int tile = (int)(f / a.nkb);
+      const long tstart = (long)tile * a.nkb;
+      const long fend = tstart + a.nkb < f1 ? tstart + a.nkb : f1;
+      const int buf = seg & 1;
+      mbar_wait(&acc_full[buf], (uint32_t)(seg >> 1) & 1u, ST_EPI_WAIT, &g_status_decode);
+      if (tr != nullptr && et == 0 && fend == f1) tr[3] = globaltimer();
+      __syncwarp();
+      tc_fence_after();
+      float v[32];
+      tmem_ld_32x32b_x32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * BNC), v);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      const int n = tile * BM + r;
+      float y[MAXB];
 #pragma unroll
-    for (int b = 0; b < MAXB; b++) ys[r * YS_LD + b] = y[b];
-    __syncthreads();
-    const int head = tile;  // one 128-row tile = one head
-    const int i = r & 63;
-    const bool lo_half = r < 64;
-    const int partner = r ^ 64;
-    if (head < a.NH + a.NKV) {
-      for (int b = 0; b < a.B; b++) {
-        const int p = a.pos[b];
-        float sn, cs;
-        sincosf((float)p * a.inv[i], &sn, &cs);
-        const float other = ys[partner * YS_LD + b];
-        const float o = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
-        if (head < a.NH) {
-          a.q[(size_t)b * a.ldq + n] = o;
-        } else if (p >= 0 && p < a.S) {
-          a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o);
+      for (int b = 0; b < MAXB; b++) y[b] = v[b] + v[MAXB + b];
+
+      const int first = owner_of(tstart, a.total, G), last = owner_of(tstart + a.nkb - 1, a.total, G);
+      const int nseg = last - first + 1;
+      bool run = true;
+      if (nseg > 1) {
+        const int slot = cta - first;
+        float4* dst = reinterpret_cast<float4*>(a.partial + (((size_t)tile * a.maxseg + slot) * BM + r) * MAXB);
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          __stcg(dst + j, make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]));
+        __threadfence();
+        epi_sync();
+        if (et == 0) *s_last = (atomicAdd(&a.counters[tile], 1) == nseg - 1);
+        epi_sync();
+        run = *s_last != 0;
+        if (run) {
+          __threadfence();
+#pragma unroll
+          for (int b = 0; b < MAXB; b++) y[b] = 0.f;
+          for (int sl = 0; sl < nseg; sl++) {
+            const float4* src =
+                reinterpret_cast<const float4*>(a.partial + (((size_t)tile * a.maxseg + sl) * BM + r) * MAXB);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const float4 t4 = __ldcg(src + j);
+              y[4 * j] += t4.x; y[4 * j + 1] += t4.y; y[4 * j + 2] += t4.z; y[4 * j + 3] += t4.w;
+            }
+          }
+          if (et == 0) a.counters[tile] = 0;  // ready for the next launch
         }
       }
-    } else {
-      for (int b = 0; b < a.B; b++) {
-        const int p = a.pos[b];
-        if (p >= 0 && p < a.S)
-          a.vc[(((size_t)b * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[b]);
-      }
-    }
-  } else if constexpr (EPI == EPI_SWIGLU) {
+      if (run) {
+        if (EPI != EPI_RESID && a.ss_in != nullptr) {
+          if (et < MAXB) {
+            float ssum = 0.f;
+            for (int t = 0; t < a.ss_tiles; t++) ssum += a.ss_in[t * MAXB + et];
+            s_scale[et] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
+          }
+          epi_sync();
 #pragma unroll
-    for (int b = 0; b < MAXB; b++) ys[r * YS_LD + b] = y[b];
-    __syncthreads();
-    if (r < 64) {
-      const int f = tile * 64 + r;
-      for (int b = 0; b < a.B; b++) {
-        const float g = y[b], u = ys[(r + 64) * YS_LD + b];
-        const float act = g / (1.0f + expf(-g)) * u;
-        const uint16_t hi = f2bf_bits(act);
-        a.act_out[(size_t)b * a.ld_act + f] = hi;
-        a.act_out[(size_t)(MAXB + b) * a.ld_act + f] = f2bf_bits(act - bf2f(hi));
-      }
-    }
-  } else if constexpr (EPI == EPI_LOGITS) {
-    __shared__ unsigned long long red[4][MAXB];
-    for (int b = 0; b < a.B; b++) {
-      unsigned long long key = 0;
-      if (n < a.V) {
-        a.logits[(size_t)b * a.V + n] = y[b];
-        key = ((unsigned long long)orderable(y[b]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
-      }
+          for (int b = 0; b < MAXB; b++) y[b] *= s_scale[b];
+        }
+        if constexpr (EPI == EPI_RESID) {
+          float xs[MAXB];
+          for (int b = 0; b < a.B; b++) {
+            const float xn = a.x[(size_t)b * a.ldx + n] + y[b];
+            a.x[(size_t)b * a.ldx + n] = xn;
+            xs[b] = xn;
+          }
+          if (a.act_next != nullptr) {
+            const float w = a.w_next[n];
+            for (int b = 0; b < a.B; b++) {
+              const float h = xs[b] * w;
+              const uint16_t hi = f2bf_bits(h);
+              a.act_next[(size_t)b * a.ld_next + n] = hi;
+              a.act_next[(size_t)(MAXB + b) * a.ld_next + n] = f2bf_bits(h - bf2f(hi));
+            }
+            // per-tile sum of squares of the new x, fixed reduction order
+            for (int b = 0; b < a.B; b++) {
+              float sq = xs[b] * xs[b];
+              sq = warp_sum(sq);
+              if (lane == 0) ys[(warp & 3) * YS_LD + b] = sq;
+            }
+            epi_sync();
+            if (et < a.B) {
+              const float t4 = (ys[0 * YS_LD + et] + ys[1 * YS_LD + et]) + (ys[2 * YS_LD + et] + ys[3 * YS_LD + et]);
+              a.ss_out[tile * MAXB + et] = t4;
+            }
+          }
+        } else if constexpr (EPI == EPI_QKV) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
-        key = t > key ? t : key;
+          for (int b = 0; b < MAXB; b++) ys[r * YS_LD + b] = y[b];
+          epi_sync();
+          const int head = tile;  // one 128-row tile = one head
+          const int i = r & 63;
+          const bool lo_half = r < 64;
+          const int partner = r ^ 64;
+          if (head < a.NH + a.NKV) {
+            for (int b = 0; b < a.B; b++) {
+              const int p = a.pos[b];
+              float sn, cs;
+              sincosf((float)p * a.inv[i], &sn, &cs);
+              const float other = ys[partner * YS_LD + b];
+              const float o = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
+              if (head < a.NH) {
+                a.q[(size_t)b * a.ldq + n] = o;
+              } else if (p >= 0 && p < a.S) {
+                a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o);
+              }
+            }
+          } else {
+            for (int b = 0; b < a.B; b++) {
+              const int p = a.pos[b];
+              if (p >= 0 && p < a.S)
+                a.vc[(((size_t)b * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[b]);
+            }
+          }
+        } else if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll
+          for (int b = 0; b < MAXB; b++) ys[r * YS_LD + b] = y[b];
+          epi_sync();
+          if (r < 64) {
+            const int fcol = tile * 64 + r;
+            for (int b = 0; b < a.B; b++) {
+              const float g = y[b], u = ys[(r + 64) * YS_LD + b];
+              const float act = g / (1.0f + expf(-g)) * u;
+              const uint16_t hi = f2bf_bits(act);
+              a.act_out[(size_t)b * a.ld_act + fcol] = hi;
+              a.act_out[(size_t)(MAXB + b) * a.ld_act + fcol] = f2bf_bits(act - bf2f(hi));
+            }
+          }
+        } else if constexpr (EPI == EPI_LOGITS) {
+          for (int b = 0; b < a.B; b++) {
+            unsigned long long key = 0;
+            if (n < a.V) {
+              a.logits[(size_t)b * a.V + n] = y[b];
+              key = ((unsigned long long)orderable(y[b]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
+              key = t > key ? t : key;
+            }
+            if (lane == 0) s_red[(warp & 3) * MAXB + b] = key;
+          }
+          epi_sync();
+          if (et < a.B) {
+            unsigned long long k = s_red[et];
+            for (int w = 1; w < 4; w++) k = s_red[w * MAXB + et] > k ? s_red[w * MAXB + et] : k;
+            atomicMax(&a.best[et], k);
+          }
+        }
+        epi_sync();  // ys / s_scale / s_red are reused by the next segment
       }
-      if (lane == 0) red[warp][b] = key;
-    }
-    __syncthreads();
-    if (r < a.B) {
-      unsigned long long k = red[0][r];
-      for (int w = 1; w < 4; w++) k = red[w][r] > k ? red[w][r] : k;
-      atomicMax(&a.best[r], k);
+      f = fend;
     }
   }
+  tc_fence_before();
+  __syncthreads();
+  if (tr != nullptr && threadIdx.x == 0) tr[4] = globaltimer();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-// ---------------------------------------------------------------- prep
-// act[b] = bf16(h), act[16+b] = bf16(h - bf16(h)) with h = rms(x) * w (or
-// h = x when w == nullptr).  Also clears the argmax keys when best != nullptr.
-__global__ void __launch_bounds__(256) prep_act_kernel(const float* __restrict__ x, int ldx, int H,
-                                                       const float* __restrict__ w, float eps,
-                                                       uint16_t* __restrict__ act, int ld_act,
-                                                       unsigned long long* best) {
-  __shared__ float red[8];
-  const int b = blockIdx.x;
+// -------------------------------------------------------- operand producers
+// act[b] = hi(h), act[16+b] = lo(h) with h = x * w (w == nullptr: h = x), and,
+// when ss != nullptr, ss[t][b] = sum of x^2 over columns [128t, 128t+128).
+// One CTA per stream.  Also clears the argmax keys when best != nullptr.
+__global__ void __launch_bounds__(256) operand_kernel(const float* __restrict__ x, int ldx, int H,
+                                                      const float* __restrict__ w, uint16_t* __restrict__ act,
+                                                      int ld_act, float* __restrict__ ss,
+                                                      unsigned long long* best) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* xr = x + (size_t)b * ldx;
-  float inv = 1.f;
-  if (w != nullptr) {
-    float s = 0.f;
-    for (int k = threadIdx.x; k < H; k += 256) s = fmaf(xr[k], xr[k], s);
-    s = warp_sum(s);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      float t = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
-      t = warp_sum(t);
-      if (threadIdx.x == 0) red[0] = 1.0f / sqrtf(t / (float)H + eps);
-    }
-    __syncthreads();
-    inv = red[0];
-  }
   for (int k = threadIdx.x; k < H; k += 256) {
-    const float h = w != nullptr ? xr[k] * inv * w[k] : xr[k];
+    const float h = w != nullptr ? xr[k] * w[k] : xr[k];
     const uint16_t hi = f2bf_bits(h);
     act[(size_t)b * ld_act + k] = hi;
     act[(size_t)(MAXB + b) * ld_act + k] = f2bf_bits(h - bf2f(hi));
+  }
+  if (ss != nullptr) {
+    // tile t: four 32-column quarters, each a warp sum, added pairwise like the residual epilogue
+    for (int t = warp; t < H / 128; t += 8) {
+      float q[4];
+#pragma unroll
+      for (int qq = 0; qq < 4; qq++) {
+        const float v = xr[t * 128 + qq * 32 + lane];
+        q[qq] = warp_sum(v * v);
+      }
+      if (lane == 0) ss[t * MAXB + b] = (q[0] + q[1]) + (q[2] + q[3]);
+    }
   }
   if (best != nullptr && threadIdx.x == 0) best[b] = 0ull;
 }
 
 __global__ void finalize_argmax_kernel(const unsigned long long* __restrict__ best, int32_t* __restrict__ next,
                                        int B) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int b = threadIdx.x;
   if (b < B) next[b] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best[b] & 0xFFFFFFFFull));
 }
@@ -377,48 +518,79 @@ static int act_map(const void* act, int K, int ld, CUtensorMap* out) {
   return RNGD_OK;
 }
 
-// K splits per weight shape: about two waves of two CTAs per SM, at least
-// 8 K blocks (128 KB of weights) per unit.  Depends on the shape only.
-int decode_nsplit(int N, int K) {
-  const int tiles = (N + BM - 1) / BM, nkb = K / BK;
-  int s = (2 * 2 * kNumSMs + tiles - 1) / tiles;
-  if (s > nkb / 8) s = nkb / 8;
-  return s < 1 ? 1 : s;
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    n = (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) ? v : kNumSMs;
+  }
+  return n;
+}
+
+// CTAs of a GEMM: one per SM, fewer when there are fewer K blocks than SMs
+static int gemm_grid(int N, int K) {
+  const long total = (long)((N + BM - 1) / BM) * (K / BK);
+  const int g = num_sms();
+  return total < g ? (int)total : g;
+}
+
+// pieces a tile can be cut into under the stream-K split (for the partial buffer)
+static int max_segments(int N, int K, int grid) {
+  const long tiles = (N + BM - 1) / BM, nkb = K / BK, total = tiles * nkb;
+  int mx = 1;
+  for (long t = 0; t < tiles; t++) {
+    const int s = owner_of(t * nkb + nkb - 1, total, grid) - owner_of(t * nkb, total, grid) + 1;
+    mx = s > mx ? s : mx;
+  }
+  return mx;
 }
 
 template <int EPI>
-static int launch_wsgemm(const void* W, int L, int layer, int N, int K, const void* act, int ld_act_in,
-                         GemmArgs a, cudaStream_t s) {
+static int launch_skgemm(const void* W, int L, int layer, int N, int K, const void* act, int ld_act_in, GemmArgs a,
+                         cudaStream_t s) {
   RNGD_REQUIRE(K % BK == 0 && K >= BK, "decode GEMM: K=%d must be a multiple of 64", K);
   RNGD_REQUIRE(N % BM == 0 || EPI == EPI_LOGITS, "decode GEMM: N=%d must be a multiple of 128", N);
   CUtensorMap tw, tx;
   RNGD_TRY(weight_map(W, L, N, K, &tw));
   RNGD_TRY(act_map(act, K, ld_act_in, &tx));
+  const int grid = gemm_grid(N, K);
   a.N = N;
   a.K = K;
   a.nkb = K / BK;
-  a.nsplit = EPI == EPI_LOGITS ? 1 : decode_nsplit(N, K);
+  a.tiles = (N + BM - 1) / BM;
+  a.total = a.tiles * a.nkb;
+  a.maxseg = max_segments(N, K, grid);
   a.layer = layer;
-  const int tiles = (N + BM - 1) / BM;
+  RNGD_REQUIRE(a.total >= grid, "decode GEMM: %d K blocks cannot feed %d CTAs", a.total, grid);
+  RNGD_REQUIRE(a.maxseg == 1 || (a.partial && a.counters), "decode GEMM: split tiles need partial/counters");
   static bool attr_set[4] = {false, false, false, false};
   if (!attr_set[EPI]) {
-    RNGD_TRY(check_cuda(cudaFuncSetAttribute(wsgemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    RNGD_TRY(check_cuda(cudaFuncSetAttribute(skgemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kSmemBytes),
-                        "cudaFuncSetAttribute(wsgemm)"));
+                        "cudaFuncSetAttribute(skgemm)"));
     attr_set[EPI] = true;
   }
-  wsgemm_kernel<EPI><<<tiles * a.nsplit, 128, kSmemBytes, s>>>(tw, tx, a);
-  return check_launch("wsgemm_kernel");
+  return launch_pdl(skgemm_kernel<EPI>, dim3(grid), dim3(THREADS), kSmemBytes, s, "skgemm_kernel", tw, tx, a);
 }
 
-int launch_prep(const float* x, int ldx, int B, int H, const float* w, float eps, void* act, int ld_act,
-                unsigned long long* best, cudaStream_t s) {
-  prep_act_kernel<<<B, 256, 0, s>>>(x, ldx, H, w, eps, (uint16_t*)act, ld_act, best);
-  return check_launch("prep_act_kernel");
+int launch_operand(const float* x, int ldx, int B, int H, const float* w, void* act, int ld_act, float* ss,
+                   unsigned long long* best, cudaStream_t s) {
+  return launch_pdl(operand_kernel, dim3(B), dim3(256), 0, s, "operand_kernel", x, ldx, H, w, (uint16_t*)act, ld_act,
+                    ss, best);
 }
 
 int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B,
                            int NH, int NKV, int HD, int S, float* part, void* act, int ld_act, cudaStream_t s);
+int launch_embed(const void* emb, const int32_t* toks, int H, int V, float* x, int B, cudaStream_t s);
+
+// scratch sizes of one GEMM shape under the stream-K split
+static void shape_workspace(int N, int K, size_t* pf, size_t* ct) {
+  const int ms = max_segments(N, K, gemm_grid(N, K));
+  const size_t tiles = (size_t)(N + BM - 1) / BM;
+  *pf = ms > 1 ? tiles * ms * BM * MAXB : 0;
+  *ct = ms > 1 ? tiles : 0;
+}
 
 }  // namespace rngd
 
@@ -427,12 +599,13 @@ using namespace rngd;
 static int check_tc_io(const rngd_model_t* m, const rngd_decode_io_t* io) {
   RNGD_REQUIRE(m && io, "null model or io");
   RNGD_REQUIRE(m->HD == 128 && m->NH == 4 * m->NKV, "decode: kernels are built for HD=128, NH=4*NKV");
-  RNGD_REQUIRE(m->H % 128 == 0 && m->M % 64 == 0 && (2 * m->M) % 128 == 0 && m->H % 64 == 0,
+  RNGD_REQUIRE(m->H % 128 == 0 && (2 * m->M) % 128 == 0 && m->M % 64 == 0,
                "decode: H and 2*M must be multiples of 128");
   RNGD_REQUIRE(io->B >= 1 && io->B <= 16 && io->B <= io->Bcap, "decode: B=%d outside 1..min(16, Bcap)", io->B);
   RNGD_REQUIRE(io->S % 128 == 0 && io->S > 0 && io->S <= 8192, "decode: S=%d must be a multiple of 128", io->S);
-  RNGD_REQUIRE(io->kcache && io->vcache && io->toks && io->pos && io->x && io->q && io->act && io->act2 &&
-                   io->logits && io->attn_part && io->partial && io->counters && io->best && io->next,
+  RNGD_REQUIRE(io->kcache && io->vcache && io->toks && io->pos && io->x && io->q && io->act && io->act_o &&
+                   io->act2 && io->ss && io->logits && io->attn_part && io->partial && io->counters && io->best &&
+                   io->next,
                "decode: null buffer");
   return RNGD_OK;
 }
@@ -441,15 +614,13 @@ extern "C" int rngd_decode_workspace(const rngd_model_t* m, int S, size_t* parti
                                      size_t* act_cols, size_t* act2_cols) {
   RNGD_REQUIRE(m && partial_floats && counters && act_cols && act2_cols, "workspace: null argument");
   const int QN = m->NH * m->HD, KN = m->NKV * m->HD;
-  const int shapes[4][2] = {{QN + 2 * KN, m->H}, {m->H, QN}, {2 * m->M, m->H}, {m->H, m->M}};
+  const int shapes[5][2] = {{QN + 2 * KN, m->H}, {m->H, QN}, {2 * m->M, m->H}, {m->H, m->M}, {m->V, m->H}};
   size_t pf = 0, ct = 0;
   for (auto& sh : shapes) {
-    const int ns = decode_nsplit(sh[0], sh[1]);
-    const size_t t = (size_t)(sh[0] + BM - 1) / BM;
-    if (ns > 1) {
-      pf = pf > (size_t)ns * sh[0] * MAXB ? pf : (size_t)ns * sh[0] * MAXB;
-      ct = ct > t ? ct : t;
-    }
+    size_t p, c;
+    shape_workspace(sh[0], sh[1], &p, &c);
+    pf = pf > p ? pf : p;
+    ct = ct > c ? ct : c;
   }
   *partial_floats = pf;
   *counters = ct;
@@ -459,32 +630,35 @@ extern "C" int rngd_decode_workspace(const rngd_model_t* m, int S, size_t* parti
   return RNGD_OK;
 }
 
+static unsigned long long* g_trace = nullptr;  // set by rngd_tc_gemv_trace (diagnostics)
+
+extern "C" int rngd_tc_gemv_trace(uint64_t* trace) {
+  g_trace = (unsigned long long*)trace;
+  return RNGD_OK;
+}
+
 extern "C" int rngd_tc_gemv(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy,
-                            void* act, float* partial, int32_t* counters, rngd_stream_t stream) {
+                            void* act, float* partial, int32_t* counters, int prep, rngd_stream_t stream) {
   RNGD_REQUIRE(W && X && Y && act, "tc_gemv: null pointer");
   RNGD_REQUIRE(B >= 1 && B <= MAXB, "tc_gemv: B=%d outside 1..16", B);
   RNGD_REQUIRE(N % BM == 0 && K % BK == 0, "tc_gemv: need N %% 128 == 0 and K %% 64 == 0 (N=%d K=%d)", N, K);
-  RNGD_REQUIRE(decode_nsplit(N, K) == 1 || (partial && counters), "tc_gemv: split-K needs partial and counters");
   cudaStream_t s = (cudaStream_t)stream;
-  RNGD_TRY(launch_prep(X, ldx, B, K, nullptr, 0.f, act, K, nullptr, s));
+  if (prep) RNGD_TRY(launch_operand(X, ldx, B, K, nullptr, act, K, nullptr, nullptr, s));
   GemmArgs a = {};
   a.B = B;
   a.partial = partial;
   a.counters = counters;
   a.x = Y;
   a.ldx = ldy;
-  return launch_wsgemm<EPI_RESID>(W, 1, 0, N, K, act, K, a, s);
+  a.trace = g_trace;
+  return launch_skgemm<EPI_RESID>(W, 1, 0, N, K, act, K, a, s);
 }
 
 extern "C" int rngd_tc_gemv_workspace(int N, int K, size_t* partial_floats, size_t* counters) {
   RNGD_REQUIRE(partial_floats && counters, "tc_gemv_workspace: null argument");
-  const int ns = decode_nsplit(N, K);
-  *partial_floats = ns > 1 ? (size_t)ns * N * MAXB : 0;
-  *counters = ns > 1 ? (size_t)(N / BM) : 0;
+  shape_workspace(N, K, partial_floats, counters);
   return RNGD_OK;
 }
-
-extern "C" int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream);
 
 extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, int layer1,
                                   rngd_stream_t stream) {
@@ -505,20 +679,26 @@ extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t*
     a.B = B;
     a.partial = io->partial;
     a.counters = io->counters;
-    // attention block
-    RNGD_TRY(launch_prep(io->x, H, B, H, m->n1 + (size_t)l * H, m->eps, io->act, ld_act, nullptr, s));
+    a.ss_in = io->ss;
+    a.ss_tiles = H / BM;
+    a.eps = m->eps;
+    a.inv_h = 1.0f / (float)H;
+    // attention block: io->act holds x * n1[l] (written by the prologue or the previous layer)
     a.pos = io->pos; a.inv = m->inv_freq; a.q = io->q; a.ldq = QN; a.kc = kc; a.vc = vc;
     a.NH = m->NH; a.NKV = m->NKV; a.S = io->S;
-    RNGD_TRY(launch_wsgemm<EPI_QKV>(m->wqkv, m->L, l, NQKV, H, io->act, ld_act, a, s));
+    RNGD_TRY(launch_skgemm<EPI_QKV>(m->wqkv, m->L, l, NQKV, H, io->act, ld_act, a, s));
     RNGD_TRY(launch_attn_decode_act(io->q, QN, kc, vc, io->pos, B, m->NH, m->NKV, m->HD, io->S, io->attn_part,
-                                    io->act, ld_act, s));
+                                    io->act_o, QN, s));
+    // O projection + residual; writes x * n2[l] for the MLP
     a.x = io->x; a.ldx = H;
-    RNGD_TRY(launch_wsgemm<EPI_RESID>(m->wo, m->L, l, H, QN, io->act, ld_act, a, s));
+    a.w_next = m->n2 + (size_t)l * H; a.act_next = (uint16_t*)io->act; a.ld_next = ld_act; a.ss_out = io->ss;
+    RNGD_TRY(launch_skgemm<EPI_RESID>(m->wo, m->L, l, H, QN, io->act_o, QN, a, s));
     // MLP block
-    RNGD_TRY(launch_prep(io->x, H, B, H, m->n2 + (size_t)l * H, m->eps, io->act, ld_act, nullptr, s));
     a.act_out = (uint16_t*)io->act2; a.ld_act = Mi;
-    RNGD_TRY(launch_wsgemm<EPI_SWIGLU>(m->wgu, m->L, l, 2 * Mi, H, io->act, ld_act, a, s));
-    RNGD_TRY(launch_wsgemm<EPI_RESID>(m->wd, m->L, l, H, Mi, io->act2, Mi, a, s));
+    RNGD_TRY(launch_skgemm<EPI_SWIGLU>(m->wgu, m->L, l, 2 * Mi, H, io->act, ld_act, a, s));
+    // down projection + residual; writes x * n1[l+1] (or the final norm) for what follows
+    a.w_next = l + 1 < m->L ? m->n1 + (size_t)(l + 1) * H : m->norm;
+    RNGD_TRY(launch_skgemm<EPI_RESID>(m->wd, m->L, l, H, Mi, io->act2, Mi, a, s));
   }
   return RNGD_OK;
 }
@@ -528,15 +708,32 @@ extern "C" int rngd_decode_lmhead(const rngd_model_t* m, const rngd_decode_io_t*
   cudaStream_t s = (cudaStream_t)stream;
   const int H = m->H, QN = m->NH * m->HD;
   const int ld_act = H > QN ? H : QN;
-  RNGD_TRY(launch_prep(io->x, H, io->B, H, m->norm, m->eps, io->act, ld_act, (unsigned long long*)io->best, s));
+  // io->act holds x * norm from the last layer's residual epilogue
   GemmArgs a = {};
   a.B = io->B;
+  a.partial = io->partial;
+  a.counters = io->counters;
+  a.ss_in = io->ss;
+  a.ss_tiles = H / BM;
+  a.eps = m->eps;
+  a.inv_h = 1.0f / (float)H;
   a.logits = io->logits;
   a.best = (unsigned long long*)io->best;
   a.V = m->V;
-  RNGD_TRY(launch_wsgemm<EPI_LOGITS>(m->lm, 1, 0, m->V, H, io->act, ld_act, a, s));
-  finalize_argmax_kernel<<<1, 32, 0, s>>>((const unsigned long long*)io->best, io->next, io->B);
-  return check_launch("finalize_argmax_kernel");
+  RNGD_TRY(launch_skgemm<EPI_LOGITS>(m->lm, 1, 0, m->V, H, io->act, ld_act, a, s));
+  return launch_pdl(finalize_argmax_kernel, dim3(1), dim3(32), 0, s, "finalize_argmax_kernel",
+                    (const unsigned long long*)io->best, io->next, io->B);
+}
+
+// x = embed[toks]; act = hi/lo(x * n1[0]); ss = per-tile sums of squares; argmax
+// keys cleared for this step's lm_head (engines/decode_batch.py:432).
+extern "C" int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_stream_t stream) {
+  RNGD_TRY(check_tc_io(m, io));
+  cudaStream_t s = (cudaStream_t)stream;
+  RNGD_TRY(launch_embed(m->embed, io->toks, m->H, m->V, io->x, io->B, s));
+  const int H = m->H, QN = m->NH * m->HD;
+  const int ld_act = H > QN ? H : QN;
+  return launch_operand(io->x, H, io->B, H, m->n1, io->act, ld_act, io->ss, (unsigned long long*)io->best, s);
 }
 
 int rngd::read_status_decode(int* st, int reset) {

@@ -49,9 +49,9 @@ class Model(ctypes.Structure):
 class DecodeIO(ctypes.Structure):
     """rngd_decode_io_t"""
     _fields_ = [("B", _i32), ("Bcap", _i32), ("S", _i32), ("kv_layers", _i32), ("kcache", _vp), ("vcache", _vp),
-                ("toks", _vp), ("pos", _vp), ("x", _vp), ("q", _vp), ("act", _vp), ("act2", _vp),
-                ("logits", _vp), ("attn_part", _vp), ("partial", _vp), ("counters", _vp), ("best", _vp),
-                ("next", _vp)]
+                ("toks", _vp), ("pos", _vp), ("x", _vp), ("q", _vp), ("act", _vp), ("act_o", _vp),
+                ("act2", _vp), ("ss", _vp), ("logits", _vp), ("attn_part", _vp), ("partial", _vp),
+                ("counters", _vp), ("best", _vp), ("next", _vp)]
 
 
 def _sig(name, *args):
@@ -76,8 +76,9 @@ _sig("rngd_decode_advance", _IOP, _vp)
 _szp = ctypes.POINTER(ctypes.c_size_t)
 _sig("rngd_decode_workspace", _MP, ctypes.c_int, _szp, _szp, _szp, _szp)
 _sig("rngd_tc_gemv", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp,
-     _vp, _vp, _vp)
+     _vp, _vp, ctypes.c_int, _vp)
 _sig("rngd_tc_gemv_workspace", ctypes.c_int, ctypes.c_int, _szp, _szp)
+_sig("rngd_tc_gemv_trace", _vp)
 _sig("rngd_device_status", ctypes.POINTER(ctypes.c_int), ctypes.c_int)
 _sig("rngd_gemv_bf16", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
      ctypes.c_int, _vp)

@@ -85,7 +85,9 @@ class BatchDecodeEngine:
         self._q = torch.zeros((MAXB, QN), **f32)
         # hi/lo bf16 GEMM operands: rows of streams >= B must stay zero
         self._act = torch.zeros((2 * MAXB, act_cols), dtype=BF, device=d)
+        self._act_o = torch.zeros((2 * MAXB, QN), dtype=BF, device=d)
         self._act2 = torch.zeros((2 * MAXB, act2_cols), dtype=BF, device=d)
+        self._ss = torch.zeros((H // 128, MAXB), **f32)
         self._logits = torch.zeros((B, self.V), **f32)
         self._part = torch.zeros((B, c.n_heads, S // ATTN_CHUNK, c.head_dim + 2), **f32)
         self._partial = torch.zeros(max(partial_floats, 1), **f32)
@@ -100,16 +102,17 @@ class BatchDecodeEngine:
         self.use_graph = os.environ.get("RNGD_CUDA_GRAPH", "1") != "0"
         self._graphs = {}
         self._copied = torch.cuda.Event()
-        # embed; per layer: prep, QKV gemm, attn partial, attn combine, O gemm, prep, gate/up gemm,
-        # down gemm; lm_head: prep, gemm, argmax finalize; advance
-        self.launches_per_step = 1 + self.nl * 8 + 3 + 1
+        # embed + operand; per layer: QKV gemm, attn partial, attn combine, O gemm, gate/up gemm,
+        # down gemm; lm_head gemm, argmax finalize; advance
+        self.launches_per_step = 2 + self.nl * 6 + 2 + 1
 
     # ------------------------------------------------------------ buffers
     def _io(self, Kg, Vg):
         p = lambda t: t.data_ptr()
         return _lib.DecodeIO(B=self.B, Bcap=self.B, S=self.S, kv_layers=self.NG, kcache=p(Kg), vcache=p(Vg),
                              toks=p(self._toks), pos=p(self._pos), x=p(self._x), q=p(self._q),
-                             act=p(self._act), act2=p(self._act2), logits=p(self._logits),
+                             act=p(self._act), act_o=p(self._act_o), act2=p(self._act2), ss=p(self._ss),
+                             logits=p(self._logits),
                              attn_part=p(self._part), partial=p(self._partial), counters=p(self._counters),
                              best=p(self._best), next=p(self._next))
 

@@ -76,7 +76,7 @@ def test_tc_gemv_matches_fp32(B, N, K):
     for rep in range(2):                     # the second run reuses the self-resetting counters
         Yd = Y0.clone().cuda()
         _lib.call("rngd_tc_gemv", _lib.ptr(Wd), N, K, _lib.ptr(Xd), K, B, _lib.ptr(Yd), N, _lib.ptr(act),
-                  _lib.ptr(part), _lib.ptr(cnt), _lib.stream_handle())
+                  _lib.ptr(part), _lib.ptr(cnt), 1, _lib.stream_handle())
         torch.cuda.synchronize()
         assert _lib.device_status() == 0
         got = Yd.cpu().double()
