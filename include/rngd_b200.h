@@ -149,6 +149,22 @@ int rngd_attn_decode(const float* q, const void* kc, const void* vc, const int32
                      int Bcap, int NH, int NKV, int HD, int S, float* part, float* ao,
                      rngd_stream_t stream);
 
+/* Allocation-free form of rngd_attn_decode, for callers that cannot call
+ * cudaMalloc: code running inside someone else's CUDA-graph capture or memory
+ * pool, or a host whose allocator owns all device memory.  It has no
+ * counterpart in the reference.  The chunk partials live in a scratch array
+ * built into this library (2,129,920 bytes on every GPU that loads it, held
+ * until exit): B * NH * S/128 must be <= 4096 (B=16, NH=32 allows S <= 1024),
+ * larger requests return RNGD_ERR_ARG.  The caller still passes q, the caches,
+ * positions and the output ao.  Nothing in the scratch needs to start at zero
+ * (every record is written before it is read), but every call shares it:
+ * calls that may overlap on the GPU (other streams, other threads) race, so
+ * order them on one stream.  The first call on a device looks up the scratch
+ * address with cudaGetSymbolAddress (which may load the module); make that
+ * first call before any stream capture.  No cudaMalloc/cudaFree is made. */
+int rngd_attn_decode_noalloc(const float* q, const void* kc, const void* vc, const int32_t* pos, int B,
+                             int Bcap, int NH, int NKV, int HD, int S, float* ao, rngd_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,6 +11,8 @@
 //             -> down GEMV (+= residual)
 // HBM-bound: the GEMVs stream 436 MB of weights per layer; activations are a
 // few hundred KB and stay in L1/L2.
+#include <mutex>
+
 #include "tc.cuh"
 
 namespace rngd {
@@ -426,6 +428,33 @@ __global__ void advance_kernel(int32_t* __restrict__ toks, int32_t* __restrict__
   }
 }
 
+// ------------------------------------------------ allocation-free attention
+// Library-owned scratch for rngd_attn_decode_noalloc: room for 4096 chunk
+// partial records of HD + 2 floats (B * NH * S/128 <= 4096, e.g. 16 streams x
+// 32 heads x S <= 1024), 2,129,920 bytes.  Every GPU that loads the library
+// holds it until the process exits.
+constexpr int kNoAllocRecords = 4096;
+static __device__ __align__(256) float g_attn_scratch[kNoAllocRecords * (kHD + 2)];
+
+// Device address of g_attn_scratch, looked up once per device with that device
+// current (in host code the symbol itself is only a host-side stand-in).
+static std::mutex g_scratch_mu;
+static float* g_scratch_ptr[128] = {};
+
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  RNGD_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  RNGD_REQUIRE(dev >= 0 && dev < 128, "attn_decode_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> g(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    RNGD_TRY(check_cuda(cudaGetSymbolAddress(&p, g_attn_scratch), "cudaGetSymbolAddress(attention scratch)"));
+    g_scratch_ptr[dev] = (float*)p;
+  }
+  *out = g_scratch_ptr[dev];
+  return RNGD_OK;
+}
+
 int launch_embed(const void* emb, const int32_t* toks, int H, int V, float* x, int B, cudaStream_t s) {
   return launch_pdl(embed_kernel, dim3(B), dim3(256), 0, s, "embed_kernel", (const uint16_t*)emb, toks, H, V, x);
 }
@@ -450,6 +479,23 @@ extern "C" int rngd_attn_decode(const float* q, const void* kc, const void* vc, 
   RNGD_REQUIRE(B <= Bcap, "attn_decode: B=%d > Bcap=%d", B, Bcap);
   return launch_attn_decode(q, NH * HD, kc, vc, pos, B, NH, NKV, HD, S, part, ao, NH * HD,
                             (cudaStream_t)stream);
+}
+
+extern "C" int rngd_attn_decode_noalloc(const float* q, const void* kc, const void* vc, const int32_t* pos,
+                                        int B, int Bcap, int NH, int NKV, int HD, int S, float* ao,
+                                        rngd_stream_t stream) {
+  RNGD_REQUIRE(B >= 1 && B <= Bcap, "attn_decode_noalloc: B=%d outside 1..Bcap=%d", B, Bcap);
+  RNGD_REQUIRE(HD == kHD && NH == kG * NKV, "attn_decode_noalloc: built for HD=128 and 4 query heads per kv head");
+  RNGD_REQUIRE(S % kChunk == 0 && S > 0, "attn_decode_noalloc: S=%d must be a positive multiple of 128", S);
+  const long records = (long)B * NH * (S / kChunk);
+  RNGD_REQUIRE(records <= kNoAllocRecords,
+               "attn_decode_noalloc: B*NH*S/128 = %ld partial records exceed the built-in scratch of %d "
+               "(e.g. B=16, NH=32 allows S <= 1024); use rngd_attn_decode with caller-owned scratch",
+               records, kNoAllocRecords);
+  float* part = nullptr;
+  RNGD_TRY(noalloc_scratch(&part));
+  return launch_attn(q, NH * HD, kc, vc, pos, B, NH, NKV, HD, S, part, ao, NH * HD, nullptr, 0,
+                     (cudaStream_t)stream);
 }
 
 extern "C" int rngd_decode_advance(const rngd_decode_io_t* io, rngd_stream_t stream) {

@@ -85,6 +85,8 @@ _sig("rngd_gemv_bf16", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctype
 _sig("rngd_rmsnorm_f32", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_float, _vp, _vp)
 _sig("rngd_attn_decode", _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
      ctypes.c_int, ctypes.c_int, _vp, _vp, _vp)
+_sig("rngd_attn_decode_noalloc", _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+     ctypes.c_int, ctypes.c_int, _vp, _vp)
 
 
 def last_error():
