@@ -173,19 +173,35 @@ constexpr int kChunk = 128;
 constexpr int kG = 4;
 constexpr int kHD = 128;
 
+constexpr int kRowBytes = 272;  // smem pitch of a staged K/V row: 256 B + 16 B pad (bank-conflict free)
+constexpr size_t kAttnSmem = 2 * kChunk * kRowBytes + kG * kHD * 4 + kG * kChunk * 4 + kG * 4 * 4 + 128;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+// One CTA = (128-position chunk, kv head, stream) and the G=4 query heads of the kv head.
+// The chunk's K and V rows are staged into shared memory with cp.async first (all loads in
+// flight at once), then scores (one position per thread), softmax statistics and P.V run
+// from shared memory.
 __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restrict__ q, int ldq,
                                                            const uint16_t* __restrict__ kc,
                                                            const uint16_t* __restrict__ vc,
                                                            const int32_t* __restrict__ pos, int NH,
                                                            int NKV, int S, float* __restrict__ part) {
+  extern __shared__ __align__(16) uint8_t attn_smem[];
+  uint8_t* sK = attn_smem;
+  uint8_t* sV = sK + kChunk * kRowBytes;
+  float* qs = (float*)(sV + kChunk * kRowBytes);   // [kG][kHD]
+  float* ps = qs + kG * kHD;                       // [kG][kChunk]
+  float* red = ps + kG * kChunk;                   // [kG][4]
+  float* ored = (float*)sK;                        // [8][kG][kHD], reuses the K rows after the scores
+
   const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
   const int nchunk = gridDim.x;
   const int PS = kHD + 2;  // partial record: o[HD], m, l
-  __shared__ __align__(16) float qs[kG][kHD];
-  __shared__ float ps[kG][kChunk];
-  __shared__ float red[kG][4];
-  __shared__ __align__(16) float ored[8][kG][kHD];   // P.V partials of the 8 position groups
   grid_dep_wait();
   grid_dep_launch();  // every CTA of this grid is running: the next kernel may start its prologue
   const int P = min(pos[b] + 1, S);
@@ -200,70 +216,57 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
     return;
   }
   const int n = min(kChunk, P - s0);
-  const float scale = 0.08838834764831845f;  // 1/sqrt(128) in fp32
-  for (int i = t; i < kG * kHD; i += 128)
-    qs[i / kHD][i % kHD] = q[(size_t)b * ldq + (size_t)(kvh * kG + i / kHD) * kHD + i % kHD];
-  __syncthreads();
   const size_t head_base = ((size_t)b * NKV + kvh) * (size_t)S * kHD;
-  const uint16_t* kbase = kc + head_base + (size_t)s0 * kHD;
-  const uint16_t* vbase = vc + head_base + (size_t)s0 * kHD;
+  const uint8_t* kg = (const uint8_t*)(kc + head_base + (size_t)s0 * kHD);
+  const uint8_t* vg = (const uint8_t*)(vc + head_base + (size_t)s0 * kHD);
+  for (int i = t; i < n * 16; i += 128) {
+    const int j = i >> 4, c16 = (i & 15) * 16;
+    cp_async16(sK + j * kRowBytes + c16, kg + (size_t)j * 256 + c16);
+    cp_async16(sV + j * kRowBytes + c16, vg + (size_t)j * 256 + c16);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const float scale = 0.08838834764831845f;  // 1/sqrt(128) in fp32
+  for (int i = t; i < kG * kHD; i += 128) qs[i] = q[(size_t)b * ldq + (size_t)(kvh * kG) * kHD + i];
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
 
-  // scores: 4 lanes per position (32 dims each), 8 positions per warp pass, 4 passes per warp
-  const int sub = lane >> 2, part4 = lane & 3;
-  float sc[4][kG];
+  // scores: thread t = position s0 + t
+  float sc[kG] = {0.f, 0.f, 0.f, 0.f};
+  if (t < n) {
+    const uint8_t* krow = sK + t * kRowBytes;
+#pragma unroll 4
+    for (int d = 0; d < kHD; d += 8) {
+      float kf[8];
+      unpack8(*reinterpret_cast<const uint4*>(krow + d * 2), kf);
 #pragma unroll
-  for (int it = 0; it < 4; it++) {
-    const int j = warp * 32 + it * 8 + sub;   // position within the chunk
-    float acc[kG] = {0.f, 0.f, 0.f, 0.f};
-    if (j < n) {
-      const uint16_t* krow = kbase + (size_t)j * kHD + part4 * 32;
-#pragma unroll
-      for (int v4 = 0; v4 < 4; v4++) {
-        float kf[8];
-        unpack8(*reinterpret_cast<const uint4*>(krow + v4 * 8), kf);
-#pragma unroll
-        for (int g = 0; g < kG; g++) {
-          const float4 qa = *reinterpret_cast<const float4*>(&qs[g][part4 * 32 + v4 * 8]);
-          const float4 qb = *reinterpret_cast<const float4*>(&qs[g][part4 * 32 + v4 * 8 + 4]);
-          acc[g] = fmaf(qa.x, kf[0], acc[g]); acc[g] = fmaf(qa.y, kf[1], acc[g]);
-          acc[g] = fmaf(qa.z, kf[2], acc[g]); acc[g] = fmaf(qa.w, kf[3], acc[g]);
-          acc[g] = fmaf(qb.x, kf[4], acc[g]); acc[g] = fmaf(qb.y, kf[5], acc[g]);
-          acc[g] = fmaf(qb.z, kf[6], acc[g]); acc[g] = fmaf(qb.w, kf[7], acc[g]);
-        }
+      for (int g = 0; g < kG; g++) {
+        const float4 qa = *reinterpret_cast<const float4*>(&qs[g * kHD + d]);
+        const float4 qb = *reinterpret_cast<const float4*>(&qs[g * kHD + d + 4]);
+        float a = sc[g];
+        a = fmaf(qa.x, kf[0], a); a = fmaf(qa.y, kf[1], a); a = fmaf(qa.z, kf[2], a); a = fmaf(qa.w, kf[3], a);
+        a = fmaf(qb.x, kf[4], a); a = fmaf(qb.y, kf[5], a); a = fmaf(qb.z, kf[6], a); a = fmaf(qb.w, kf[7], a);
+        sc[g] = a;
       }
     }
-#pragma unroll
-    for (int g = 0; g < kG; g++) {
-      float v = acc[g];
-      v += __shfl_xor_sync(0xffffffffu, v, 1);
-      v += __shfl_xor_sync(0xffffffffu, v, 2);
-      sc[it][g] = j < n ? v * scale : -INFINITY;
-    }
   }
-  // softmax statistics of the chunk (per head)
-#pragma unroll
-  for (int g = 0; g < kG; g++) {
-    float m = fmaxf(fmaxf(sc[0][g], sc[1][g]), fmaxf(sc[2][g], sc[3][g]));
-    m = warp_max(m);
-    if (lane == 0) red[g][warp] = m;
-  }
-  __syncthreads();
   float mx[kG];
 #pragma unroll
-  for (int g = 0; g < kG; g++) mx[g] = fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]));
+  for (int g = 0; g < kG; g++) {
+    sc[g] = t < n ? sc[g] * scale : -INFINITY;
+    const float m = warp_max(sc[g]);
+    if (lane == 0) red[g * 4 + warp] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < kG; g++)
+    mx[g] = fmaxf(fmaxf(red[g * 4 + 0], red[g * 4 + 1]), fmaxf(red[g * 4 + 2], red[g * 4 + 3]));
   __syncthreads();
 #pragma unroll
   for (int g = 0; g < kG; g++) {
-    float ssum = 0.f;
-#pragma unroll
-    for (int it = 0; it < 4; it++) {
-      const int j = warp * 32 + it * 8 + sub;
-      const float p = j < n ? expf(sc[it][g] - mx[g]) : 0.f;
-      if (part4 == 0) ps[g][j] = p;
-      ssum += part4 == 0 ? p : 0.f;
-    }
-    ssum = warp_sum(ssum);
-    if (lane == 0) red[g][warp] = ssum;
+    const float p = t < n ? expf(sc[g] - mx[g]) : 0.f;
+    ps[g * kChunk + t] = p;
+    const float ssum = warp_sum(p);
+    if (lane == 0) red[g * 4 + warp] = ssum;
   }
   __syncthreads();
   // P.V: thread t owns dims dg*8..dg*8+7 for positions pg, pg+8, ...; partials reduced over pg
@@ -276,30 +279,31 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
 #pragma unroll 4
   for (int j = pg; j < n; j += 8) {
     float vf[8];
-    unpack8(*reinterpret_cast<const uint4*>(vbase + (size_t)j * kHD + dg * 8), vf);
+    unpack8(*reinterpret_cast<const uint4*>(sV + j * kRowBytes + dg * 16), vf);
 #pragma unroll
     for (int g = 0; g < kG; g++) {
-      const float p = ps[g][j];
+      const float p = ps[g * kChunk + j];
 #pragma unroll
       for (int d = 0; d < 8; d++) o[g][d] = fmaf(p, vf[d], o[g][d]);
     }
   }
 #pragma unroll
   for (int g = 0; g < kG; g++) {
-    *reinterpret_cast<float4*>(&ored[pg][g][dg * 8]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
-    *reinterpret_cast<float4*>(&ored[pg][g][dg * 8 + 4]) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
+    float* dst = ored + (pg * kG + g) * kHD + dg * 8;
+    *reinterpret_cast<float4*>(dst) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
   }
   __syncthreads();
 #pragma unroll
   for (int g = 0; g < kG; g++) {
     float acc = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; k++) acc += ored[k][g][t];
+    for (int k = 0; k < 8; k++) acc += ored[(k * kG + g) * kHD + t];
     float* rec = rec0 + (size_t)g * nchunk * PS;
     rec[t] = acc;
     if (t == 0) {
       rec[kHD] = mx[g];
-      rec[kHD + 1] = (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
+      rec[kHD + 1] = (red[g * 4 + 0] + red[g * 4 + 1]) + (red[g * 4 + 2] + red[g * 4 + 3]);
     }
   }
 }
@@ -342,7 +346,14 @@ static int launch_attn(const float* q, int ldq, const void* kc, const void* vc, 
   RNGD_REQUIRE(S % kChunk == 0 && S > 0 && S <= 8192, "attn_decode: S=%d must be a multiple of 128", S);
   RNGD_REQUIRE(B >= 1, "attn_decode: B=%d", B);
   const int nchunk = S / kChunk;
-  RNGD_TRY(launch_pdl(attn_partial_kernel, dim3(nchunk, NKV, B), dim3(128), 0, s, "attn_partial_kernel", q, ldq,
+  static bool smem_set = false;
+  if (!smem_set) {
+    RNGD_TRY(check_cuda(cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kAttnSmem),
+                        "cudaFuncSetAttribute(attn_partial_kernel)"));
+    smem_set = true;
+  }
+  RNGD_TRY(launch_pdl(attn_partial_kernel, dim3(nchunk, NKV, B), dim3(128), kAttnSmem, s, "attn_partial_kernel", q, ldq,
                       (const uint16_t*)kc, (const uint16_t*)vc, pos, NH, NKV, S, part));
   return launch_pdl(attn_combine_kernel, dim3(NH, B), dim3(kHD), 0, s, "attn_combine_kernel", (const float*)part,
                     nchunk, ao, ldao, NH, act, ld_act);
