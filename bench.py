@@ -237,12 +237,56 @@ def run_micro_attn(args):
           flush=True)
 
 
+def run_micro_prefill(args):
+    """One prefill GEMM shape (C=256 tokens) through rngd_tc_gemm_tokens (pfgemm_kernel)."""
+    import ctypes
+    import torch
+    from rngd_pd import _lib, synth
+    shapes = {"pf_gate_up": (28672, 4096), "pf_qkv": (6144, 4096), "pf_o": (4096, 4096), "pf_down": (4096, 14336)}
+    N, K = shapes[args.micro]
+    C = 256
+    dev = torch.device("cuda", 0)
+    W = torch.empty((2, N, K), dtype=torch.bfloat16, device=dev)
+    synth.fill_gauss(W, 0, 4, 0.02)
+    X = torch.randn(C, K, device=dev)
+    Y = torch.zeros(C, N, device=dev)
+    act = torch.zeros(2 * C, K, dtype=torch.bfloat16, device=dev)
+    pf, ct = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    _lib.call("rngd_tc_gemm_tokens_workspace", N, K, C, ctypes.byref(pf), ctypes.byref(ct))
+    part = torch.zeros(max(pf.value, 1), device=dev)
+    cnt = torch.zeros(max(ct.value, 1), dtype=torch.int32, device=dev)
+    def run(l, prep, st):
+        _lib.call("rngd_tc_gemm_tokens", _lib.ptr(W[l]), N, K, _lib.ptr(X), C, _lib.ptr(Y), _lib.ptr(act),
+                  _lib.ptr(part), _lib.ptr(cnt), prep, _lib.stream_handle(st))
+    side = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(side):
+        run(0, 1, side)
+        for i in range(3):
+            run(i % 2, 0, side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(args.steps):
+                run(i % 2, 0, side)
+        g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(side)
+        g.replay()
+        e1.record(side)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = 2 * 2 * C * N * K                      # hi and lo operand rows
+    print(json.dumps({"micro": args.micro, "N": N, "K": K, "C": C, "ms": ms, "tflops_mma": flops / ms / 1e9,
+                      "weight_gbs": N * K * 2 / ms / 1e6, "status": _lib.device_status()}), flush=True)
+
+
 def run_micro(args):
     """One decode GEMM shape alone (small device footprint; for ncu captures of skgemm_kernel)."""
     import torch
     from rngd_pd import synth
     if args.micro == "attn":
         return run_micro_attn(args)
+    if args.micro.startswith("pf_"):
+        return run_micro_prefill(args)
     shapes = {"gate_up": (28672, 4096), "qkv": (6144, 4096), "o": (4096, 4096), "down": (4096, 14336),
               "lm": (128256, 4096)}
     N, K = shapes[args.micro]
@@ -397,7 +441,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn"],
+    ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn", "pf_gate_up", "pf_qkv", "pf_o",
+                                        "pf_down"],
                     help="time one decode GEMM shape alone (small footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:

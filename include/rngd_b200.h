@@ -120,6 +120,46 @@ int rngd_decode_lmhead(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_s
  * src/rngd_pd/serving/cluster.py:1374-1380). */
 int rngd_decode_advance(const rngd_decode_io_t* io, rngd_stream_t stream);
 
+/* Final norm + lm_head + first-max argmax for `rows` (<= 16) rows of x (fp32,
+ * row stride ldx), e.g. the last prompt position of a prefill
+ * (engines/prefill_full.py:265-270 _next_token).  act: zeroed bf16 [32][H];
+ * ss: fp32 [H/128][16]; logits [rows][V]; best [16]; next [rows]; partial /
+ * counters from rngd_lmhead_workspace (counters zeroed once). */
+int rngd_lmhead_rows(const rngd_model_t* m, const float* x, int ldx, int rows, void* act, float* ss, float* logits,
+                     uint64_t* best, int32_t* next, float* partial, int32_t* counters, rngd_stream_t stream);
+int rngd_lmhead_workspace(const rngd_model_t* m, size_t* partial_floats, size_t* counters);
+
+/* ------------------------------------------------------------- prefill_full
+ * One prompt of P tokens padded to a bucket of C tokens (C a multiple of 128,
+ * engines/prefill_full.py:168-208 buckets), all 32 layers, K/V emitted in the
+ * prefill layout kv [kv_layers][2][NKV][S][HD] (K then V per layer; positions
+ * >= P are left as the caller zeroed them, engines/prefill_full.py:319-335).
+ * Operand buffers hold 2C bf16 rows: hi of token t at row t, lo at row C + t. */
+typedef struct rngd_prefill_io {
+  int32_t C;            /* bucket width (tokens computed) */
+  int32_t P;            /* prompt tokens (rows >= P are padding) */
+  int32_t S;            /* KV width in positions (>= P) */
+  int32_t kv_layers;    /* layers held by kv (the group's block) */
+  void* kv;             /* bf16 [kv_layers][2][NKV][S][HD], first layer = layer0 of the call */
+  const int32_t* toks;  /* device [C] token ids (the prompt, padded) */
+  float* x;             /* fp32 [C][H] residual stream */
+  float* q;             /* fp32 [C][NH*HD] rotated queries */
+  void* act;            /* bf16 [2C][max(H, NH*HD)] operand of x * norm weight */
+  void* act_o;          /* bf16 [2C][NH*HD] attention-output operand */
+  void* act2;           /* bf16 [2C][M] down-projection operand */
+  float* ss;            /* fp32 [H/128][C] per-128-column sums of squares of x */
+  float* partial;       /* fp32 split-K scratch, rngd_prefill_workspace() floats */
+  int32_t* counters;    /* int32 tile counters, rngd_prefill_workspace() entries, zeroed once */
+} rngd_prefill_io_t;
+
+int rngd_prefill_workspace(const rngd_model_t* m, int C, size_t* partial_floats, size_t* counters);
+/* x = embed[toks]; act = hi/lo(x * n1[0]); ss (prompt embedding, engines/prefill_full.py:356-357). */
+int rngd_prefill_embed(const rngd_model_t* m, const rngd_prefill_io_t* io, rngd_stream_t stream);
+/* Layers [layer0, layer1) of the prefill (replaces PrefillModel.forward over one layer
+ * group, kernels/prefill_full.py:56-94, called from engines/prefill_full.py:210-214). */
+int rngd_prefill_layers(const rngd_model_t* m, const rngd_prefill_io_t* io, int layer0, int layer1,
+                        rngd_stream_t stream);
+
 /* ------------------------------------------------------ kernel-level ops
  * Exposed for the parity tests and for hosts that build their own step. */
 /* Y[b][n] (+)= sum_k W[n][k] * X[b][k]; W bf16 [N][K] row-major, X/Y fp32,
@@ -139,6 +179,13 @@ int rngd_tc_gemv_workspace(int N, int K, size_t* partial_floats, size_t* counter
  * %globaltimer stamps [start, operand ready, last TMA issued, last accumulator
  * ready, end] into trace[cta*5 ..] (device memory, >= 5 * SM count entries). */
 int rngd_tc_gemv_trace(uint64_t* trace);
+/* Token-tile form (the prefill GEMM): Y[t][n] += sum_k W[n][k] * X[t][k] for
+ * C tokens (C % 128 == 0) on tcgen05, X fp32 [C][K] split into bf16 hi/lo rows
+ * of act (zeroed bf16 scratch [2C][K]); partial/counters from
+ * rngd_tc_gemm_tokens_workspace(); prep = 0 reuses the operand already in act. */
+int rngd_tc_gemm_tokens(const void* W, int N, int K, const float* X, int C, float* Y, void* act, float* partial,
+                        int32_t* counters, int prep, rngd_stream_t stream);
+int rngd_tc_gemm_tokens_workspace(int N, int K, int C, size_t* partial_floats, size_t* counters);
 /* out[r][k] = x[r][k] / sqrt(mean_k x^2 + eps) * w[k] (kernels/decode_batch.py:130). */
 int rngd_rmsnorm_f32(const float* x, int R, int H, const float* w, float eps, float* out,
                      rngd_stream_t stream);

@@ -105,11 +105,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// CTA owning flattened K-block f under the equal split of `total` over `grid` CTAs.
-__host__ __device__ __forceinline__ int owner_of(long f, long total, int grid) {
-  return (int)(((f + 1) * grid - 1) / total);
-}
-
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constant__ CUtensorMap tmW,
                                                             const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
@@ -388,12 +383,12 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
 }
 
 // -------------------------------------------------------- operand producers
-// act[b] = hi(h), act[16+b] = lo(h) with h = x * w (w == nullptr: h = x), and,
-// when ss != nullptr, ss[t][b] = sum of x^2 over columns [128t, 128t+128).
-// One CTA per stream.  Also clears the argmax keys when best != nullptr.
+// act[b] = hi(h), act[lo_off+b] = lo(h) with h = x * w (w == nullptr: h = x), and,
+// when ss != nullptr, ss[t*ss_ld + b] = sum of x^2 over columns [128t, 128t+128).
+// One CTA per row.  Also clears the argmax keys when best != nullptr.
 __global__ void __launch_bounds__(256) operand_kernel(const float* __restrict__ x, int ldx, int H,
                                                       const float* __restrict__ w, uint16_t* __restrict__ act,
-                                                      int ld_act, float* __restrict__ ss,
+                                                      int ld_act, int lo_off, float* __restrict__ ss, int ss_ld,
                                                       unsigned long long* best) {
   grid_dep_wait();
   grid_dep_launch();
@@ -403,7 +398,7 @@ __global__ void __launch_bounds__(256) operand_kernel(const float* __restrict__ 
     const float h = w != nullptr ? xr[k] * w[k] : xr[k];
     const uint16_t hi = f2bf_bits(h);
     act[(size_t)b * ld_act + k] = hi;
-    act[(size_t)(MAXB + b) * ld_act + k] = f2bf_bits(h - bf2f(hi));
+    act[(size_t)(lo_off + b) * ld_act + k] = f2bf_bits(h - bf2f(hi));
   }
   if (ss != nullptr) {
     // tile t: four 32-column quarters, each a warp sum, added pairwise like the residual epilogue
@@ -414,7 +409,7 @@ __global__ void __launch_bounds__(256) operand_kernel(const float* __restrict__ 
         const float v = xr[t * 128 + qq * 32 + lane];
         q[qq] = warp_sum(v * v);
       }
-      if (lane == 0) ss[t * MAXB + b] = (q[0] + q[1]) + (q[2] + q[3]);
+      if (lane == 0) ss[(size_t)t * ss_ld + b] = (q[0] + q[1]) + (q[2] + q[3]);
     }
   }
   if (best != nullptr && threadIdx.x == 0) best[b] = 0ull;
@@ -486,7 +481,7 @@ struct MapKeyHash {
 static std::mutex g_map_mu;
 static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
-static int weight_map(const void* w, int L, int N, int K, CUtensorMap* out) {
+int get_weight_map(const void* w, int L, int N, int K, CUtensorMap* out) {
   MapKey key{w, (uint64_t)L, (uint64_t)N, (uint64_t)K};
   std::lock_guard<std::mutex> g(g_map_mu);
   auto it = g_maps.find(key);
@@ -502,23 +497,23 @@ static int weight_map(const void* w, int L, int N, int K, CUtensorMap* out) {
   return RNGD_OK;
 }
 
-static int act_map(const void* act, int K, int ld, CUtensorMap* out) {
-  MapKey key{act, (uint64_t)K, (uint64_t)ld, 0xAC7ull};
+int get_operand_map(const void* act, int K, int ld, int rows, int box_rows, CUtensorMap* out) {
+  MapKey key{act, (uint64_t)K, (uint64_t)ld, 0xAC70000ull ^ ((uint64_t)rows << 9) ^ (uint64_t)box_rows};
   std::lock_guard<std::mutex> g(g_map_mu);
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
     *out = it->second;
     return RNGD_OK;
   }
-  const uint64_t dims[2] = {(uint64_t)K, (uint64_t)(2 * MAXB)};
+  const uint64_t dims[2] = {(uint64_t)K, (uint64_t)rows};
   const uint64_t strides[1] = {(uint64_t)ld * 2};
-  const uint32_t box[2] = {BK, BNC};
+  const uint32_t box[2] = {BK, (uint32_t)box_rows};
   RNGD_TRY(encode_tmap_bf16(out, act, 2, dims, strides, box));
   g_maps[key] = *out;
   return RNGD_OK;
 }
 
-static int num_sms() {
+int num_sms() {
   static int n = 0;
   if (n == 0) {
     int dev = 0, v = 0;
@@ -552,8 +547,8 @@ static int launch_skgemm(const void* W, int L, int layer, int N, int K, const vo
   RNGD_REQUIRE(K % BK == 0 && K >= BK, "decode GEMM: K=%d must be a multiple of 64", K);
   RNGD_REQUIRE(N % BM == 0 || EPI == EPI_LOGITS, "decode GEMM: N=%d must be a multiple of 128", N);
   CUtensorMap tw, tx;
-  RNGD_TRY(weight_map(W, L, N, K, &tw));
-  RNGD_TRY(act_map(act, K, ld_act_in, &tx));
+  RNGD_TRY(get_weight_map(W, L, N, K, &tw));
+  RNGD_TRY(get_operand_map(act, K, ld_act_in, 2 * MAXB, BNC, &tx));
   const int grid = gemm_grid(N, K);
   a.N = N;
   a.K = K;
@@ -574,10 +569,15 @@ static int launch_skgemm(const void* W, int L, int layer, int N, int K, const vo
   return launch_pdl(skgemm_kernel<EPI>, dim3(grid), dim3(THREADS), kSmemBytes, s, "skgemm_kernel", tw, tx, a);
 }
 
+int launch_operand_ex(const float* x, int ldx, int rows, int H, const float* w, void* act, int ld_act, int lo_off,
+                      float* ss, int ss_ld, unsigned long long* best, cudaStream_t s) {
+  return launch_pdl(operand_kernel, dim3(rows), dim3(256), 0, s, "operand_kernel", x, ldx, H, w, (uint16_t*)act,
+                    ld_act, lo_off, ss, ss_ld, best);
+}
+
 int launch_operand(const float* x, int ldx, int B, int H, const float* w, void* act, int ld_act, float* ss,
                    unsigned long long* best, cudaStream_t s) {
-  return launch_pdl(operand_kernel, dim3(B), dim3(256), 0, s, "operand_kernel", x, ldx, H, w, (uint16_t*)act, ld_act,
-                    ss, best);
+  return launch_operand_ex(x, ldx, B, H, w, act, ld_act, MAXB, ss, MAXB, best, s);
 }
 
 int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B,
@@ -736,6 +736,38 @@ extern "C" int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* 
   return launch_operand(io->x, H, io->B, H, m->n1, io->act, ld_act, io->ss, (unsigned long long*)io->best, s);
 }
 
+// Final norm + lm_head + first-max argmax for `rows` (<= 16) rows of x, e.g. the
+// last prompt position of a prefill (engines/prefill_full.py:265-270).
+extern "C" int rngd_lmhead_rows(const rngd_model_t* m, const float* x, int ldx, int rows, void* act, float* ss,
+                                float* logits, uint64_t* best, int32_t* next, float* partial, int32_t* counters,
+                                rngd_stream_t stream) {
+  RNGD_REQUIRE(m && x && act && ss && logits && best && next, "lmhead_rows: null argument");
+  RNGD_REQUIRE(rows >= 1 && rows <= MAXB, "lmhead_rows: rows=%d outside 1..16", rows);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int H = m->H;
+  RNGD_TRY(launch_operand_ex(x, ldx, rows, H, m->norm, act, H, MAXB, ss, MAXB, (unsigned long long*)best, s));
+  GemmArgs a = {};
+  a.B = rows;
+  a.partial = partial;
+  a.counters = counters;
+  a.ss_in = ss;
+  a.ss_tiles = H / BM;
+  a.eps = m->eps;
+  a.inv_h = 1.0f / (float)H;
+  a.logits = logits;
+  a.best = (unsigned long long*)best;
+  a.V = m->V;
+  RNGD_TRY(launch_skgemm<EPI_LOGITS>(m->lm, 1, 0, m->V, H, act, H, a, s));
+  return launch_pdl(finalize_argmax_kernel, dim3(1), dim3(32), 0, s, "finalize_argmax_kernel",
+                    (const unsigned long long*)best, next, rows);
+}
+
+extern "C" int rngd_lmhead_workspace(const rngd_model_t* m, size_t* partial_floats, size_t* counters) {
+  RNGD_REQUIRE(m && partial_floats && counters, "lmhead_workspace: null argument");
+  shape_workspace(m->V, m->H, partial_floats, counters);
+  return RNGD_OK;
+}
+
 int rngd::read_status_decode(int* st, int reset) {
   RNGD_TRY(check_cuda(cudaMemcpyFromSymbol(st, g_status_decode, sizeof(int)), "read device status"));
   if (reset) {
@@ -747,8 +779,9 @@ int rngd::read_status_decode(int* st, int reset) {
 
 extern "C" int rngd_device_status(int* status, int reset) {
   RNGD_REQUIRE(status != nullptr, "device_status: null output");
-  int st = 0;
+  int st = 0, sp = 0;
   RNGD_TRY(read_status_decode(&st, reset));
-  *status = st;
+  RNGD_TRY(read_status_prefill(&sp, reset));
+  *status = st != 0 ? st : sp;
   return RNGD_OK;
 }

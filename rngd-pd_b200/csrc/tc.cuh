@@ -198,6 +198,18 @@ static int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
 // Status words of the translation units that hold bounded waits.
 int read_status_decode(int* st, int reset);
+int read_status_prefill(int* st, int reset);
+
+// Shared host helpers (decode_tc.cu): SM count, cached tensor maps for weight
+// blocks [L][N][K] (box 64 x 128) and operand buffers [rows][K] (box 64 x box_rows).
+int num_sms();
+int get_weight_map(const void* w, int L, int N, int K, CUtensorMap* out);
+int get_operand_map(const void* act, int K, int ld, int rows, int box_rows, CUtensorMap* out);
+
+// CTA owning flattened work item f under an equal split of `total` items over `grid` CTAs.
+__host__ __device__ __forceinline__ int owner_of(long f, long total, int grid) {
+  return (int)(((f + 1) * grid - 1) / total);
+}
 
 int encode_tmap_bf16(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, const uint32_t* box);

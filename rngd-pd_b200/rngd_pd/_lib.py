@@ -54,6 +54,13 @@ class DecodeIO(ctypes.Structure):
                 ("counters", _vp), ("best", _vp), ("next", _vp)]
 
 
+class PrefillIO(ctypes.Structure):
+    """rngd_prefill_io_t"""
+    _fields_ = [("C", _i32), ("P", _i32), ("S", _i32), ("kv_layers", _i32), ("kv", _vp), ("toks", _vp),
+                ("x", _vp), ("q", _vp), ("act", _vp), ("act_o", _vp), ("act2", _vp), ("ss", _vp),
+                ("partial", _vp), ("counters", _vp)]
+
+
 def _sig(name, *args):
     f = getattr(lib, name)
     f.argtypes = list(args)
@@ -79,6 +86,15 @@ _sig("rngd_tc_gemv", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.
      _vp, _vp, ctypes.c_int, _vp)
 _sig("rngd_tc_gemv_workspace", ctypes.c_int, ctypes.c_int, _szp, _szp)
 _sig("rngd_tc_gemv_trace", _vp)
+_PIOP = ctypes.POINTER(PrefillIO)
+_sig("rngd_prefill_workspace", _MP, ctypes.c_int, _szp, _szp)
+_sig("rngd_prefill_embed", _MP, _PIOP, _vp)
+_sig("rngd_prefill_layers", _MP, _PIOP, ctypes.c_int, ctypes.c_int, _vp)
+_sig("rngd_lmhead_rows", _MP, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp)
+_sig("rngd_lmhead_workspace", _MP, _szp, _szp)
+_sig("rngd_tc_gemm_tokens", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_int,
+     _vp)
+_sig("rngd_tc_gemm_tokens_workspace", ctypes.c_int, ctypes.c_int, ctypes.c_int, _szp, _szp)
 _sig("rngd_device_status", ctypes.POINTER(ctypes.c_int), ctypes.c_int)
 _sig("rngd_gemv_bf16", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
      ctypes.c_int, _vp)

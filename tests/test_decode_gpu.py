@@ -205,32 +205,17 @@ def test_bad_inputs_raise():
 
 
 # ---------------------------------------------------------------- full size
-@pytest.fixture(scope="module")
-def full():
-    """Llama-3.1-8B-shaped synthetic model on the device and in the C oracle (seed 0)."""
-    from oracle import corc
-    from rngd_pd.engines.decode_batch import BatchDecodeEngine
-    from rngd_pd.engines.model import ModelConfig
-    from rngd_pd.engines.weights import DeviceWeights
-    from rngd_pd.synth import SyntheticState
-    cfg = ModelConfig.llama31_8b()
-    w = DeviceWeights(cfg, SyntheticState(cfg, seed=0), torch.device("cuda", 0))
-    cm = corc.CModel(R.LLAMA8B, seed=0)
-    yield cfg, w, cm
-    cm.close()
-
-
 def _engine_with(cfg, w, B, S):
     from rngd_pd.engines.decode_batch import BatchDecodeEngine
     return BatchDecodeEngine(cfg, w, B=B, S=S, group=8)
 
 
 @pytest.mark.slow
-def test_config1_full_llama_logits_and_64_greedy_steps(full):
+def test_config1_full_llama_logits_and_64_greedy_steps(full_llama):
     """B=4, 256 past tokens of seeded bf16 KV ~N(0,1) each, token ids U[0,V)
     (seed 2); logits within 2e-2 max-abs, then 64 greedy steps identical to the CPU fp32 oracle."""
     from rngd_pd import synth
-    cfg, w, cm = full
+    cfg, w, cm = full_llama
     B, S, past = 4, 512, 256
     eng = _engine_with(cfg, w, B, S)
     Ks, Vs = zip(*[synth.request_kv(cfg, S, 100 + b, past) for b in range(B)])
