@@ -127,6 +127,7 @@ def run_reference(args):
         "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": S, "parallelism": "cpu"},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "handoff": {"cpu_baseline": handoff_cpu_baseline()},
     }), flush=True)
 
 
@@ -279,12 +280,215 @@ def run_micro_prefill(args):
                       "weight_gbs": N * K * 2 / ms / 1e6, "status": _lib.device_status()}), flush=True)
 
 
+HANDOFF_BATCHES = (1, 4, 16)
+PEER_COPY_GBS = 770.0      # measured peer copy per direction on this pool's B200s (profiling recipe)
+
+
+def handoff_bytes(cfg):
+    """Config 3's unit: one 512-token request, K and V of every layer and head, bf16."""
+    return cfg.n_layers * 2 * cfg.n_kv * S * cfg.head_dim * 2
+
+
+def handoff_cpu_baseline():
+    """The reference's host-staged handoff of one 512-token request on the host (the connector's
+    bf16 wire: ser -> /dev/shm file -> deser, per layer k and v), restated in
+    rngd_pd.connector.transport; GB/s of payload."""
+    import numpy as np
+    from rngd_pd.connector import transport as tr
+    from rngd_pd.engines.model import ModelConfig
+    cfg = ModelConfig.llama31_8b()
+    rng = np.random.default_rng(5)
+    shape = (cfg.n_kv, S, cfg.head_dim)
+    k = (rng.standard_normal(shape, dtype=np.float32).view(np.uint32) >> 16 << 16).view(np.float32)
+    root = tempfile.mkdtemp(dir="/dev/shm" if os.access("/dev/shm", os.W_OK) else None)
+    t = tr.ShmTransport(root)
+    t0 = time.perf_counter()
+    for l in range(cfg.n_layers):
+        for kv in ("k", "v"):
+            key = f"req/layer.{l}/{kv}"
+            t.push(key, tr.ser(k, wire="bf16"))
+            out = tr.deser(t.pull(key, timeout=5))
+            os.unlink(t._path(key))
+    dt = time.perf_counter() - t0
+    os.rmdir(root)
+    assert out.shape == shape
+    return {"value": handoff_bytes(cfg) / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": "1 request of 512 tokens (64 layer tensors): ser bf16 -> /dev/shm -> deser"}
+
+
+def run_micro_handoff(args):
+    import torch
+    dsts = [0] + ([1] if torch.cuda.device_count() > 1 else [])
+    out = handoff_one_process(dsts, args.steps, args.warmup)
+    print(json.dumps({"micro": "handoff", "unit": "GB/s", "results": out}), flush=True)
+
+
+def handoff_one_process(dsts, reps, warmup):
+    """Config 3 in one process: 1/4/16 requests of 512 tokens pushed by the fused handoff kernel
+    from GPU 0 into decode lanes on each GPU of `dsts` (GPU 0: HBM -> HBM; another GPU: over
+    NVLink with peer access); byte-exact check of every lane; for a peer, a copy-engine peer
+    copy of the same bytes as comparator."""
+    import torch
+    from rngd_pd import synth
+    from rngd_pd.engines.model import ModelConfig
+    from rngd_pd.nvlink import NvlinkTransport
+    cfg = ModelConfig.llama31_8b()
+    L, NKV, HD = cfg.n_layers, cfg.n_kv, cfg.head_dim
+    per_req = handoff_bytes(cfg)
+    src = torch.device("cuda", 0)
+    torch.cuda.set_device(src)
+    kvs = [synth.handoff_kv(cfg, S, 1000 + i, device=src) for i in range(B)]
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    out = []
+    for dst in dsts:
+        ddev = torch.device("cuda", dst)
+        rx = NvlinkTransport(dst)
+        K = torch.zeros((L, B, NKV, S, HD), dtype=torch.bfloat16, device=ddev)
+        V = torch.zeros_like(K)
+        rx.bind_cache(K, V)
+        tx = rx if dst == 0 else NvlinkTransport(0)
+        key = tx.set_remote_handshake(rx.handshake_metadata()) if tx is not rx else None
+        s = torch.cuda.Stream(device=src)
+        for n in HANDOFF_BATCHES:
+            times, used = [], []
+            for rep in range(warmup + reps):
+                ids = [f"r{n}.{rep}.{b}" for b in range(n)]
+                used = [(rep * n + b) % B for b in range(n)]      # rotate sources: > L2 across reps
+                for b, r in enumerate(ids):
+                    tk = rx.reserve(r, b, sender_device=0)
+                    if key is not None:
+                        tx.add_lease(key, tk)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                for b, r in enumerate(ids):
+                    tx.push_device(r, kvs[used[b]], stream=s)
+                e1.record(s)
+                for r in ids:
+                    rx.wait(r, timeout=10)
+                e1.synchronize()
+                if rep >= warmup:
+                    times.append(e0.elapsed_time(e1))
+                for r in ids:
+                    rx.release(r)
+            exact = all(torch.equal(K[:, b].view(torch.int16), kvs[used[b]][:, 0].to(ddev).view(torch.int16)) and
+                        torch.equal(V[:, b].view(torch.int16), kvs[used[b]][:, 1].to(ddev).view(torch.int16))
+                        for b in range(n))
+            ms = statistics.median(times)
+            gbs = n * per_req / ms / 1e6
+            row = {"dst": f"cuda:{dst}", "requests": n, "ms": ms, "payload_bytes": n * per_req, "gbs": gbs,
+                   "byte_exact": exact}
+            if dst == 0:
+                row.update(bound="hbm", frac=2 * gbs / hbm, peak=hbm)
+            else:
+                flat = torch.empty(n * per_req // 2, dtype=torch.bfloat16, device=ddev)
+                ce = []
+                for rep in range(3 + reps):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    with torch.cuda.stream(s):
+                        e0.record(s)
+                        for b in range(n):
+                            flat[b * (per_req // 2):(b + 1) * (per_req // 2)].copy_(
+                                kvs[(rep * n + b) % B].view(-1), non_blocking=True)
+                        e1.record(s)
+                    e1.synchronize()
+                    if rep >= 3:
+                        ce.append(e0.elapsed_time(e1))
+                del flat
+                row.update(bound="nvlink", frac=gbs / PEER_COPY_GBS, peak=PEER_COPY_GBS,
+                           copy_engine_gbs=n * per_req / statistics.median(ce) / 1e6)
+            out.append(row)
+        if tx is not rx:
+            tx.close()
+        rx.close()
+        del K, V
+    return out
+
+
+def handoff_pairs(rank, world, dev, reps, warmup):
+    """Config 3 across processes: GPU 2i prefills (seeded caches) and pushes into GPU 2i+1's
+    decode cache, mapped through CUDA IPC; 1/4/16 requests per batch.  Returns, on every rank,
+    {requests: max-over-senders ms} and whether every receiver's lanes were byte-exact."""
+    import torch
+    import torch.distributed as dist
+    from rngd_pd import synth
+    from rngd_pd.engines.model import ModelConfig
+    from rngd_pd.nvlink import NvlinkTransport, ipc_empty
+    cfg = ModelConfig.llama31_8b()
+    L, NKV, HD = cfg.n_layers, cfg.n_kv, cfg.head_dim
+    sender = rank % 2 == 0
+    partner = rank + 1 if sender else rank - 1
+    t = NvlinkTransport(dev.index)
+    kvs = K = V = None
+    if sender:
+        kvs = [synth.handoff_kv(cfg, S, 1000 + i, device=dev) for i in range(B)]
+    else:
+        K = ipc_empty((L, B, NKV, S, HD), torch.bfloat16, dev)
+        V = ipc_empty((L, B, NKV, S, HD), torch.bfloat16, dev)
+        t.bind_cache(K, V)
+    metas = [None] * world
+    dist.all_gather_object(metas, None if sender else t.handshake_metadata())
+    key = t.set_remote_handshake(metas[partner]) if sender else None
+    s = torch.cuda.Stream(device=dev)
+    out, exact = {}, True
+    for n in HANDOFF_BATCHES:
+        times = []
+        for rep in range(warmup + reps):
+            used = [(rep * n + b) % B for b in range(n)]
+            tickets = None
+            if not sender:
+                tickets = [t.reserve(f"r{n}.{rep}.{b}", b, sender_device=partner) for b in range(n)]
+            allt = [None] * world
+            dist.all_gather_object(allt, tickets)
+            if sender:
+                for tk in allt[partner]:
+                    t.add_lease(key, tk)
+            dist.barrier()
+            if sender:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                for b, tk in enumerate(allt[partner]):
+                    t.push_device(tk["req"], kvs[used[b]], stream=s)
+                e1.record(s)
+                e1.synchronize()
+                if rep >= warmup:
+                    times.append(e0.elapsed_time(e1))
+            else:
+                for tk in tickets:
+                    t.wait(tk["req"], timeout=20)
+            dist.barrier()
+            if not sender:
+                if rep == warmup + reps - 1:
+                    for b in range(n):
+                        ref = synth.handoff_kv(cfg, S, 1000 + used[b], device=dev)
+                        exact &= bool(torch.equal(K[:, b].view(torch.int16), ref[:, 0].view(torch.int16)) and
+                                      torch.equal(V[:, b].view(torch.int16), ref[:, 1].view(torch.int16)))
+                        del ref
+                for tk in tickets:
+                    t.release(tk["req"])
+        ms = torch.tensor([statistics.median(times) if times else 0.0], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        out[n] = float(ms.item())
+    ok = torch.tensor([1 if exact else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    t.close()                      # senders unmap before receivers free
+    dist.barrier()
+    del K, V, kvs
+    return out, bool(ok.item())
+
+
 def run_micro(args):
     """One decode GEMM shape alone (small device footprint; for ncu captures of skgemm_kernel)."""
     import torch
     from rngd_pd import synth
     if args.micro == "attn":
         return run_micro_attn(args)
+    if args.micro == "handoff":
+        return run_micro_handoff(args)
     if args.micro.startswith("pf_"):
         return run_micro_prefill(args)
     shapes = {"gate_up": (28672, 4096), "qkv": (6144, 4096), "o": (4096, 4096), "down": (4096, 14336),
@@ -387,6 +591,25 @@ def run_ours(args):
     e2e_s = float(t.item())
 
     roof = gemm_roofline(eng) if rank == 0 else None
+
+    # ------------------------------------------------- KV handoff (config 3)
+    from rngd_pd.engines.model import ModelConfig as _MC
+    per_req = handoff_bytes(_MC.llama31_8b())
+    hreps = 10
+    if world >= 2 and world % 2 == 0:
+        hms, hexact = handoff_pairs(rank, world, dev, hreps, 3)
+        pairs = world // 2
+        handoff = {"unit": "GB/s", "pairs": pairs, "per_request_bytes": per_req, "byte_exact": hexact,
+                   "path": "GPU 2i -> GPU 2i+1, separate processes, CUDA IPC + NVLink P2P stores",
+                   "results": [{"requests": n, "ms": ms, "gbs": pairs * n * per_req / ms / 1e6,
+                                "frac": n * per_req / ms / 1e6 / PEER_COPY_GBS, "peak": PEER_COPY_GBS,
+                                "bound": "nvlink"} for n, ms in hms.items()]}
+    elif rank == 0:
+        rows = handoff_one_process([local], hreps, 3)
+        handoff = {"unit": "GB/s", "pairs": 0, "per_request_bytes": per_req,
+                   "byte_exact": all(r["byte_exact"] for r in rows),
+                   "path": "one GPU: prefill-layout cache -> decode lanes on the same GPU (HBM read + write)",
+                   "results": rows}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -408,6 +631,7 @@ def run_ours(args):
         pass
     cpu = None
     if not args.no_cpu_baseline:
+        handoff["cpu_baseline"] = handoff_cpu_baseline()
         times, cores = cpu_reference_steps(1, 0)
         cpu = {"value": B / times[0], "unit": "tok/s", "cores": cores, "kind": "port",
                "sample": "1 full decode step (32 layers + lm_head, B=16, S=512) of the C restatement"}
@@ -430,6 +654,7 @@ def run_ours(args):
         "e2e": {"value": world * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 2 * B * 4,
                 "d2h_bytes_per_step": B * 4},
         "gpu_launches": eng.launches_per_step * K,
+        "handoff": handoff,
     }
     print(json.dumps(line), flush=True)
 
@@ -442,7 +667,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn", "pf_gate_up", "pf_qkv", "pf_o",
-                                        "pf_down"],
+                                        "pf_down", "handoff"],
                     help="time one decode GEMM shape alone (small footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:

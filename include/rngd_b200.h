@@ -160,6 +160,41 @@ int rngd_prefill_embed(const rngd_model_t* m, const rngd_prefill_io_t* io, rngd_
 int rngd_prefill_layers(const rngd_model_t* m, const rngd_prefill_io_t* io, int layer0, int layer1,
                         rngd_stream_t stream);
 
+/* ------------------------------------------------------ KV handoff (NVLink)
+ * Replaces the host-staged KV transports of the connector
+ * (connector/rngd_kv.py:122-166 save_kv_layer / wait_for_layer_load over
+ * connector/transport.py:80-101 ShmTransport) with peer-to-peer stores.
+ * Buffers shared across processes are cudaMalloc allocations exported with
+ * CUDA IPC (the handshake hooks connector/transport.py:55-60 carry the handles). */
+/* cudaMalloc `bytes` (zeroed) and its IPC handle (rngd_ipc_handle_size() bytes). */
+int rngd_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int rngd_ipc_free(void* ptr);
+/* Map a peer process's buffer (cudaIpcOpenMemHandle, lazy peer access). */
+int rngd_ipc_open(const void* handle, void** ptr);
+int rngd_ipc_close(void* ptr);
+int rngd_ipc_handle_size(void);
+/* Enable direct access from `device` to `peer` (one process driving both GPUs). */
+int rngd_peer_enable(int device, int peer);
+/* Pinned host memory mapped into the device address space (status words). */
+int rngd_host_alloc_mapped(size_t bytes, void** host, void** dev);
+int rngd_host_free(void* host);
+/* Move positions [0, tokens) of layers [layer0, layer1) of one request's cache
+ * into lane `lane` of dst_k / dst_v (decode layout [L][Bcap][NKV][S][HD] bf16,
+ * local or peer memory), then publish flags[l] = seq (int64, system-scope
+ * release) for each moved layer.  Source: src_k / src_v point at layer0's K and
+ * V blocks ([NKV][S][HD] bf16 each, local) and successive layers are
+ * src_layer_stride elements apart (2*NKV*S*HD for the prefill layout
+ * [L][2][NKV][S][HD]).  done: a zeroed uint32 on the sending device, one per
+ * stream of handoffs. */
+int rngd_kv_handoff(const void* src_k, const void* src_v, size_t src_layer_stride, void* dst_k, void* dst_v, int L,
+                    int NKV, int S, int HD, int tokens, int lane, int Bcap, int layer0, int layer1, uint32_t* done,
+                    int64_t* flags, int64_t seq, rngd_stream_t stream);
+/* Bounded device wait until flags[l] >= seq for l in [layer0, layer1): writes 0,
+ * or RNGD_ERR_TIMEOUT's wait code 4 after timeout_ns (<= 10 s), to *status
+ * (e.g. host-mapped); later work on `stream` is ordered after the arrival. */
+int rngd_kv_wait(const int64_t* flags, int layer0, int layer1, int64_t seq, int64_t timeout_ns, int32_t* status,
+                 rngd_stream_t stream);
+
 /* ------------------------------------------------------ kernel-level ops
  * Exposed for the parity tests and for hosts that build their own step. */
 /* Y[b][n] (+)= sum_k W[n][k] * X[b][k]; W bf16 [N][K] row-major, X/Y fp32,

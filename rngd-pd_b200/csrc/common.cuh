@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <atomic>
 #include <stdio.h>
 
 #include "../../include/rngd_b200.h"
@@ -36,6 +38,20 @@ inline int check_launch(const char* what) { return check_cuda(cudaGetLastError()
     int _st = (expr);           \
     if (_st != RNGD_OK) return _st; \
   } while (0)
+
+// Raise a kernel's dynamic shared-memory limit on the current device once.  The
+// attribute belongs to (kernel, device), so `mask` keeps one bit per device ordinal;
+// a process driving several GPUs sets it on each before its first launch there.
+inline int set_smem_limit_once(const void* func, int bytes, std::atomic<unsigned long long>* mask,
+                               const char* what) {
+  int dev = 0;
+  RNGD_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (mask->load(std::memory_order_acquire) & bit) return RNGD_OK;
+  RNGD_TRY(check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what));
+  mask->fetch_or(bit, std::memory_order_acq_rel);
+  return RNGD_OK;
+}
 
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }

@@ -346,13 +346,9 @@ static int launch_attn(const float* q, int ldq, const void* kc, const void* vc, 
   RNGD_REQUIRE(S % kChunk == 0 && S > 0 && S <= 8192, "attn_decode: S=%d must be a multiple of 128", S);
   RNGD_REQUIRE(B >= 1, "attn_decode: B=%d", B);
   const int nchunk = S / kChunk;
-  static bool smem_set = false;
-  if (!smem_set) {
-    RNGD_TRY(check_cuda(cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)kAttnSmem),
-                        "cudaFuncSetAttribute(attn_partial_kernel)"));
-    smem_set = true;
-  }
+  static std::atomic<unsigned long long> smem_set{0};
+  RNGD_TRY(set_smem_limit_once((const void*)attn_partial_kernel, (int)kAttnSmem, &smem_set,
+                               "cudaFuncSetAttribute(attn_partial_kernel)"));
   RNGD_TRY(launch_pdl(attn_partial_kernel, dim3(nchunk, NKV, B), dim3(128), kAttnSmem, s, "attn_partial_kernel", q, ldq,
                       (const uint16_t*)kc, (const uint16_t*)vc, pos, NH, NKV, S, part));
   return launch_pdl(attn_combine_kernel, dim3(NH, B), dim3(kHD), 0, s, "attn_combine_kernel", (const float*)part,

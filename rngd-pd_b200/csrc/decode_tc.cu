@@ -559,13 +559,9 @@ static int launch_skgemm(const void* W, int L, int layer, int N, int K, const vo
   a.layer = layer;
   RNGD_REQUIRE(a.total >= grid, "decode GEMM: %d K blocks cannot feed %d CTAs", a.total, grid);
   RNGD_REQUIRE(a.maxseg == 1 || (a.partial && a.counters), "decode GEMM: split tiles need partial/counters");
-  static bool attr_set[4] = {false, false, false, false};
-  if (!attr_set[EPI]) {
-    RNGD_TRY(check_cuda(cudaFuncSetAttribute(skgemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)kSmemBytes),
-                        "cudaFuncSetAttribute(skgemm)"));
-    attr_set[EPI] = true;
-  }
+  static std::atomic<unsigned long long> attr_set{0};  // one per EPI instantiation
+  RNGD_TRY(set_smem_limit_once((const void*)skgemm_kernel<EPI>, (int)kSmemBytes, &attr_set,
+                               "cudaFuncSetAttribute(skgemm)"));
   return launch_pdl(skgemm_kernel<EPI>, dim3(grid), dim3(THREADS), kSmemBytes, s, "skgemm_kernel", tw, tx, a);
 }
 

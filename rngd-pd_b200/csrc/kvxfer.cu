@@ -1,0 +1,178 @@
+// KV handoff prefill GPU -> decode GPU over NVLink (peer-to-peer stores).
+//
+// Replaces the reference's host-staged handoff: download, bf16 wire encoding,
+// /dev/shm file, decode, upload (src/rngd_pd/connector/rngd_kv.py:122-166,
+// src/rngd_pd/connector/transport.py:29-101, src/rngd_pd/serving/cluster.py:438-467).
+// A request's cache travels in the prefill layout [L][2][NKV][S][HD] (K then V per
+// layer); the decode cache keeps K and V as [L][Bcap][NKV][S][HD].  Moving
+// layers [l0, l1) of one request's first `tokens` positions into decode lane `lane`
+// is therefore a set of contiguous tokens*HD-element runs, one per (layer, K|V, head):
+// one fused kernel (a CTA per 32 KB chunk of a run) reads them from local HBM
+// (16-byte loads) and stores them straight into the destination, which may be a
+// peer GPU's memory mapped by CUDA IPC or peer access, so pack, transfer and unpack
+// are one pass.
+//
+// Completion fence: every CTA issues fence.sc.sys after its stores and bumps a
+// sender-side counter; the CTA that brings the counter to the grid size issues
+// another fence.sc.sys and publishes flags[l] = seq for each moved layer with a
+// system-scope release store (the "threadfence reduction" pattern at system
+// scope), so a reader that observes the flag with acquire semantics sees all the
+// layer's bytes.  The reader's wait is a bounded device loop that reports a
+// status; it never traps or spins forever.
+#include "tc.cuh"
+
+namespace rngd {
+
+constexpr int kXferThreads = 256;
+constexpr int kXferVec = 8;                                    // 16-byte vectors per thread per chunk
+constexpr unsigned kXferChunk = kXferThreads * kXferVec;       // 2048 vectors = 32 KB
+
+// One CTA per chunk of one run.  A run is (layer, K|V, head): the first `tokens` positions of
+// one head, run_vec contiguous 16-byte vectors in both layouts (heads sit head_vec vectors
+// apart).  The chunk -> (run, part) split is one division per CTA, so the per-vector work is
+// an add, a load and a store; every thread keeps kXferVec independent loads in flight.
+__global__ void __launch_bounds__(kXferThreads) kv_handoff_kernel(
+    const uint4* __restrict__ src_k, const uint4* __restrict__ src_v, long src_stride_vec, uint4* __restrict__ dst_k,
+    uint4* __restrict__ dst_v, unsigned run_vec, unsigned head_vec, unsigned chunks_per_run, int NKV, int lane,
+    int Bcap, int layer0, unsigned int* __restrict__ done, int layer1, long long* __restrict__ flags, long long seq) {
+  grid_dep_wait();
+  const unsigned run = blockIdx.x / chunks_per_run, part = blockIdx.x - run * chunks_per_run;
+  const unsigned h = run % (unsigned)NKV, lkv = run / (unsigned)NKV, lr = lkv >> 1;
+  const bool isv = lkv & 1u;
+  const uint4* s = (isv ? src_v : src_k) + (long)lr * src_stride_vec + (long)h * head_vec;
+  uint4* d = (isv ? dst_v : dst_k) + (((long)(layer0 + (int)lr) * Bcap + lane) * NKV + h) * (long)head_vec;
+  const unsigned o0 = part * kXferChunk + threadIdx.x;
+  uint4 v[kXferVec];
+#pragma unroll
+  for (int j = 0; j < kXferVec; j++) {
+    const unsigned o = o0 + j * kXferThreads;
+    if (o < run_vec) v[j] = ldg_nc_v4(s + o);
+  }
+#pragma unroll
+  for (int j = 0; j < kXferVec; j++) {
+    const unsigned o = o0 + j * kXferThreads;
+    if (o < run_vec) d[o] = v[j];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(done, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int l = layer0; l < layer1; l++)
+        asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(flags + l), "l"(seq) : "memory");
+      *done = 0u;  // ready for the next handoff on this stream
+    }
+  }
+}
+
+// Bounded wait for flags[l] >= seq for l in [layer0, layer1): status 0 when all
+// arrived, ST_FLAG_WAIT after timeout_ns.  The status goes to a word the host
+// can read without synchronising (host-mapped) and is also returned in *dev_status.
+__global__ void kv_wait_kernel(const long long* __restrict__ flags, int layer0, int layer1, long long seq,
+                               long long timeout_ns, int* status) {
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = globaltimer();
+  int st = 0;
+  for (int l = layer0; l < layer1 && st == 0; l++) {
+    for (;;) {
+      long long v;
+      asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(flags + l) : "memory");
+      if (v >= seq) break;
+      if ((long long)(globaltimer() - t0) > timeout_ns) {
+        st = ST_FLAG_WAIT;
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  asm volatile("st.volatile.global.b32 [%0], %1;" ::"l"(status), "r"(st) : "memory");
+  __threadfence_system();
+}
+
+}  // namespace rngd
+
+using namespace rngd;
+
+extern "C" int rngd_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  RNGD_REQUIRE(ptr && handle && bytes > 0, "ipc_alloc: bad arguments");
+  void* p = nullptr;
+  RNGD_TRY(check_cuda(cudaMalloc(&p, bytes), "cudaMalloc (IPC-exportable buffer)"));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle((cudaIpcMemHandle_t*)handle, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return check_cuda(e, "cudaIpcGetMemHandle");
+  }
+  *ptr = p;
+  return RNGD_OK;
+}
+
+extern "C" int rngd_ipc_free(void* ptr) { return check_cuda(cudaFree(ptr), "cudaFree (IPC buffer)"); }
+
+extern "C" int rngd_ipc_open(const void* handle, void** ptr) {
+  RNGD_REQUIRE(handle && ptr, "ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+extern "C" int rngd_ipc_close(void* ptr) { return check_cuda(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle"); }
+
+extern "C" int rngd_ipc_handle_size(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int rngd_peer_enable(int device, int peer) {
+  int can = 0;
+  RNGD_TRY(check_cuda(cudaDeviceCanAccessPeer(&can, device, peer), "cudaDeviceCanAccessPeer"));
+  RNGD_REQUIRE(can, "device %d cannot access device %d directly", device, peer);
+  int cur = 0;
+  RNGD_TRY(check_cuda(cudaGetDevice(&cur), "cudaGetDevice"));
+  RNGD_TRY(check_cuda(cudaSetDevice(device), "cudaSetDevice"));
+  cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    e = cudaSuccess;
+  }
+  cudaSetDevice(cur);
+  return check_cuda(e, "cudaDeviceEnablePeerAccess");
+}
+
+extern "C" int rngd_host_alloc_mapped(size_t bytes, void** host, void** dev) {
+  RNGD_REQUIRE(host && dev && bytes > 0, "host_alloc_mapped: bad arguments");
+  RNGD_TRY(check_cuda(cudaHostAlloc(host, bytes, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc"));
+  memset(*host, 0, bytes);
+  return check_cuda(cudaHostGetDevicePointer(dev, *host, 0), "cudaHostGetDevicePointer");
+}
+
+extern "C" int rngd_host_free(void* host) { return check_cuda(cudaFreeHost(host), "cudaFreeHost"); }
+
+extern "C" int rngd_kv_handoff(const void* src_k, const void* src_v, size_t src_layer_stride, void* dst_k,
+                               void* dst_v, int L, int NKV, int S, int HD, int tokens, int lane, int Bcap, int layer0,
+                               int layer1, uint32_t* done, int64_t* flags, int64_t seq, rngd_stream_t stream) {
+  RNGD_REQUIRE(src_k && src_v && dst_k && dst_v && done && flags, "kv_handoff: null pointer");
+  RNGD_REQUIRE(0 <= lane && lane < Bcap, "kv_handoff: lane %d outside 0..%d", lane, Bcap - 1);
+  RNGD_REQUIRE(0 <= layer0 && layer0 < layer1 && layer1 <= L, "kv_handoff: layers [%d, %d) outside [0, %d)",
+               layer0, layer1, L);
+  RNGD_REQUIRE(NKV > 0 && HD > 0 && 0 < tokens && tokens <= S, "kv_handoff: tokens %d outside 1..S=%d", tokens, S);
+  RNGD_REQUIRE(((uintptr_t)src_k | (uintptr_t)src_v | (uintptr_t)dst_k | (uintptr_t)dst_v) % 16 == 0 &&
+                   src_layer_stride % 8 == 0 && (HD * 2) % 16 == 0,
+               "kv_handoff: buffers must be 16-byte aligned and HD*2 a multiple of 16");
+  const long run_vec = (long)tokens * HD * 2 / 16, head_vec = (long)S * HD * 2 / 16;
+  const long cpr = (run_vec + kXferChunk - 1) / kXferChunk;
+  const long grid = cpr * 2 * NKV * (layer1 - layer0);
+  RNGD_REQUIRE(head_vec < (1l << 31) && grid < (1l << 31), "kv_handoff: S*HD or the request too large for one launch");
+  return launch_pdl(kv_handoff_kernel, dim3((unsigned)grid), dim3(kXferThreads), 0, (cudaStream_t)stream,
+                    "kv_handoff_kernel", (const uint4*)src_k, (const uint4*)src_v, (long)(src_layer_stride / 8),
+                    (uint4*)dst_k, (uint4*)dst_v, (unsigned)run_vec, (unsigned)head_vec, (unsigned)cpr, NKV, lane,
+                    Bcap, layer0, (unsigned int*)done, layer1, (long long*)flags, (long long)seq);
+}
+
+extern "C" int rngd_kv_wait(const int64_t* flags, int layer0, int layer1, int64_t seq, int64_t timeout_ns,
+                            int32_t* status, rngd_stream_t stream) {
+  RNGD_REQUIRE(flags && status, "kv_wait: null pointer");
+  RNGD_REQUIRE(0 <= layer0 && layer0 < layer1, "kv_wait: bad layer range");
+  RNGD_REQUIRE(timeout_ns > 0 && timeout_ns <= 10000000000ll, "kv_wait: timeout must be in (0, 10 s]");
+  kv_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((const long long*)flags, layer0, layer1, (long long)seq,
+                                                     (long long)timeout_ns, (int*)status);
+  return check_launch("kv_wait_kernel");
+}

@@ -475,13 +475,9 @@ static int launch_pf(const void* W, int L, int layer, int N, int K, const void* 
   a.maxseg = pf_maxseg(units, a.nkb, grid);
   a.layer = layer;
   RNGD_REQUIRE(a.maxseg == 1 || (a.partial && a.counters), "prefill GEMM: split tiles need partial/counters");
-  static bool attr_set = false;
-  if (!attr_set) {
-    RNGD_TRY(check_cuda(cudaFuncSetAttribute(pfgemm_kernel<EPI, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)PCfg<NT>::SMEM),
-                        "cudaFuncSetAttribute(pfgemm)"));
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> attr_set{0};
+  RNGD_TRY(set_smem_limit_once((const void*)pfgemm_kernel<EPI, NT>, (int)PCfg<NT>::SMEM, &attr_set,
+                               "cudaFuncSetAttribute(pfgemm)"));
   return launch_pdl(pfgemm_kernel<EPI, NT>, dim3(grid), dim3(192), PCfg<NT>::SMEM, s, "pfgemm_kernel", tw, tx, a);
 }
 

@@ -95,6 +95,17 @@ _sig("rngd_lmhead_workspace", _MP, _szp, _szp)
 _sig("rngd_tc_gemm_tokens", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_int,
      _vp)
 _sig("rngd_tc_gemm_tokens_workspace", ctypes.c_int, ctypes.c_int, ctypes.c_int, _szp, _szp)
+_sig("rngd_ipc_alloc", ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _vp)
+_sig("rngd_ipc_free", _vp)
+_sig("rngd_ipc_open", _vp, ctypes.POINTER(ctypes.c_void_p))
+_sig("rngd_ipc_close", _vp)
+_sig("rngd_ipc_handle_size")
+_sig("rngd_peer_enable", ctypes.c_int, ctypes.c_int)
+_sig("rngd_host_alloc_mapped", ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p))
+_sig("rngd_host_free", _vp)
+_sig("rngd_kv_handoff", _vp, _vp, ctypes.c_size_t, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, ctypes.c_int64, _vp)
+_sig("rngd_kv_wait", _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _vp, _vp)
 _sig("rngd_device_status", ctypes.POINTER(ctypes.c_int), ctypes.c_int)
 _sig("rngd_gemv_bf16", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
      ctypes.c_int, _vp)
@@ -152,3 +163,20 @@ def decode_workspace(model, S):
 def exported_symbols():
     """Names declared in include/rngd_b200.h, for the ABI completeness test."""
     return [n for n in dir(lib) if n.startswith("rngd_")]
+
+
+def on_device(fn):
+    """Run an engine method with the engine's GPU current (`self.dev`, or `self.e.dev` for a
+    helper object holding its engine as `e`), so streams, launches and the library's per-device
+    state all agree when one process drives several GPUs."""
+    import functools
+
+    @functools.wraps(fn)
+    def wrapped(self, *a, **k):
+        import torch
+        dev = getattr(self, "dev", None)
+        if dev is None:
+            dev = self.e.dev
+        with torch.cuda.device(dev):
+            return fn(self, *a, **k)
+    return wrapped

@@ -126,18 +126,41 @@ class BatchDecodeEngine:
                 raise ValueError(f"cache group must be a contiguous bf16 {shape} tensor on {self.dev}, "
                                  f"got {tuple(t.shape)} {t.dtype} on {t.device}")
 
-    def _alloc_cache(self):
+    def _alloc_cache(self, ipc=False):
         c = self.cfg
-        K = torch.zeros((self.nl, self.B, c.n_kv, self.S, c.head_dim), dtype=BF, device=self.dev)
-        V = torch.zeros_like(K)
+        shape = (self.nl, self.B, c.n_kv, self.S, c.head_dim)
+        if ipc:
+            from rngd_pd.nvlink import ipc_empty
+            K, V = ipc_empty(shape, BF, self.dev), ipc_empty(shape, BF, self.dev)
+        else:
+            K = torch.zeros(shape, dtype=BF, device=self.dev)
+            V = torch.zeros_like(K)
         return ([K[g * self.NG:(g + 1) * self.NG] for g in range(self.ngroups)],
                 [V[g * self.NG:(g + 1) * self.NG] for g in range(self.ngroups)])
+
+    @_lib.on_device
+    def full_kv(self, Kd, Vd):
+        """The whole resident cache (K, V) [L][B][NKV][S][HD] behind a group list from blank_kv /
+        adopt_kv_device / load_kv: what a KV transport binds to write requests into lanes."""
+        self._check_cache(Kd, Vd)
+        c = self.cfg
+        shape = (self.nl, self.B, c.n_kv, self.S, c.head_dim)
+        out = []
+        for groups in (Kd, Vd):
+            g0 = groups[0]
+            step = g0.numel() * g0.element_size()
+            if any(t.data_ptr() != g0.data_ptr() + g * step for g, t in enumerate(groups)):
+                raise ValueError("full_kv: cache groups are not consecutive slices of one allocation")
+            out.append(torch.empty(0, dtype=BF, device=self.dev).set_(g0.untyped_storage(), g0.storage_offset(),
+                                                                      shape))
+        return out[0], out[1]
 
     # ---------------------------------------------------------- KV intake
     @staticmethod
     def _bf16_host(a):
         return a if torch.is_tensor(a) else torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(BF)
 
+    @_lib.on_device
     def prepare_kv(self, Ks, Vs):
         """Host-side stack + cast, off the device (engines/decode_batch.py:305-330).
         Ks/Vs: per-stream K [nl, NKV, HD, S] / V [nl, NKV, S, HD], padded to B lanes
@@ -156,6 +179,7 @@ class BatchDecodeEngine:
         return (torch.from_numpy(np.ascontiguousarray(K, dtype=np.float32)).to(BF),
                 torch.from_numpy(np.ascontiguousarray(V, dtype=np.float32)).to(BF))
 
+    @_lib.on_device
     def upload_prepared_kv(self, prepared):
         """Transfer + relayout to the decode layout (engines/decode_batch.py:343-351)."""
         K, V = prepared
@@ -168,9 +192,11 @@ class BatchDecodeEngine:
             Vd[g].copy_(Vdev[sl])
         return Kd, Vd
 
+    @_lib.on_device
     def load_kv(self, Ks, Vs):
         return self.upload_prepared_kv(self.prepare_kv(Ks, Vs))
 
+    @_lib.on_device
     def write_slot_kv(self, Kd, Vd, idx, K, V):
         """Replace lane idx of the resident cache in place (engines/decode_batch.py:357-377).
         K [nl, NKV, HD, S] / V [nl, NKV, S, HD]: host float32/bf16 or device tensors."""
@@ -184,16 +210,19 @@ class BatchDecodeEngine:
             Vd[g][:, idx].copy_(Vt[sl])
         return Kd, Vd
 
+    @_lib.on_device
     def download_kv(self, Kd, Vd):
         """Resident cache -> host [nl, B, NKV, HD, S] / [nl, B, NKV, S, HD] float32."""
         K = torch.cat([k.transpose(-1, -2).float().cpu() for k in Kd], 0).numpy()
         V = torch.cat([v.float().cpu() for v in Vd], 0).numpy()
         return K, V
 
+    @_lib.on_device
     def upload_kv(self, K, V):
         """[nl, B, ...] host arrays (reference layout) back onto the device, per group."""
         return self.upload_prepared_kv((self._bf16_host(K), self._bf16_host(V)))
 
+    @_lib.on_device
     def adopt_kv_device(self, Ks, Vs):
         """Per-request device caches (prefill on this card, reference layout) batched in place
         (engines/decode_batch.py:399-414)."""
@@ -206,9 +235,11 @@ class BatchDecodeEngine:
             self.write_slot_kv(Kd, Vd, b, Ks[b], Vs[b])
         return Kd, Vd
 
-    def blank_kv(self):
-        """An empty resident cache: every slot free (engines/decode_batch.py:416-420)."""
-        return self._alloc_cache()
+    @_lib.on_device
+    def blank_kv(self, ipc=False):
+        """An empty resident cache: every slot free (engines/decode_batch.py:416-420).
+        ipc=True allocates it so that a prefill process can map it (rngd_pd.nvlink)."""
+        return self._alloc_cache(ipc)
 
     # ---------------------------------------------------------------- step
     def _launch(self, Kd, Vd, stream):
@@ -269,6 +300,7 @@ class BatchDecodeEngine:
             else:
                 self._launch(Kd, Vd, s)
 
+    @_lib.on_device
     def step(self, toks, positions, Kd, Vd):
         """One token for each of B streams. Returns next tokens and the cache."""
         toks, positions = self._validate(toks, positions)
@@ -278,6 +310,7 @@ class BatchDecodeEngine:
         self.stream.synchronize()
         return self._out_host.tolist(), Kd, Vd
 
+    @_lib.on_device
     def step_logits(self, toks, positions, Kd, Vd):
         """The same step returning fp32 logits in the reference layout [NG, Vp/NG, B]
         (zero-padded past V) on the device, for teacher-forced comparisons."""
@@ -288,6 +321,7 @@ class BatchDecodeEngine:
         lg[:self.V] = self._logits.t()
         return lg.view(self.NGV, self.Vp // self.NGV, self.B), Kd, Vd
 
+    @_lib.on_device
     def set_inputs(self, toks, positions):
         """Upload tokens/positions for step_device() (validated like step())."""
         toks, positions = self._validate(toks, positions)
@@ -299,6 +333,7 @@ class BatchDecodeEngine:
             self._pos.copy_(self._in_host[1], non_blocking=True)
             self._copied.record(self.stream)
 
+    @_lib.on_device
     def step_device(self, Kd, Vd, n=1):
         """n greedy steps entirely on the device: each step's argmax becomes the next
         step's token and every position advances by one (no host round trip).  The
@@ -314,9 +349,11 @@ class BatchDecodeEngine:
                 else:
                     g.replay()
 
+    @_lib.on_device
     def next_tokens_device(self):
         return self._next
 
+    @_lib.on_device
     def logits_bv(self):
         """The last step's logits as [B, V] fp32 (device)."""
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)

@@ -38,6 +38,7 @@ class _DevicePrefillStage:
         eng._begin(self._b, tokens, self.kv)
         self.g = 0
 
+    @_lib.on_device
     def advance(self, n=1):
         for _ in range(n):
             self.e._group(self._b, self.g, self.kv)
@@ -46,6 +47,7 @@ class _DevicePrefillStage:
                 return True
         return False
 
+    @_lib.on_device
     def result(self):
         nxt = self.e._finish(self._b)
         K, V = self.e.reference_layout(self.kv)
@@ -82,6 +84,7 @@ class FullPrefillEngine:
         self._build_lmhead()
 
     # ------------------------------------------------------------- buckets
+    @_lib.on_device
     def add_bucket(self, C):
         """Buffers for one prefill width (engines/prefill_full.py:168-203)."""
         if C in self.buckets:
@@ -117,6 +120,7 @@ class FullPrefillEngine:
         fits = [c for c in sorted(self.buckets) if c >= P]
         return fits[0] if fits else max(self.buckets)
 
+    @_lib.on_device
     def _build_lmhead(self):
         import ctypes
         c, d = self.cfg, self.dev
@@ -175,6 +179,7 @@ class FullPrefillEngine:
         s.synchronize()
         return int(lm["next"].item())
 
+    @_lib.on_device
     def prefill_kv_device(self, tokens, kv=None):
         """The whole pass; returns (kv [L, 2, NKV, S, HD] bf16 on the device, next token).
         `kv` may be a caller-owned zeroed buffer of that shape (e.g. a decode-side landing zone)."""
@@ -194,6 +199,7 @@ class FullPrefillEngine:
         self.last_compute_ms = (time.perf_counter() - t0) * 1e3
         return kv, nxt
 
+    @_lib.on_device
     def logits(self):
         """fp32 logits [V] of the last prefill's final position (device)."""
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)
@@ -204,6 +210,7 @@ class FullPrefillEngine:
         """prefill layout [L, 2, NKV, S, HD] -> reference K [L, NKV, HD, S], V [L, NKV, S, HD] (views)."""
         return kv[:, 0].transpose(-1, -2), kv[:, 1]
 
+    @_lib.on_device
     def prefill_device(self, tokens):
         """Prefill and leave the cache on the device in the reference layout (bf16), padded to S
         with zeros past the prompt (engines/prefill_full.py:278-304)."""
@@ -211,10 +218,12 @@ class FullPrefillEngine:
         K, V = self.reference_layout(kv)
         return K.contiguous(), V.contiguous(), nxt
 
+    @_lib.on_device
     def begin_device_prefill(self, tokens):
         """Prefill as resumable layer-group steps (engines/prefill_full.py:306-317)."""
         return _DevicePrefillStage(self, tokens)
 
+    @_lib.on_device
     def prefill_stream(self, tokens, sink):
         """Hand each layer group's cache over as it exists (engines/prefill_full.py:337-388):
         sink(g, kh, vh) with host float32 kh [NG, NKV, HD, S], vh [NG, NKV, S, HD]."""
@@ -242,6 +251,7 @@ class FullPrefillEngine:
         self.last_download_ms = t_d * 1e3
         return self._finish(b)
 
+    @_lib.on_device
     def prefill_stream_device(self, tokens, sink):
         """The same with device views: sink(g, kv_group [NG, 2, NKV, S, HD]) right after the group's
         kernels are queued on self.stream (the sink orders its own work after that stream)."""
@@ -257,6 +267,7 @@ class FullPrefillEngine:
             sink(g, kv[g * self.NG:(g + 1) * self.NG])
         return self._finish(b)
 
+    @_lib.on_device
     def prefill(self, tokens):
         """The same pass, handed back as host float32 arrays in the reference layout
         (engines/prefill_full.py:390-400)."""

@@ -76,3 +76,15 @@ def request_kv(cfg, S, seed, length, device="cuda", sigma=1.0):
     K[:, :, length:] = 0
     V[:, :, length:] = 0
     return K.transpose(2, 3).contiguous(), V
+
+
+def handoff_kv(cfg, S, seed, device="cuda", sigma=1.0):
+    """One request's cache in the prefill layout [L, 2, NKV, S, HD] bf16, every position
+    ~N(0, sigma) under the request's seed: K from the (seed, 0x8000) stream and V from
+    (seed, 0x8001), each drawn in [L, NKV, S, HD] order (the KV handoff workload)."""
+    import torch
+    shape = (cfg.n_layers, cfg.n_kv, S, cfg.head_dim)
+    kv = torch.empty((cfg.n_layers, 2) + shape[1:], dtype=torch.bfloat16, device=device)
+    kv[:, 0] = fill_gauss(torch.empty(shape, dtype=torch.bfloat16, device=device), seed, T_KCACHE, sigma)
+    kv[:, 1] = fill_gauss(torch.empty(shape, dtype=torch.bfloat16, device=device), seed, T_VCACHE, sigma)
+    return kv

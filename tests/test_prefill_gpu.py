@@ -4,7 +4,8 @@ Small-dimension prompts across buckets against the numpy restatement of the
 reference's cpu_layer_p (KV cache and last-token logits), the staged / streamed /
 device entry points against each other, prefill -> decode on one card, and
 BASELINE config 2 at full Llama-3.1-8B size against the C restatement (last-token
-logits within 2e-2 max-abs, same next token, KV within one bf16 ulp).
+logits within 2e-2 max-abs, same next token, layer-0 KV within one bf16 ulp, every
+layer's KV within 0.05 max-abs and 5e-3 mean-abs).
 """
 import numpy as np
 import pytest
@@ -148,15 +149,19 @@ def test_config2_full_prefill_C256(full_llama):
     err = float(np.abs(lg - lgr).max())
     assert err < 2e-2, f"last-token logits max-abs {err}"
     assert nxt == nxt_ref
-    # KV: both sides round to bf16; fp32 summation-order noise, amplified through 32 random
-    # layers, moves a value across a rounding boundary now and then
+    # KV: both sides round to bf16.  Layer 0 sees only one GEMM's summation-order noise, so its
+    # values agree to the last bf16 bit but for rounding-boundary cases; each later layer feeds
+    # the previous differences through 32 random-weight layers, which grow them steadily
+    # (measured: mean |dKV| 1e-6 at layer 0, 2.3e-3 at layer 31, values of rms 1.27; max 0.031)
     Kd = kv[:, 0].transpose(-1, -2).contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
     Vd = kv[:, 1].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
     for dev_bits, ref_bits in ((Kd, Kr), (Vd, Vr)):
-        ulps = np.abs(_ordered(dev_bits) - _ordered(ref_bits))
-        assert (ulps <= 1).mean() > 0.99, f"{(ulps <= 1).mean():.4f} of KV values within one bf16 ulp"
-        diff = np.abs(sy.bf16_bits_to_f32(dev_bits) - sy.bf16_bits_to_f32(ref_bits)).max()
-        assert diff < 0.05, f"KV max-abs difference {diff}"
+        ulps0 = np.abs(_ordered(dev_bits[0]) - _ordered(ref_bits[0]))
+        assert (ulps0 <= 1).mean() > 0.999, f"layer 0: {(ulps0 <= 1).mean():.5f} of KV values within one bf16 ulp"
+        for l in range(cfg.n_layers):
+            d = np.abs(sy.bf16_bits_to_f32(dev_bits[l]) - sy.bf16_bits_to_f32(ref_bits[l]))
+            assert d.max() < 0.05, f"layer {l}: KV max-abs difference {d.max()}"
+            assert d.mean() < 5e-3, f"layer {l}: KV mean-abs difference {d.mean()}"
 
 
 def _ordered(bits):
