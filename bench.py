@@ -186,7 +186,7 @@ class TcGemm:
 
 
 def gemm_roofline(eng, reps=32):
-    """The dominant kernel (the tcgen05 decode GEMM, wsgemm_kernel) per weight shape, CUDA events on its stream."""
+    """The dominant kernel (the tcgen05 decode GEMM, skgemm_kernel) per weight shape, CUDA events on its stream."""
     import torch
     w, c = eng.w, eng.cfg
     H, M = c.hidden, c.inter
@@ -323,11 +323,29 @@ def run_micro_handoff(args):
     print(json.dumps({"micro": "handoff", "unit": "GB/s", "results": out}), flush=True)
 
 
+SLEEP_CYCLES = 400_000     # ~0.2 ms of torch.cuda._sleep ahead of a timed launch hides host enqueue time
+
+
+def _time_pushes(tx, items, s):
+    """One batched push (a single launch for <= 16 requests) timed with CUDA events on its stream;
+    a short clock sleep queued first keeps the stream busy while the host enqueues the launch, so
+    the events bracket the kernel and not the Python call."""
+    import torch
+    with torch.cuda.stream(s):
+        torch.cuda._sleep(SLEEP_CYCLES)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    tx.push_many(items, stream=s)
+    e1.record(s)
+    return e0, e1
+
+
 def handoff_one_process(dsts, reps, warmup):
     """Config 3 in one process: 1/4/16 requests of 512 tokens pushed by the fused handoff kernel
-    from GPU 0 into decode lanes on each GPU of `dsts` (GPU 0: HBM -> HBM; another GPU: over
-    NVLink with peer access); byte-exact check of every lane; for a peer, a copy-engine peer
-    copy of the same bytes as comparator."""
+    (one launch per batch) from GPU 0 into decode lanes on each GPU of `dsts` (GPU 0: HBM -> HBM;
+    another GPU: over NVLink with peer access); byte-exact check of every lane.  Per batch size:
+    the kernel's device time, and the API time (push_many + the receiver's wait() seeing every
+    flag, host wall clock); for a peer, a copy-engine peer copy of the same bytes as comparator."""
     import torch
     from rngd_pd import synth
     from rngd_pd.engines.model import ModelConfig
@@ -355,41 +373,48 @@ def handoff_one_process(dsts, reps, warmup):
         key = tx.set_remote_handshake(rx.handshake_metadata()) if tx is not rx else None
         s = torch.cuda.Stream(device=src)
         for n in HANDOFF_BATCHES:
-            times, used = [], []
-            for rep in range(warmup + reps):
+            dev_ms, api_ms, used = [], [], []
+            for rep in range(2 * (warmup + reps)):
+                timed_dev = rep % 2 == 0                         # alternate device-timed / API-timed
                 ids = [f"r{n}.{rep}.{b}" for b in range(n)]
                 used = [(rep * n + b) % B for b in range(n)]      # rotate sources: > L2 across reps
                 for b, r in enumerate(ids):
                     tk = rx.reserve(r, b, sender_device=0)
                     if key is not None:
                         tx.add_lease(key, tk)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(s)
-                for b, r in enumerate(ids):
-                    tx.push_device(r, kvs[used[b]], stream=s)
-                e1.record(s)
-                for r in ids:
-                    rx.wait(r, timeout=10)
-                e1.synchronize()
-                if rep >= warmup:
-                    times.append(e0.elapsed_time(e1))
+                items = [(r, kvs[used[b]], None) for b, r in enumerate(ids)]
+                if timed_dev:
+                    e0, e1 = _time_pushes(tx, items, s)
+                    for r in ids:
+                        rx.wait(r, timeout=10)
+                    e1.synchronize()
+                    if rep // 2 >= warmup:
+                        dev_ms.append(e0.elapsed_time(e1))
+                else:
+                    t0 = time.perf_counter()
+                    tx.push_many(items, stream=s)
+                    for r in ids:
+                        rx.wait(r, timeout=10)
+                    if rep // 2 >= warmup:
+                        api_ms.append((time.perf_counter() - t0) * 1e3)
                 for r in ids:
                     rx.release(r)
             exact = all(torch.equal(K[:, b].view(torch.int16), kvs[used[b]][:, 0].to(ddev).view(torch.int16)) and
                         torch.equal(V[:, b].view(torch.int16), kvs[used[b]][:, 1].to(ddev).view(torch.int16))
                         for b in range(n))
-            ms = statistics.median(times)
+            ms, ams = statistics.median(dev_ms), statistics.median(api_ms)
             gbs = n * per_req / ms / 1e6
-            row = {"dst": f"cuda:{dst}", "requests": n, "ms": ms, "payload_bytes": n * per_req, "gbs": gbs,
-                   "byte_exact": exact}
+            row = {"dst": f"cuda:{dst}", "requests": n, "launches": 1, "ms": ms, "payload_bytes": n * per_req,
+                   "gbs": gbs, "api_ms": ams, "api_gbs": n * per_req / ams / 1e6, "byte_exact": exact}
             if dst == 0:
-                row.update(bound="hbm", frac=2 * gbs / hbm, peak=hbm)
+                row.update(bound="hbm", frac=2 * gbs / hbm, peak=hbm, note="frac counts read + write")
             else:
                 flat = torch.empty(n * per_req // 2, dtype=torch.bfloat16, device=ddev)
                 ce = []
                 for rep in range(3 + reps):
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     with torch.cuda.stream(s):
+                        torch.cuda._sleep(SLEEP_CYCLES)
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         e0.record(s)
                         for b in range(n):
                             flat[b * (per_req // 2):(b + 1) * (per_req // 2)].copy_(
@@ -449,11 +474,7 @@ def handoff_pairs(rank, world, dev, reps, warmup):
                     t.add_lease(key, tk)
             dist.barrier()
             if sender:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(s)
-                for b, tk in enumerate(allt[partner]):
-                    t.push_device(tk["req"], kvs[used[b]], stream=s)
-                e1.record(s)
+                e0, e1 = _time_pushes(t, [(tk["req"], kvs[used[b]], None) for b, tk in enumerate(allt[partner])], s)
                 e1.synchronize()
                 if rep >= warmup:
                     times.append(e0.elapsed_time(e1))
@@ -626,7 +647,7 @@ def run_ours(args):
     dom = roof["gate_up"]
     traffic = None
     try:
-        traffic = _j.load(open(os.path.join(REPO, "profiles", "traffic.json"))).get("wsgemm_gate_up")
+        traffic = _j.load(open(os.path.join(REPO, "profiles", "traffic.json"))).get("skgemm_gate_up")
     except (OSError, ValueError):
         pass
     cpu = None

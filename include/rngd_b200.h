@@ -189,6 +189,23 @@ int rngd_host_free(void* host);
 int rngd_kv_handoff(const void* src_k, const void* src_v, size_t src_layer_stride, void* dst_k, void* dst_v, int L,
                     int NKV, int S, int HD, int tokens, int lane, int Bcap, int layer0, int layer1, uint32_t* done,
                     int64_t* flags, int64_t seq, rngd_stream_t stream);
+/* One request of a batched handoff: its layer0 K / V blocks (as in rngd_kv_handoff),
+ * the decode lane it lands in, how many leading positions move, and the lease's
+ * sequence number published in the lane's flags. */
+#define RNGD_KV_MAX_BATCH 16
+typedef struct {
+  const void* src_k;
+  const void* src_v;
+  int lane;
+  int tokens;
+  int64_t seq;
+} rngd_kv_item_t;
+/* rngd_kv_handoff for 1..RNGD_KV_MAX_BATCH requests (distinct lanes) into one
+ * receiver in a single launch.  flags: the receiver's whole [Bcap][L] int64 flag
+ * array; done: n zeroed uint32 counters on the sending device (one set per stream). */
+int rngd_kv_handoff_batch(const rngd_kv_item_t* items, int n, size_t src_layer_stride, void* dst_k, void* dst_v,
+                          int L, int NKV, int S, int HD, int Bcap, int layer0, int layer1, uint32_t* done,
+                          int64_t* flags, rngd_stream_t stream);
 /* Bounded device wait until flags[l] >= seq for l in [layer0, layer1): writes 0,
  * or RNGD_ERR_TIMEOUT's wait code 4 after timeout_ns (<= 10 s), to *status
  * (e.g. host-mapped); later work on `stream` is ordered after the arrival. */

@@ -7,17 +7,17 @@
 // layer); the decode cache keeps K and V as [L][Bcap][NKV][S][HD].  Moving
 // layers [l0, l1) of one request's first `tokens` positions into decode lane `lane`
 // is therefore a set of contiguous tokens*HD-element runs, one per (layer, K|V, head):
-// one fused kernel (a CTA per 32 KB chunk of a run) reads them from local HBM
+// one fused kernel (a CTA per 32 KB chunk of a run, up to 16 requests per launch)
+// reads them from local HBM
 // (16-byte loads) and stores them straight into the destination, which may be a
 // peer GPU's memory mapped by CUDA IPC or peer access, so pack, transfer and unpack
 // are one pass.
 //
-// Completion fence: every CTA issues fence.sc.sys after its stores and bumps a
-// sender-side counter; the CTA that brings the counter to the grid size issues
-// another fence.sc.sys and publishes flags[l] = seq for each moved layer with a
-// system-scope release store (the "threadfence reduction" pattern at system
-// scope), so a reader that observes the flag with acquire semantics sees all the
-// layer's bytes.  The reader's wait is a bounded device loop that reports a
+// Completion fence: every CTA fences after its stores and counts itself into its
+// request's counter; the CTA that completes a request's count issues fence.sc.sys
+// and publishes flags[l] = seq for each moved layer with a system-scope release
+// store (the "threadfence reduction" pattern), so a reader that observes the flag
+// with acquire semantics sees all the request's bytes.  The reader's wait is a bounded device loop that reports a
 // status; it never traps or spins forever.
 #include "tc.cuh"
 
@@ -27,20 +27,44 @@ constexpr int kXferThreads = 256;
 constexpr int kXferVec = 8;                                    // 16-byte vectors per thread per chunk
 constexpr unsigned kXferChunk = kXferThreads * kXferVec;       // 2048 vectors = 32 KB
 
-// One CTA per chunk of one run.  A run is (layer, K|V, head): the first `tokens` positions of
-// one head, run_vec contiguous 16-byte vectors in both layouts (heads sit head_vec vectors
-// apart).  The chunk -> (run, part) split is one division per CTA, so the per-vector work is
-// an add, a load and a store; every thread keeps kXferVec independent loads in flight.
-__global__ void __launch_bounds__(kXferThreads) kv_handoff_kernel(
-    const uint4* __restrict__ src_k, const uint4* __restrict__ src_v, long src_stride_vec, uint4* __restrict__ dst_k,
-    uint4* __restrict__ dst_v, unsigned run_vec, unsigned head_vec, unsigned chunks_per_run, int NKV, int lane,
-    int Bcap, int layer0, unsigned int* __restrict__ done, int layer1, long long* __restrict__ flags, long long seq) {
+// A batch of requests moved by one launch into lanes of one receiver's cache.
+struct XferBatch {
+  const uint4* src_k[RNGD_KV_MAX_BATCH];
+  const uint4* src_v[RNGD_KV_MAX_BATCH];
+  long long seq[RNGD_KV_MAX_BATCH];
+  unsigned run_vec[RNGD_KV_MAX_BATCH];   // 16-byte vectors of one run (tokens * HD * 2 / 16)
+  unsigned cpr[RNGD_KV_MAX_BATCH];       // chunks per run
+  unsigned first[RNGD_KV_MAX_BATCH + 1]; // first CTA of each request; first[n] = grid
+  int lane[RNGD_KV_MAX_BATCH];
+  int n;
+};
+
+// One CTA per chunk: 32 KB of one run of one request.  A run is (layer, K|V, head): the
+// first `tokens` positions of one head, run_vec contiguous 16-byte vectors in both layouts
+// (heads sit head_vec vectors apart).  The CTA -> (request, run, part) split costs a scan
+// over at most 16 entries and two divisions per CTA; the per-vector work is an add, a load
+// and a store, with kXferVec independent loads in flight per thread.
+//
+// Completion: each CTA fences at gpu scope (the counters live on this GPU) and counts itself
+// into its request's counter; the CTA that completes a request fences at system scope and
+// publishes that request's layer flags with a system-scope release, so a reader acquiring a
+// flag sees every byte of the request.
+__global__ void __launch_bounds__(kXferThreads) kv_handoff_kernel(const __grid_constant__ XferBatch b,
+                                                                  long src_stride_vec, uint4* __restrict__ dst_k,
+                                                                  uint4* __restrict__ dst_v, unsigned head_vec,
+                                                                  int NKV, int L, int Bcap, int layer0, int layer1,
+                                                                  unsigned int* __restrict__ done,
+                                                                  long long* __restrict__ flags) {
   grid_dep_wait();
-  const unsigned run = blockIdx.x / chunks_per_run, part = blockIdx.x - run * chunks_per_run;
+  int r = 0;
+  while (r + 1 < b.n && blockIdx.x >= b.first[r + 1]) r++;
+  const unsigned cta = blockIdx.x - b.first[r];
+  const unsigned run = cta / b.cpr[r], part = cta - run * b.cpr[r];
   const unsigned h = run % (unsigned)NKV, lkv = run / (unsigned)NKV, lr = lkv >> 1;
   const bool isv = lkv & 1u;
-  const uint4* s = (isv ? src_v : src_k) + (long)lr * src_stride_vec + (long)h * head_vec;
-  uint4* d = (isv ? dst_v : dst_k) + (((long)(layer0 + (int)lr) * Bcap + lane) * NKV + h) * (long)head_vec;
+  const unsigned run_vec = b.run_vec[r];
+  const uint4* s = (isv ? b.src_v[r] : b.src_k[r]) + (long)lr * src_stride_vec + (long)h * head_vec;
+  uint4* d = (isv ? dst_v : dst_k) + (((long)(layer0 + (int)lr) * Bcap + b.lane[r]) * NKV + h) * (long)head_vec;
   const unsigned o0 = part * kXferChunk + threadIdx.x;
   uint4 v[kXferVec];
 #pragma unroll
@@ -55,13 +79,14 @@ __global__ void __launch_bounds__(kXferThreads) kv_handoff_kernel(
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
-    const unsigned int prev = atomicAdd(done, 1u);
-    if (prev == gridDim.x - 1) {
+    __threadfence();
+    const unsigned prev = atomicAdd(done + r, 1u);
+    if (prev == b.first[r + 1] - b.first[r] - 1) {
       __threadfence_system();
+      long long* f = flags + (long)b.lane[r] * L;
       for (int l = layer0; l < layer1; l++)
-        asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(flags + l), "l"(seq) : "memory");
-      *done = 0u;  // ready for the next handoff on this stream
+        asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(f + l), "l"(b.seq[r]) : "memory");
+      done[r] = 0u;  // ready for the next handoff on this stream
     }
   }
 }
@@ -146,25 +171,64 @@ extern "C" int rngd_host_alloc_mapped(size_t bytes, void** host, void** dev) {
 
 extern "C" int rngd_host_free(void* host) { return check_cuda(cudaFreeHost(host), "cudaFreeHost"); }
 
+extern "C" int rngd_kv_handoff_batch(const rngd_kv_item_t* items, int n, size_t src_layer_stride, void* dst_k,
+                                     void* dst_v, int L, int NKV, int S, int HD, int Bcap, int layer0, int layer1,
+                                     uint32_t* done, int64_t* flags, rngd_stream_t stream) {
+  RNGD_REQUIRE(items && 1 <= n && n <= RNGD_KV_MAX_BATCH, "kv_handoff: 1..%d requests per launch, got %d",
+               RNGD_KV_MAX_BATCH, n);
+  RNGD_REQUIRE(dst_k && dst_v && done && flags, "kv_handoff: null pointer");
+  RNGD_REQUIRE(0 <= layer0 && layer0 < layer1 && layer1 <= L, "kv_handoff: layers [%d, %d) outside [0, %d)",
+               layer0, layer1, L);
+  RNGD_REQUIRE(NKV > 0 && HD > 0 && S > 0 && (HD * 2) % 16 == 0 && src_layer_stride % 8 == 0 &&
+                   ((uintptr_t)dst_k | (uintptr_t)dst_v) % 16 == 0,
+               "kv_handoff: HD*2 and the layer stride must be 16-byte multiples, buffers 16-byte aligned");
+  const long head_vec = (long)S * HD * 2 / 16;
+  RNGD_REQUIRE(head_vec < (1l << 31), "kv_handoff: S*HD too large");
+  XferBatch b;
+  memset(&b, 0, sizeof(b));
+  b.n = n;
+  long grid = 0;
+  for (int i = 0; i < n; i++) {
+    const rngd_kv_item_t& it = items[i];
+    RNGD_REQUIRE(it.src_k && it.src_v && ((uintptr_t)it.src_k | (uintptr_t)it.src_v) % 16 == 0,
+                 "kv_handoff: request %d: null or unaligned source", i);
+    RNGD_REQUIRE(0 <= it.lane && it.lane < Bcap, "kv_handoff: request %d: lane %d outside 0..%d", i, it.lane,
+                 Bcap - 1);
+    RNGD_REQUIRE(0 < it.tokens && it.tokens <= S, "kv_handoff: request %d: tokens %d outside 1..S=%d", i, it.tokens,
+                 S);
+    for (int j = 0; j < i; j++)
+      RNGD_REQUIRE(items[j].lane != it.lane, "kv_handoff: requests %d and %d share lane %d", j, i, it.lane);
+    const long run_vec = (long)it.tokens * HD * 2 / 16;
+    const long cpr = (run_vec + kXferChunk - 1) / kXferChunk;
+    b.src_k[i] = (const uint4*)it.src_k;
+    b.src_v[i] = (const uint4*)it.src_v;
+    b.seq[i] = (long long)it.seq;
+    b.run_vec[i] = (unsigned)run_vec;
+    b.cpr[i] = (unsigned)cpr;
+    b.lane[i] = it.lane;
+    b.first[i] = (unsigned)grid;
+    grid += cpr * 2 * NKV * (layer1 - layer0);
+    RNGD_REQUIRE(grid < (1l << 31), "kv_handoff: batch too large for one launch");
+  }
+  b.first[n] = (unsigned)grid;
+  return launch_pdl(kv_handoff_kernel, dim3((unsigned)grid), dim3(kXferThreads), 0, (cudaStream_t)stream,
+                    "kv_handoff_kernel", b, (long)(src_layer_stride / 8), (uint4*)dst_k, (uint4*)dst_v,
+                    (unsigned)head_vec, NKV, L, Bcap, layer0, layer1, (unsigned int*)done, (long long*)flags);
+}
+
 extern "C" int rngd_kv_handoff(const void* src_k, const void* src_v, size_t src_layer_stride, void* dst_k,
                                void* dst_v, int L, int NKV, int S, int HD, int tokens, int lane, int Bcap, int layer0,
                                int layer1, uint32_t* done, int64_t* flags, int64_t seq, rngd_stream_t stream) {
-  RNGD_REQUIRE(src_k && src_v && dst_k && dst_v && done && flags, "kv_handoff: null pointer");
-  RNGD_REQUIRE(0 <= lane && lane < Bcap, "kv_handoff: lane %d outside 0..%d", lane, Bcap - 1);
-  RNGD_REQUIRE(0 <= layer0 && layer0 < layer1 && layer1 <= L, "kv_handoff: layers [%d, %d) outside [0, %d)",
-               layer0, layer1, L);
-  RNGD_REQUIRE(NKV > 0 && HD > 0 && 0 < tokens && tokens <= S, "kv_handoff: tokens %d outside 1..S=%d", tokens, S);
-  RNGD_REQUIRE(((uintptr_t)src_k | (uintptr_t)src_v | (uintptr_t)dst_k | (uintptr_t)dst_v) % 16 == 0 &&
-                   src_layer_stride % 8 == 0 && (HD * 2) % 16 == 0,
-               "kv_handoff: buffers must be 16-byte aligned and HD*2 a multiple of 16");
-  const long run_vec = (long)tokens * HD * 2 / 16, head_vec = (long)S * HD * 2 / 16;
-  const long cpr = (run_vec + kXferChunk - 1) / kXferChunk;
-  const long grid = cpr * 2 * NKV * (layer1 - layer0);
-  RNGD_REQUIRE(head_vec < (1l << 31) && grid < (1l << 31), "kv_handoff: S*HD or the request too large for one launch");
-  return launch_pdl(kv_handoff_kernel, dim3((unsigned)grid), dim3(kXferThreads), 0, (cudaStream_t)stream,
-                    "kv_handoff_kernel", (const uint4*)src_k, (const uint4*)src_v, (long)(src_layer_stride / 8),
-                    (uint4*)dst_k, (uint4*)dst_v, (unsigned)run_vec, (unsigned)head_vec, (unsigned)cpr, NKV, lane,
-                    Bcap, layer0, (unsigned int*)done, layer1, (long long*)flags, (long long)seq);
+  RNGD_REQUIRE(flags, "kv_handoff: null flags");
+  rngd_kv_item_t it;
+  it.src_k = src_k;
+  it.src_v = src_v;
+  it.lane = lane;
+  it.tokens = tokens;
+  it.seq = seq;
+  // the single-request form takes the lane's own flag row
+  return rngd_kv_handoff_batch(&it, 1, src_layer_stride, dst_k, dst_v, L, NKV, S, HD, Bcap, layer0, layer1, done,
+                               flags - (long)lane * L, stream);
 }
 
 extern "C" int rngd_kv_wait(const int64_t* flags, int layer0, int layer1, int64_t seq, int64_t timeout_ns,

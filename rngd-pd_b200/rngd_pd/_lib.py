@@ -105,6 +105,14 @@ _sig("rngd_host_alloc_mapped", ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p),
 _sig("rngd_host_free", _vp)
 _sig("rngd_kv_handoff", _vp, _vp, ctypes.c_size_t, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, ctypes.c_int64, _vp)
+class KvItem(ctypes.Structure):
+    _fields_ = [("src_k", ctypes.c_void_p), ("src_v", ctypes.c_void_p), ("lane", ctypes.c_int),
+                ("tokens", ctypes.c_int), ("seq", ctypes.c_int64)]
+
+
+KV_MAX_BATCH = 16
+_sig("rngd_kv_handoff_batch", ctypes.POINTER(KvItem), ctypes.c_int, ctypes.c_size_t, _vp, _vp, ctypes.c_int,
+     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp)
 _sig("rngd_kv_wait", _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _vp, _vp)
 _sig("rngd_device_status", ctypes.POINTER(ctypes.c_int), ctypes.c_int)
 _sig("rngd_gemv_bf16", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,

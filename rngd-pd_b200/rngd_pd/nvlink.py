@@ -351,17 +351,28 @@ class NvlinkTransport(Transport):
         """Move a request's cache (prefill layout [L][2][NKV][S][HD] bf16 on this device, or the
         layer block [layer1-layer0][2][NKV][S][HD] starting at layer0) into its leased lane.
         tokens: move positions [0, tokens) only (the prompt); default all S.  Returns the bytes moved."""
-        peer, lane, seq = self._target(req_id)
-        L = peer.L
-        layer1 = L if layer1 is None else layer1
-        if kv.dtype != BF or not kv.is_contiguous() or kv.device != self.device:
-            raise ValueError(f"nvlink: kv must be a contiguous bf16 tensor on {self.device}")
-        blk = kv if kv.shape[0] == layer1 - layer0 else kv[layer0:layer1]
-        if tuple(blk.shape[1:]) != (2, peer.NKV, peer.S, peer.HD):
-            raise ValueError(f"nvlink: kv layer block {tuple(blk.shape)} does not match the receiver's "
-                             f"[*, 2, {peer.NKV}, {peer.S}, {peer.HD}]")
-        return self._launch(peer, lane, seq, blk[:, 0], blk[:, 1], 2 * peer.NKV * peer.S * peer.HD, layer0, layer1,
-                            stream, tokens)
+        return self.push_many([(req_id, kv, tokens)], layer0, layer1, stream)
+
+    def push_many(self, items, layer0=0, layer1=None, stream=None):
+        """push_device for several requests [(req_id, kv, tokens or None), ...]: one launch per
+        receiver and per 16 requests (rngd_kv_handoff_batch).  Returns the bytes moved."""
+        groups = {}
+        for req_id, kv, tokens in items:
+            peer, lane, seq = self._target(req_id)
+            l1 = peer.L if layer1 is None else layer1
+            if kv.dtype != BF or not kv.is_contiguous() or kv.device != self.device:
+                raise ValueError(f"nvlink: kv must be a contiguous bf16 tensor on {self.device}")
+            blk = kv if kv.shape[0] == l1 - layer0 else kv[layer0:l1]
+            if tuple(blk.shape[1:]) != (2, peer.NKV, peer.S, peer.HD) or blk.shape[0] != l1 - layer0:
+                raise ValueError(f"nvlink: kv layer block {tuple(blk.shape)} does not match the receiver's "
+                                 f"[{l1 - layer0}, 2, {peer.NKV}, {peer.S}, {peer.HD}]")
+            groups.setdefault(id(peer), (peer, l1, []))[2].append((lane, seq, blk[:, 0], blk[:, 1], tokens))
+        moved = 0
+        for peer, l1, reqs in groups.values():
+            for i in range(0, len(reqs), _lib.KV_MAX_BATCH):
+                moved += self._launch(peer, reqs[i:i + _lib.KV_MAX_BATCH], 2 * peer.NKV * peer.S * peer.HD, layer0,
+                                      l1, stream)
+        return moved
 
     def push_layer(self, req_id, layer, k, v, stream=None, tokens=None):
         """Move one layer's k [NKV][S][HD] and v [NKV][S][HD] (the connector's save_kv_layer)."""
@@ -371,29 +382,34 @@ class NvlinkTransport(Transport):
                     tuple(t.shape) != (peer.NKV, peer.S, peer.HD):
                 raise ValueError(f"nvlink: layer tensors must be contiguous bf16 [{peer.NKV}, {peer.S}, "
                                  f"{peer.HD}] on {self.device}")
-        return self._launch(peer, lane, seq, k, v, 0, layer, layer + 1, stream, tokens)
+        return self._launch(peer, [(lane, seq, k, v, tokens)], 0, layer, layer + 1, stream)
 
     def _counter(self, s):
         key = s.cuda_stream
         with self._lock:
             c = self._done.get(key)
             if c is None:
-                c = self._done[key] = torch.zeros(1, dtype=torch.int32, device=self.device)
+                c = self._done[key] = torch.zeros(_lib.KV_MAX_BATCH, dtype=torch.int32, device=self.device)
         return c
 
-    def _launch(self, peer, lane, seq, k, v, stride, layer0, layer1, stream, tokens=None):
+    def _launch(self, peer, reqs, stride, layer0, layer1, stream):
+        """One rngd_kv_handoff_batch launch: reqs = [(lane, seq, k, v, tokens), ...] (<= 16)."""
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
-        tokens = peer.S if tokens is None else int(tokens)
-        # the caller may drop its cache right after this call: keep the allocator from handing the
-        # memory to other work before the handoff kernel on `s` has read it
-        k.record_stream(s)
-        v.record_stream(s)
-        flags = peer.flags + lane * peer.L * 8
+        arr = (_lib.KvItem * len(reqs))()
+        moved = 0
+        for i, (lane, seq, k, v, tokens) in enumerate(reqs):
+            tokens = peer.S if tokens is None else int(tokens)
+            # the caller may drop its cache right after this call: keep the allocator from handing
+            # the memory to other work before the handoff kernel on `s` has read it
+            k.record_stream(s)
+            v.record_stream(s)
+            arr[i] = _lib.KvItem(k.data_ptr(), v.data_ptr(), lane, tokens, seq)
+            moved += (layer1 - layer0) * 2 * peer.NKV * tokens * peer.HD * 2
         with torch.cuda.device(self.device):
-            _lib.call("rngd_kv_handoff", _lib.ptr(k), _lib.ptr(v), stride, ctypes.c_void_p(peer.k),
-                      ctypes.c_void_p(peer.v), peer.L, peer.NKV, peer.S, peer.HD, tokens, lane, peer.Bcap, layer0,
-                      layer1, _lib.ptr(self._counter(s)), ctypes.c_void_p(flags), seq, _lib.stream_handle(s))
-        return (layer1 - layer0) * 2 * peer.NKV * tokens * peer.HD * 2
+            _lib.call("rngd_kv_handoff_batch", arr, len(reqs), stride, ctypes.c_void_p(peer.k),
+                      ctypes.c_void_p(peer.v), peer.L, peer.NKV, peer.S, peer.HD, peer.Bcap, layer0, layer1,
+                      _lib.ptr(self._counter(s)), ctypes.c_void_p(peer.flags), _lib.stream_handle(s))
+        return moved
 
     def record(self, seconds, nbytes):
         """Log one transfer under rm-core's measurement names."""

@@ -64,6 +64,56 @@ def test_prompt_positions_only(rx, tokens):
     assert not K[:, 1:].any()
 
 
+def test_push_many_one_launch_per_sixteen_requests():
+    """push_many: 20 requests with different prompt lengths into 20 lanes (two launches of the
+    batched kernel); every lane byte-exact, every lease's flags published."""
+    from rngd_pd.nvlink import NvlinkTransport
+    Lb, Bb, Sb = 2, 20, 128
+    t = NvlinkTransport(0)
+    K = torch.zeros((Lb, Bb, NKV, Sb, HD), dtype=BF, device="cuda")
+    V = torch.zeros_like(K)
+    t.bind_cache(K, V)
+    g = torch.Generator().manual_seed(99)
+    kvs = [torch.randn((Lb, 2, NKV, Sb, HD), generator=g).to(BF).cuda() for _ in range(Bb)]
+    toks = [1 + (17 * b) % Sb for b in range(Bb)]
+    items = []
+    for b in range(Bb):
+        t.reserve(f"q{b}", Bb - 1 - b)
+        items.append((f"q{b}", kvs[b], toks[b]))
+    moved = t.push_many(items)
+    assert moved == sum(Lb * 2 * NKV * n * HD * 2 for n in toks)
+    for b in range(Bb):
+        t.wait(f"q{b}", timeout=5)
+        lane, n = Bb - 1 - b, toks[b]
+        assert torch.equal(_bits(K[:, lane, :, :n]), _bits(kvs[b][:, 0, :, :n]))
+        assert torch.equal(_bits(V[:, lane, :, :n]), _bits(kvs[b][:, 1, :, :n]))
+        assert not K[:, lane, :, n:].any() and not V[:, lane, :, n:].any()
+    t.close()
+
+
+def test_batched_entry_point_rejects_bad_batches(rx):
+    from rngd_pd import _lib
+    t, K, V = rx
+    kv = _kv(21)
+    done = torch.zeros(16, dtype=torch.int32, device="cuda")
+    st = _lib.stream_handle(torch.cuda.current_stream())
+
+    def call(items, n=None):
+        arr = (_lib.KvItem * max(len(items), 1))(*items)
+        return _lib.call("rngd_kv_handoff_batch", arr, len(items) if n is None else n, 2 * NKV * S * HD,
+                         _lib.ptr(K), _lib.ptr(V), L, NKV, S, HD, BCAP, 0, L, _lib.ptr(done),
+                         _lib.ptr(t._cache[2]), st)
+
+    it = lambda lane, tokens=S: _lib.KvItem(kv.data_ptr(), kv[:, 1].data_ptr(), lane, tokens, 1)
+    for bad in ([], [it(0), it(0)], [it(0, 0)], [it(0, S + 1)], [it(BCAP)]):
+        with pytest.raises(_lib.RngdError):
+            call(bad)
+    with pytest.raises(_lib.RngdError):
+        call([it(0)] * 17, n=17)
+    torch.cuda.synchronize()
+    assert not K.any() and not t._cache[2].any()   # nothing was launched
+
+
 def test_layer_blocks_single_layers_and_partial_wait(rx):
     t, K, V = rx
     t.reserve("r", 0)
