@@ -158,7 +158,7 @@ class TcGemm:
     def time(self, reps, stream, trace=None):
         """Mean launch duration (ms) over `reps` back-to-back launches (captured in a CUDA graph so host
         launch cost does not gate short kernels), rotating through the layers so weights are cold.
-        trace: optional int64 device buffer [reps][1024][5] for per-launch CTA timelines."""
+        trace: optional int64 device buffer [reps][1024][8] for per-launch CTA timelines."""
         import torch
         from rngd_pd import _lib
         L = len(self.W)
@@ -521,7 +521,7 @@ def run_micro(args):
     g = TcGemm(W, N, K, dev)
     ms = g.time(args.steps, torch.cuda.current_stream(dev))
     # traced graph of 4 launches: per launch, CTA stamps relative to launch 0's earliest start (us)
-    tr = torch.zeros((4, 1024, 5), dtype=torch.int64, device=dev)
+    tr = torch.zeros((4, 1024, 8), dtype=torch.int64, device=dev)
     g.time(4, torch.cuda.current_stream(dev), trace=tr)
     t = tr.cpu().double()
     t0 = t[0, :, 0][t[0, :, 0] > 0].min()
@@ -529,8 +529,9 @@ def run_micro(args):
     for i in range(4):
         ti = t[i][t[i, :, 0] > 0]
         rel = (ti - t0) / 1e3
-        q = lambda col: [round(float(rel[:, col].min()), 2), round(float(rel[:, col].max()), 2)]
-        timeline.append({"start": q(0), "operand": q(1), "last_tma": q(2), "last_acc": q(3), "end": q(4)})
+        q = lambda col: [round(float(v), 2) for v in (rel[:, col].min(), rel[:, col].median(), rel[:, col].max())]
+        timeline.append({k: q(c) for c, k in enumerate(("start", "operand", "last_tma", "last_arrival", "last_mma",
+                                                         "last_acc", "epi_done", "end"))})
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
@@ -539,7 +540,7 @@ def run_micro(args):
     hbm = peaks.get("hbm_gbs", 6650.0)
     print(json.dumps({"micro": args.micro, "N": N, "K": K, "B": B, "ms": ms, "bytes": g.nbytes,
                       "gbs": g.nbytes / ms / 1e6, "frac_hbm": g.nbytes / ms / 1e6 / hbm,
-                      "pdl": os.environ.get("RNGD_PDL", "1"), "timeline_us_min_max": timeline}), flush=True)
+                      "pdl": os.environ.get("RNGD_PDL", "1"), "timeline_us_min_med_max": timeline}), flush=True)
 
 
 def run_ours(args):

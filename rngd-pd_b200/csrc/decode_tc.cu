@@ -85,13 +85,13 @@ struct GemmArgs {
   unsigned long long* best;
   int V;
   // optional per-CTA timeline (ns, %globaltimer): [cta][start, operand ready, last TMA issued,
-  // last accumulator ready, end]; nullptr = off
+  // last stage arrived, last MMA committed, last accumulator ready, epilogue done, end]; nullptr = off
   unsigned long long* trace;
 };
 
-// smem: stages | barriers (2*STAGES + 4) + tmem slot/flags (64 B) | scale (64 B) | ys | s_red
-constexpr size_t kBarBytes = (2 * STAGES + 4) * 8;
-constexpr size_t kSmemBytes = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + kBarBytes + 64 + 64 +
+// smem: stages | barriers (2*STAGES + 5) + tmem slot/flags (64 B) | scale (64 B) | pos (64 B) | ys | s_red
+constexpr size_t kBarBytes = (2 * STAGES + 5) * 8;
+constexpr size_t kSmemBytes = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + kBarBytes + 64 + 64 + 64 +
                               BM * YS_LD * 4 + 4 * MAXB * 8;
 
 __device__ __forceinline__ uint32_t orderable(float f) {
@@ -116,16 +116,18 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* epi_done = acc_empty + 2;    // the 128 epilogue threads are past their last TMEM read
   uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + kBarBytes);
   int* s_last = (int*)(tmem_slot + 1);
   float* s_scale = (float*)((uint8_t*)full + kBarBytes + 64);  // [16]
-  float* ys = (float*)((uint8_t*)full + kBarBytes + 128);
+  int* s_pos = (int*)((uint8_t*)full + kBarBytes + 128);       // [16]
+  float* ys = (float*)((uint8_t*)full + kBarBytes + 192);
   unsigned long long* s_red = (unsigned long long*)(ys + BM * YS_LD);  // [4][16]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   const long f0 = (long)cta * a.total / G, f1 = (long)(cta + 1) * a.total / G;
-  unsigned long long* tr = a.trace != nullptr ? a.trace + (size_t)cta * 5 : nullptr;
+  unsigned long long* tr = a.trace != nullptr ? a.trace + (size_t)cta * 8 : nullptr;
   if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer();
 
   if (threadIdx.x == 0) {
@@ -137,6 +139,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
     }
+    mbar_init(epi_done, 128);
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
@@ -203,6 +206,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
           ok = mbar_wait(&full[s], ph, ST_MMA_WAIT, &g_status_decode);
           if (!ok) break;
+          if (tr != nullptr && g + 1 == f1) tr[3] = globaltimer();
           tc_fence_after();
           const uint32_t aBase = smem_u32(sA + s * A_BYTES), bBase = smem_u32(sB + s * B_BYTES);
 #pragma unroll
@@ -214,28 +218,60 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
         umma_commit(&acc_full[buf]);
         f = fend;
       }
+      if (tr != nullptr) tr[4] = globaltimer();
+      // TMEM is freed below only after every epilogue thread has read its last accumulator
+      mbar_wait(epi_done, 0u, ST_EPI_WAIT, &g_status_decode);
+      tc_fence_after();
+      if (tr != nullptr) tr[7] = globaltimer();
     }
     __syncwarp();
+    tmem_dealloc(tmem, TMEM_COLS);
   } else {
     // ---------------- epilogue warps 2..5: thread r owns row r of the tile (TMEM lane r)
     grid_dep_wait();
     const int r = ((warp & 3) << 5) | lane;
     const int et = threadIdx.x - 64;  // 0..127 index among the epilogue threads
+    // Per-launch constants, read once with independent loads: a chain of dependent global
+    // loads inside each segment's epilogue was most of the GEMM's tail.  The RMS sums are
+    // added in the same order as ever (t = 0, 1, ...), so the scale is bit-identical.
+    if (EPI != EPI_RESID && a.ss_in != nullptr && et < MAXB) {
+      float ssum = 0.f;
+      for (int t0 = 0; t0 < a.ss_tiles; t0 += 16) {
+        float v16[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) v16[j] = t0 + j < a.ss_tiles ? a.ss_in[(t0 + j) * MAXB + et] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+          if (t0 + j < a.ss_tiles) ssum += v16[j];
+      }
+      s_scale[et] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
+    }
+    if (EPI == EPI_QKV && et < MAXB) s_pos[et] = et < a.B ? a.pos[et] : -1;
+    epi_sync();
     int seg = 0;
     for (long f = f0; f < f1; seg++) {
       const int tile = (int)(f / a.nkb);
       const long tstart = (long)tile * a.nkb;
       const long fend = tstart + a.nkb < f1 ? tstart + a.nkb : f1;
       const int buf = seg & 1;
+      const int n = tile * BM + r;
+      // the residual row and norm weight do not depend on this GEMM: fetch them while the
+      // accumulator is still being computed (only the tile's reducing CTA writes x[.][n])
+      float xo[MAXB];
+      float wn = 0.f;
+      if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+        for (int b = 0; b < MAXB; b++) xo[b] = b < a.B ? a.x[(size_t)b * a.ldx + n] : 0.f;
+        if (a.act_next != nullptr) wn = a.w_next[n];
+      }
       mbar_wait(&acc_full[buf], (uint32_t)(seg >> 1) & 1u, ST_EPI_WAIT, &g_status_decode);
-      if (tr != nullptr && et == 0 && fend == f1) tr[3] = globaltimer();
+      if (tr != nullptr && et == 0 && fend == f1) tr[5] = globaltimer();
       __syncwarp();
       tc_fence_after();
       float v[32];
       tmem_ld_32x32b_x32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * BNC), v);
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
-      const int n = tile * BM + r;
       float y[MAXB];
 #pragma unroll
       for (int b = 0; b < MAXB; b++) y[b] = v[b] + v[MAXB + b];
@@ -258,13 +294,28 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           __threadfence();
 #pragma unroll
           for (int b = 0; b < MAXB; b++) y[b] = 0.f;
-          for (int sl = 0; sl < nseg; sl++) {
-            const float4* src =
+          // pieces summed in K order; two pieces' loads in flight at a time
+          for (int sl = 0; sl < nseg; sl += 2) {
+            const float4* src0 =
                 reinterpret_cast<const float4*>(a.partial + (((size_t)tile * a.maxseg + sl) * BM + r) * MAXB);
+            float4 t0[4], t1[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) t0[j] = __ldcg(src0 + j);
+            const bool two = sl + 1 < nseg;
+            if (two) {
+              const float4* src1 = src0 + (size_t)BM * MAXB / 4;
+#pragma unroll
+              for (int j = 0; j < 4; j++) t1[j] = __ldcg(src1 + j);
+            }
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-              const float4 t4 = __ldcg(src + j);
-              y[4 * j] += t4.x; y[4 * j + 1] += t4.y; y[4 * j + 2] += t4.z; y[4 * j + 3] += t4.w;
+              y[4 * j] += t0[j].x; y[4 * j + 1] += t0[j].y; y[4 * j + 2] += t0[j].z; y[4 * j + 3] += t0[j].w;
+            }
+            if (two) {
+#pragma unroll
+              for (int j = 0; j < 4; j++) {
+                y[4 * j] += t1[j].x; y[4 * j + 1] += t1[j].y; y[4 * j + 2] += t1[j].z; y[4 * j + 3] += t1[j].w;
+              }
             }
           }
           if (et == 0) a.counters[tile] = 0;  // ready for the next launch
@@ -272,35 +323,33 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       }
       if (run) {
         if (EPI != EPI_RESID && a.ss_in != nullptr) {
-          if (et < MAXB) {
-            float ssum = 0.f;
-            for (int t = 0; t < a.ss_tiles; t++) ssum += a.ss_in[t * MAXB + et];
-            s_scale[et] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
-          }
-          epi_sync();
 #pragma unroll
           for (int b = 0; b < MAXB; b++) y[b] *= s_scale[b];
         }
         if constexpr (EPI == EPI_RESID) {
           float xs[MAXB];
-          for (int b = 0; b < a.B; b++) {
-            const float xn = a.x[(size_t)b * a.ldx + n] + y[b];
-            a.x[(size_t)b * a.ldx + n] = xn;
-            xs[b] = xn;
+#pragma unroll
+          for (int b = 0; b < MAXB; b++) {
+            xs[b] = xo[b] + y[b];
+            if (b < a.B) a.x[(size_t)b * a.ldx + n] = xs[b];
           }
           if (a.act_next != nullptr) {
-            const float w = a.w_next[n];
-            for (int b = 0; b < a.B; b++) {
-              const float h = xs[b] * w;
-              const uint16_t hi = f2bf_bits(h);
-              a.act_next[(size_t)b * a.ld_next + n] = hi;
-              a.act_next[(size_t)(MAXB + b) * a.ld_next + n] = f2bf_bits(h - bf2f(hi));
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {
+              if (b < a.B) {
+                const float h = xs[b] * wn;
+                const uint16_t hi = f2bf_bits(h);
+                a.act_next[(size_t)b * a.ld_next + n] = hi;
+                a.act_next[(size_t)(MAXB + b) * a.ld_next + n] = f2bf_bits(h - bf2f(hi));
+              }
             }
             // per-tile sum of squares of the new x, fixed reduction order
-            for (int b = 0; b < a.B; b++) {
-              float sq = xs[b] * xs[b];
-              sq = warp_sum(sq);
-              if (lane == 0) ys[(warp & 3) * YS_LD + b] = sq;
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {
+              if (b < a.B) {
+                const float sq = warp_sum(xs[b] * xs[b]);
+                if (lane == 0) ys[(warp & 3) * YS_LD + b] = sq;
+              }
             }
             epi_sync();
             if (et < a.B) {
@@ -317,22 +366,27 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           const bool lo_half = r < 64;
           const int partner = r ^ 64;
           if (head < a.NH + a.NKV) {
-            for (int b = 0; b < a.B; b++) {
-              const int p = a.pos[b];
-              float sn, cs;
-              sincosf((float)p * a.inv[i], &sn, &cs);
-              const float other = ys[partner * YS_LD + b];
-              const float o = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
-              if (head < a.NH) {
-                a.q[(size_t)b * a.ldq + n] = o;
-              } else if (p >= 0 && p < a.S) {
-                a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o);
+            const float invf = a.inv[i];
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {
+              if (b < a.B) {
+                const int p = s_pos[b];
+                float sn, cs;
+                sincosf((float)p * invf, &sn, &cs);
+                const float other = ys[partner * YS_LD + b];
+                const float o = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
+                if (head < a.NH) {
+                  a.q[(size_t)b * a.ldq + n] = o;
+                } else if (p >= 0 && p < a.S) {
+                  a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o);
+                }
               }
             }
           } else {
-            for (int b = 0; b < a.B; b++) {
-              const int p = a.pos[b];
-              if (p >= 0 && p < a.S)
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {
+              const int p = s_pos[b];
+              if (b < a.B && p >= 0 && p < a.S)
                 a.vc[(((size_t)b * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[b]);
             }
           }
@@ -342,27 +396,33 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           epi_sync();
           if (r < 64) {
             const int fcol = tile * 64 + r;
-            for (int b = 0; b < a.B; b++) {
-              const float g = y[b], u = ys[(r + 64) * YS_LD + b];
-              const float act = g / (1.0f + expf(-g)) * u;
-              const uint16_t hi = f2bf_bits(act);
-              a.act_out[(size_t)b * a.ld_act + fcol] = hi;
-              a.act_out[(size_t)(MAXB + b) * a.ld_act + fcol] = f2bf_bits(act - bf2f(hi));
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {
+              if (b < a.B) {
+                const float g = y[b], u = ys[(r + 64) * YS_LD + b];
+                const float act = g / (1.0f + expf(-g)) * u;
+                const uint16_t hi = f2bf_bits(act);
+                a.act_out[(size_t)b * a.ld_act + fcol] = hi;
+                a.act_out[(size_t)(MAXB + b) * a.ld_act + fcol] = f2bf_bits(act - bf2f(hi));
+              }
             }
           }
         } else if constexpr (EPI == EPI_LOGITS) {
-          for (int b = 0; b < a.B; b++) {
-            unsigned long long key = 0;
-            if (n < a.V) {
-              a.logits[(size_t)b * a.V + n] = y[b];
-              key = ((unsigned long long)orderable(y[b]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
-            }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
-              key = t > key ? t : key;
+          for (int b = 0; b < MAXB; b++) {
+            if (b < a.B) {
+              unsigned long long key = 0;
+              if (n < a.V) {
+                a.logits[(size_t)b * a.V + n] = y[b];
+                key = ((unsigned long long)orderable(y[b]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
+              }
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
+                key = t > key ? t : key;
+              }
+              if (lane == 0) s_red[(warp & 3) * MAXB + b] = key;
             }
-            if (lane == 0) s_red[(warp & 3) * MAXB + b] = key;
           }
           epi_sync();
           if (et < a.B) {
@@ -371,15 +431,14 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
             atomicMax(&a.best[et], k);
           }
         }
-        epi_sync();  // ys / s_scale / s_red are reused by the next segment
+        epi_sync();  // ys / s_red are reused by the next segment
       }
       f = fend;
     }
+    if (tr != nullptr && et == 0) tr[6] = globaltimer();
+    tc_fence_before();
+    mbar_arrive(epi_done);
   }
-  tc_fence_before();
-  __syncthreads();
-  if (tr != nullptr && threadIdx.x == 0) tr[4] = globaltimer();
-  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // -------------------------------------------------------- operand producers
