@@ -158,7 +158,7 @@ class TcGemm:
     def time(self, reps, stream, trace=None):
         """Mean launch duration (ms) over `reps` back-to-back launches (captured in a CUDA graph so host
         launch cost does not gate short kernels), rotating through the layers so weights are cold.
-        trace: optional int64 device buffer [reps][1024][8] for per-launch CTA timelines."""
+        trace: optional int64 device buffer [reps][1024][16] for per-launch CTA timelines."""
         import torch
         from rngd_pd import _lib
         L = len(self.W)
@@ -521,7 +521,7 @@ def run_micro(args):
     g = TcGemm(W, N, K, dev)
     ms = g.time(args.steps, torch.cuda.current_stream(dev))
     # traced graph of 4 launches: per launch, CTA stamps relative to launch 0's earliest start (us)
-    tr = torch.zeros((4, 1024, 8), dtype=torch.int64, device=dev)
+    tr = torch.zeros((4, 1024, 16), dtype=torch.int64, device=dev)
     g.time(4, torch.cuda.current_stream(dev), trace=tr)
     t = tr.cpu().double()
     t0 = t[0, :, 0][t[0, :, 0] > 0].min()

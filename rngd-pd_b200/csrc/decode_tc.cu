@@ -51,6 +51,7 @@ constexpr int STAGES = 5;
 constexpr int YS_LD = 17;
 constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int TMEM_COLS = 64;          // two 32-column accumulators
+constexpr int kRedBatch = 6;           // split-tile pieces whose partials are loaded together
 
 enum Epi : int { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
 
@@ -84,8 +85,10 @@ struct GemmArgs {
   float* logits;
   unsigned long long* best;
   int V;
-  // optional per-CTA timeline (ns, %globaltimer): [cta][start, operand ready, last TMA issued,
-  // last stage arrived, last MMA committed, last accumulator ready, epilogue done, end]; nullptr = off
+  // optional per-CTA timeline (ns, %globaltimer), 16 entries per CTA: start, operand ready, last
+  // TMA issued, last stage arrived, last MMA committed, last accumulator ready, epilogue done,
+  // end; then for the last segment: accumulator read, split-tile count done, partials summed,
+  // epilogue stores issued, segment done; nullptr = off
   unsigned long long* trace;
 };
 
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   const long f0 = (long)cta * a.total / G, f1 = (long)(cta + 1) * a.total / G;
-  unsigned long long* tr = a.trace != nullptr ? a.trace + (size_t)cta * 8 : nullptr;
+  unsigned long long* tr = a.trace != nullptr ? a.trace + (size_t)cta * 16 : nullptr;
   if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer();
 
   if (threadIdx.x == 0) {
@@ -184,6 +187,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       }
       if (tr != nullptr) tr[2] = globaltimer();
       grid_dep_launch();  // all weight reads issued: the next kernel may start prefetching
+
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -272,6 +276,8 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       tmem_ld_32x32b_x32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * BNC), v);
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
+      const bool tlast = tr != nullptr && et == 0 && fend == f1;
+      if (tlast) tr[8] = globaltimer();
       float y[MAXB];
 #pragma unroll
       for (int b = 0; b < MAXB; b++) y[b] = v[b] + v[MAXB + b];
@@ -285,40 +291,51 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
 #pragma unroll
         for (int j = 0; j < 4; j++)
           __stcg(dst + j, make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]));
-        __threadfence();
+        // The barrier orders every epilogue thread's partial stores before thread 0's counter
+        // update, whose release (gpu scope) publishes them; the last arriver's acquire on the
+        // same update, followed by the barrier, orders its threads' partial reads after all
+        // pieces were written.  No full fence on either side.
         epi_sync();
-        if (et == 0) *s_last = (atomicAdd(&a.counters[tile], 1) == nseg - 1);
+        if (et == 0) {
+          int old;
+          asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                       : "=r"(old)
+                       : "l"(a.counters + tile)
+                       : "memory");
+          *s_last = (old == nseg - 1);
+        }
         epi_sync();
         run = *s_last != 0;
+        if (tlast) tr[9] = globaltimer();
         if (run) {
-          __threadfence();
 #pragma unroll
           for (int b = 0; b < MAXB; b++) y[b] = 0.f;
-          // pieces summed in K order; two pieces' loads in flight at a time
-          for (int sl = 0; sl < nseg; sl += 2) {
-            const float4* src0 =
-                reinterpret_cast<const float4*>(a.partial + (((size_t)tile * a.maxseg + sl) * BM + r) * MAXB);
-            float4 t0[4], t1[4];
+          // pieces summed in K order; every piece's loads issued before the first add (one L2
+          // round trip for up to kRedBatch pieces instead of one per piece)
+          for (int s0 = 0; s0 < nseg; s0 += kRedBatch) {
+            float4 tp[kRedBatch][4];
 #pragma unroll
-            for (int j = 0; j < 4; j++) t0[j] = __ldcg(src0 + j);
-            const bool two = sl + 1 < nseg;
-            if (two) {
-              const float4* src1 = src0 + (size_t)BM * MAXB / 4;
+            for (int q = 0; q < kRedBatch; q++) {
+              if (s0 + q < nseg) {
+                const float4* src = reinterpret_cast<const float4*>(
+                    a.partial + (((size_t)tile * a.maxseg + s0 + q) * BM + r) * MAXB);
 #pragma unroll
-              for (int j = 0; j < 4; j++) t1[j] = __ldcg(src1 + j);
+                for (int j = 0; j < 4; j++) tp[q][j] = __ldcg(src + j);
+              }
             }
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-              y[4 * j] += t0[j].x; y[4 * j + 1] += t0[j].y; y[4 * j + 2] += t0[j].z; y[4 * j + 3] += t0[j].w;
-            }
-            if (two) {
+            for (int q = 0; q < kRedBatch; q++) {
+              if (s0 + q < nseg) {
 #pragma unroll
-              for (int j = 0; j < 4; j++) {
-                y[4 * j] += t1[j].x; y[4 * j + 1] += t1[j].y; y[4 * j + 2] += t1[j].z; y[4 * j + 3] += t1[j].w;
+                for (int j = 0; j < 4; j++) {
+                  y[4 * j] += tp[q][j].x; y[4 * j + 1] += tp[q][j].y;
+                  y[4 * j + 2] += tp[q][j].z; y[4 * j + 3] += tp[q][j].w;
+                }
               }
             }
           }
           if (et == 0) a.counters[tile] = 0;  // ready for the next launch
+          if (tlast) tr[10] = globaltimer();
         }
       }
       if (run) {
@@ -327,6 +344,8 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           for (int b = 0; b < MAXB; b++) y[b] *= s_scale[b];
         }
         if constexpr (EPI == EPI_RESID) {
+          // All 16 streams are computed unconditionally (streams >= B hold zeros) so the
+          // per-stream chains interleave; only the stores are predicated on B.
           float xs[MAXB];
 #pragma unroll
           for (int b = 0; b < MAXB; b++) {
@@ -336,20 +355,27 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           if (a.act_next != nullptr) {
 #pragma unroll
             for (int b = 0; b < MAXB; b++) {
+              const float h = xs[b] * wn;
+              const uint16_t hi = f2bf_bits(h);
+              const uint16_t lo = f2bf_bits(h - bf2f(hi));
               if (b < a.B) {
-                const float h = xs[b] * wn;
-                const uint16_t hi = f2bf_bits(h);
                 a.act_next[(size_t)b * a.ld_next + n] = hi;
-                a.act_next[(size_t)(MAXB + b) * a.ld_next + n] = f2bf_bits(h - bf2f(hi));
+                a.act_next[(size_t)(MAXB + b) * a.ld_next + n] = lo;
               }
             }
-            // per-tile sum of squares of the new x, fixed reduction order
+            // per-tile sum of squares of the new x: the same xor butterfly for every stream,
+            // 16 of them interleaved
+            float sq[MAXB];
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) {
-              if (b < a.B) {
-                const float sq = warp_sum(xs[b] * xs[b]);
-                if (lane == 0) ys[(warp & 3) * YS_LD + b] = sq;
-              }
+            for (int b = 0; b < MAXB; b++) sq[b] = xs[b] * xs[b];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+              for (int b = 0; b < MAXB; b++) sq[b] += __shfl_xor_sync(0xffffffffu, sq[b], o);
+            }
+            if (lane == 0) {
+#pragma unroll
+              for (int b = 0; b < MAXB; b++) ys[(warp & 3) * YS_LD + b] = sq[b];
             }
             epi_sync();
             if (et < a.B) {
@@ -367,18 +393,22 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           const int partner = r ^ 64;
           if (head < a.NH + a.NKV) {
             const float invf = a.inv[i];
+            float o[MAXB];
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {  // all streams (pos -1 past B), stores predicated
+              float sn, cs;
+              sincosf((float)s_pos[b] * invf, &sn, &cs);
+              const float other = ys[partner * YS_LD + b];
+              o[b] = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
+            }
 #pragma unroll
             for (int b = 0; b < MAXB; b++) {
+              const int p = s_pos[b];
               if (b < a.B) {
-                const int p = s_pos[b];
-                float sn, cs;
-                sincosf((float)p * invf, &sn, &cs);
-                const float other = ys[partner * YS_LD + b];
-                const float o = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
                 if (head < a.NH) {
-                  a.q[(size_t)b * a.ldq + n] = o;
+                  a.q[(size_t)b * a.ldq + n] = o[b];
                 } else if (p >= 0 && p < a.S) {
-                  a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o);
+                  a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o[b]);
                 }
               }
             }
@@ -398,31 +428,37 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
             const int fcol = tile * 64 + r;
 #pragma unroll
             for (int b = 0; b < MAXB; b++) {
+              const float g = y[b], u = ys[(r + 64) * YS_LD + b];
+              const float act = g / (1.0f + expf(-g)) * u;
+              const uint16_t hi = f2bf_bits(act);
+              const uint16_t lo = f2bf_bits(act - bf2f(hi));
               if (b < a.B) {
-                const float g = y[b], u = ys[(r + 64) * YS_LD + b];
-                const float act = g / (1.0f + expf(-g)) * u;
-                const uint16_t hi = f2bf_bits(act);
                 a.act_out[(size_t)b * a.ld_act + fcol] = hi;
-                a.act_out[(size_t)(MAXB + b) * a.ld_act + fcol] = f2bf_bits(act - bf2f(hi));
+                a.act_out[(size_t)(MAXB + b) * a.ld_act + fcol] = lo;
               }
             }
           }
         } else if constexpr (EPI == EPI_LOGITS) {
+          unsigned long long key[MAXB];
 #pragma unroll
           for (int b = 0; b < MAXB; b++) {
-            if (b < a.B) {
-              unsigned long long key = 0;
-              if (n < a.V) {
-                a.logits[(size_t)b * a.V + n] = y[b];
-                key = ((unsigned long long)orderable(y[b]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
-              }
-#pragma unroll
-              for (int o = 16; o > 0; o >>= 1) {
-                const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
-                key = t > key ? t : key;
-              }
-              if (lane == 0) s_red[(warp & 3) * MAXB + b] = key;
+            key[b] = 0;
+            if (n < a.V) {
+              if (b < a.B) a.logits[(size_t)b * a.V + n] = y[b];
+              key[b] = ((unsigned long long)orderable(y[b]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
             }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {
+              const unsigned long long t = __shfl_xor_sync(0xffffffffu, key[b], o);
+              key[b] = t > key[b] ? t : key[b];
+            }
+          }
+          if (lane == 0) {
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) s_red[(warp & 3) * MAXB + b] = key[b];
           }
           epi_sync();
           if (et < a.B) {
@@ -431,7 +467,9 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
             atomicMax(&a.best[et], k);
           }
         }
+        if (tlast) tr[11] = globaltimer();
         epi_sync();  // ys / s_red are reused by the next segment
+        if (tlast) tr[12] = globaltimer();
       }
       f = fend;
     }
@@ -600,6 +638,19 @@ static int max_segments(int N, int K, int grid) {
   return mx;
 }
 
+// set by rngd_trace_decode_gemms (diagnostics): later GEMM launches without a trace of their
+// own record their CTA timelines into consecutive [1024][8] blocks until g_seq_left runs out
+static unsigned long long* g_seq = nullptr;
+static int g_seq_left = 0;
+
+static void seq_trace(GemmArgs* a) {
+  if (a->trace == nullptr && g_seq != nullptr && g_seq_left > 0) {
+    a->trace = g_seq;
+    g_seq += 1024 * 16;
+    g_seq_left--;
+  }
+}
+
 template <int EPI>
 static int launch_skgemm(const void* W, int L, int layer, int N, int K, const void* act, int ld_act_in, GemmArgs a,
                          cudaStream_t s) {
@@ -618,6 +669,7 @@ static int launch_skgemm(const void* W, int L, int layer, int N, int K, const vo
   a.layer = layer;
   RNGD_REQUIRE(a.total >= grid, "decode GEMM: %d K blocks cannot feed %d CTAs", a.total, grid);
   RNGD_REQUIRE(a.maxseg == 1 || (a.partial && a.counters), "decode GEMM: split tiles need partial/counters");
+  seq_trace(&a);
   static std::atomic<unsigned long long> attr_set{0};  // one per EPI instantiation
   RNGD_TRY(set_smem_limit_once((const void*)skgemm_kernel<EPI>, (int)kSmemBytes, &attr_set,
                                "cudaFuncSetAttribute(skgemm)"));
@@ -691,6 +743,14 @@ extern "C" int rngd_tc_gemv_trace(uint64_t* trace) {
   g_trace = (unsigned long long*)trace;
   return RNGD_OK;
 }
+
+extern "C" int rngd_trace_decode_gemms(uint64_t* trace, int launches) {
+  RNGD_REQUIRE(launches >= 0, "trace_decode_gemms: negative launch count");
+  g_seq = (unsigned long long*)trace;
+  g_seq_left = trace != nullptr ? launches : 0;
+  return RNGD_OK;
+}
+
 
 extern "C" int rngd_tc_gemv(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy,
                             void* act, float* partial, int32_t* counters, int prep, rngd_stream_t stream) {

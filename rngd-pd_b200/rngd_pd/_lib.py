@@ -86,6 +86,7 @@ _sig("rngd_tc_gemv", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.
      _vp, _vp, ctypes.c_int, _vp)
 _sig("rngd_tc_gemv_workspace", ctypes.c_int, ctypes.c_int, _szp, _szp)
 _sig("rngd_tc_gemv_trace", _vp)
+_sig("rngd_trace_decode_gemms", _vp, ctypes.c_int)
 _PIOP = ctypes.POINTER(PrefillIO)
 _sig("rngd_prefill_workspace", _MP, ctypes.c_int, _szp, _szp)
 _sig("rngd_prefill_embed", _MP, _PIOP, _vp)
