@@ -57,16 +57,19 @@ __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u <<
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
 __device__ __forceinline__ float bf2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
 
-// Round-to-nearest-even fp32 -> bf16 bits (finite inputs), the same integer
-// rule the oracle uses, so host and device roundings agree bit for bit.
+// Round-to-nearest-even fp32 -> bf16 bits (finite inputs).  The host uses the same
+// integer rule as the oracle; the device uses the hardware RNE convert, which gives
+// the same bits for every finite input, so host and device roundings agree.
 __host__ __device__ __forceinline__ uint16_t f2bf_bits(float f) {
 #ifdef __CUDA_ARCH__
-  uint32_t u = __float_as_uint(f);
+  uint16_t r;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(f));
+  return r;
 #else
   uint32_t u;
   memcpy(&u, &f, 4);
-#endif
   return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+#endif
 }
 
 // 8 bf16 (one 16-byte vector) -> 8 fp32

@@ -92,10 +92,12 @@ struct GemmArgs {
   unsigned long long* trace;
 };
 
-// smem: stages | barriers (2*STAGES + 5) + tmem slot/flags (64 B) | scale (64 B) | pos (64 B) | ys | s_red
+// smem: stages | barriers (2*STAGES + 5) + tmem slot/flags (64 B) | scale (64 B) | pos (64 B) | ys | s_red |
+// rope (QKV: cos/sin of every stream's position for the 64 frequencies)
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8;
+constexpr int kRopeFreqs = 64;  // HD / 2
 constexpr size_t kSmemBytes = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + kBarBytes + 64 + 64 + 64 +
-                              BM * YS_LD * 4 + 4 * MAXB * 8;
+                              BM * YS_LD * 4 + 4 * MAXB * 8 + MAXB * kRopeFreqs * 8;
 
 __device__ __forceinline__ uint32_t orderable(float f) {
   uint32_t u = __float_as_uint(f);
@@ -126,6 +128,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
   int* s_pos = (int*)((uint8_t*)full + kBarBytes + 128);       // [16]
   float* ys = (float*)((uint8_t*)full + kBarBytes + 192);
   unsigned long long* s_red = (unsigned long long*)(ys + BM * YS_LD);  // [4][16]
+  float2* s_rope = (float2*)(s_red + 4 * MAXB);                        // [16][64] (cos, sin)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -250,7 +253,19 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       }
       s_scale[et] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
     }
-    if (EPI == EPI_QKV && et < MAXB) s_pos[et] = et < a.B ? a.pos[et] : -1;
+    if (EPI == EPI_QKV) {
+      if (et < MAXB) s_pos[et] = et < a.B ? a.pos[et] : -1;
+      // RoPE factors of this step, computed while the weights stream (they used to be
+      // computed per segment, on the tail of the GEMM): entry [b][i] = (cos, sin) of pos[b] * inv[i]
+#pragma unroll
+      for (int k = 0; k < MAXB * kRopeFreqs / 128; k++) {
+        const int idx = et + 128 * k, b = idx / kRopeFreqs, i = idx % kRopeFreqs;
+        const int p = b < a.B ? a.pos[b] : -1;
+        float sn, cs;
+        sincosf((float)p * a.inv[i], &sn, &cs);
+        s_rope[idx] = make_float2(cs, sn);
+      }
+    }
     epi_sync();
     int seg = 0;
     for (long f = f0; f < f1; seg++) {
@@ -352,6 +367,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
             xs[b] = xo[b] + y[b];
             if (b < a.B) a.x[(size_t)b * a.ldx + n] = xs[b];
           }
+          if (tlast) tr[13] = globaltimer();
           if (a.act_next != nullptr) {
 #pragma unroll
             for (int b = 0; b < MAXB; b++) {
@@ -363,6 +379,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
                 a.act_next[(size_t)(MAXB + b) * a.ld_next + n] = lo;
               }
             }
+            if (tlast) tr[14] = globaltimer();
             // per-tile sum of squares of the new x: the same xor butterfly for every stream,
             // 16 of them interleaved
             float sq[MAXB];
@@ -377,6 +394,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
 #pragma unroll
               for (int b = 0; b < MAXB; b++) ys[(warp & 3) * YS_LD + b] = sq[b];
             }
+            if (tlast) tr[15] = globaltimer();
             epi_sync();
             if (et < a.B) {
               const float t4 = (ys[0 * YS_LD + et] + ys[1 * YS_LD + et]) + (ys[2 * YS_LD + et] + ys[3 * YS_LD + et]);
@@ -392,15 +410,16 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           const bool lo_half = r < 64;
           const int partner = r ^ 64;
           if (head < a.NH + a.NKV) {
-            const float invf = a.inv[i];
+            if (tlast) tr[13] = globaltimer();
             float o[MAXB];
 #pragma unroll
             for (int b = 0; b < MAXB; b++) {  // all streams (pos -1 past B), stores predicated
-              float sn, cs;
-              sincosf((float)s_pos[b] * invf, &sn, &cs);
+              const float2 cssn = s_rope[b * kRopeFreqs + i];
+              const float cs = cssn.x, sn = cssn.y;
               const float other = ys[partner * YS_LD + b];
               o[b] = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
             }
+            if (tlast) tr[14] = globaltimer();
 #pragma unroll
             for (int b = 0; b < MAXB; b++) {
               const int p = s_pos[b];
