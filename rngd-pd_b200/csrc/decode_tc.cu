@@ -92,12 +92,10 @@ struct GemmArgs {
   unsigned long long* trace;
 };
 
-// smem: stages | barriers (2*STAGES + 5) + tmem slot/flags (64 B) | scale (64 B) | pos (64 B) | ys | s_red |
-// rope (QKV: cos/sin of every stream's position for the 64 frequencies)
+// smem: stages | barriers (2*STAGES + 5) + tmem slot/flags (64 B) | scale (64 B) | pos (64 B) | ys | s_red
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8;
-constexpr int kRopeFreqs = 64;  // HD / 2
 constexpr size_t kSmemBytes = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + kBarBytes + 64 + 64 + 64 +
-                              BM * YS_LD * 4 + 4 * MAXB * 8 + MAXB * kRopeFreqs * 8;
+                              BM * YS_LD * 4 + 4 * MAXB * 8;
 
 __device__ __forceinline__ uint32_t orderable(float f) {
   uint32_t u = __float_as_uint(f);
@@ -128,7 +126,6 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
   int* s_pos = (int*)((uint8_t*)full + kBarBytes + 128);       // [16]
   float* ys = (float*)((uint8_t*)full + kBarBytes + 192);
   unsigned long long* s_red = (unsigned long long*)(ys + BM * YS_LD);  // [4][16]
-  float2* s_rope = (float2*)(s_red + 4 * MAXB);                        // [16][64] (cos, sin)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -253,17 +250,16 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       }
       s_scale[et] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
     }
-    if (EPI == EPI_QKV) {
+    // RoPE factors of this step for this thread's frequency (r mod 64), computed while the
+    // weights stream rather than on the GEMM's tail: (cos, sin) of pos[b] * inv[r mod 64]
+    float rcos[MAXB], rsin[MAXB];
+    if constexpr (EPI == EPI_QKV) {
       if (et < MAXB) s_pos[et] = et < a.B ? a.pos[et] : -1;
-      // RoPE factors of this step, computed while the weights stream (they used to be
-      // computed per segment, on the tail of the GEMM): entry [b][i] = (cos, sin) of pos[b] * inv[i]
+      const float invf = a.inv[r & 63];
 #pragma unroll
-      for (int k = 0; k < MAXB * kRopeFreqs / 128; k++) {
-        const int idx = et + 128 * k, b = idx / kRopeFreqs, i = idx % kRopeFreqs;
+      for (int b = 0; b < MAXB; b++) {
         const int p = b < a.B ? a.pos[b] : -1;
-        float sn, cs;
-        sincosf((float)p * a.inv[i], &sn, &cs);
-        s_rope[idx] = make_float2(cs, sn);
+        sincosf((float)p * invf, &rsin[b], &rcos[b]);
       }
     }
     epi_sync();
@@ -406,7 +402,6 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
           for (int b = 0; b < MAXB; b++) ys[r * YS_LD + b] = y[b];
           epi_sync();
           const int head = tile;  // one 128-row tile = one head
-          const int i = r & 63;
           const bool lo_half = r < 64;
           const int partner = r ^ 64;
           if (head < a.NH + a.NKV) {
@@ -414,8 +409,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
             float o[MAXB];
 #pragma unroll
             for (int b = 0; b < MAXB; b++) {  // all streams (pos -1 past B), stores predicated
-              const float2 cssn = s_rope[b * kRopeFreqs + i];
-              const float cs = cssn.x, sn = cssn.y;
+              const float cs = rcos[b], sn = rsin[b];
               const float other = ys[partner * YS_LD + b];
               o[b] = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
             }
