@@ -40,7 +40,7 @@ struct PCfg {
   static constexpr int STAGES = NT == 256 ? 2 : 4;
   static constexpr int TMEM_COLS = 2 * NT;        // double-buffered accumulator
   static constexpr size_t BAR_BYTES = (2 * STAGES + 4) * 8;
-  static constexpr size_t SMEM = 1024 + STAGES * STAGE + BAR_BYTES + 64 + 128 + PBM * P_YS_LD * 4 + 4 * 32 * 4;
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE + BAR_BYTES + 64 + NT * 4 + PBM * P_YS_LD * 4 + 4 * 32 * 4;
 };
 
 enum PEpi : int { PEPI_QKV = 0, PEPI_RESID = 1, PEPI_SWIGLU = 2 };
@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + Cfg::BAR_BYTES);
   int* s_last = (int*)(tmem_slot + 1);
-  float* s_scale = (float*)((uint8_t*)full + Cfg::BAR_BYTES + 64);   // [32]
-  float* ys = (float*)((uint8_t*)full + Cfg::BAR_BYTES + 64 + 128);  // [128][33]
+  float* s_scale = (float*)((uint8_t*)full + Cfg::BAR_BYTES + 64);   // [NT] RMS scale of the unit's tokens
+  float* ys = s_scale + NT;                                          // [128][33]
   float* s_red = ys + PBM * P_YS_LD;                                  // [4][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -203,6 +203,24 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       const int mt = (int)(u / a.ntok), jt = (int)(u % a.ntok);
       const int n = mt * PBM + r;
       const int buf = seg & 1;
+      // RMS scales of this unit's NT tokens, read while the accumulator is still being built:
+      // token jt*NT + i's sum over the ss tiles in tile order, loads batched 16 at a time
+      if (EPI != PEPI_RESID && a.ss_in != nullptr) {
+        for (int i = et; i < NT; i += 128) {
+          const int tok = jt * NT + i;
+          float ssum = 0.f;
+          for (int t0 = 0; t0 < a.ss_tiles; t0 += 16) {
+            float v16[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) v16[j] = t0 + j < a.ss_tiles ? a.ss_in[(size_t)(t0 + j) * a.C + tok] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+              if (t0 + j < a.ss_tiles) ssum += v16[j];
+          }
+          s_scale[i] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
+        }
+        pf_sync();
+      }
       mbar_wait(&acc_full[buf], (uint32_t)(seg >> 1) & 1u, ST_EPI_WAIT, &g_status_prefill);
       __syncwarp();
       tc_fence_after();
@@ -244,21 +262,17 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
           }
           const int t0 = jt * NT + cc * 32;  // first token of the chunk
           if (EPI != PEPI_RESID && a.ss_in != nullptr) {
-            if (et < 32) {
-              float ssum = 0.f;
-              for (int t = 0; t < a.ss_tiles; t++) ssum += a.ss_in[(size_t)t * a.C + t0 + et];
-              s_scale[et] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
-            }
-            pf_sync();
 #pragma unroll
-            for (int i = 0; i < 32; i++) y[i] *= s_scale[i];
+            for (int i = 0; i < 32; i++) y[i] *= s_scale[cc * 32 + i];
           }
           if constexpr (EPI == PEPI_RESID) {
+            float xo[32];  // all 32 residual loads in flight before the first store
+#pragma unroll
+            for (int i = 0; i < 32; i++) xo[i] = a.x[(size_t)(t0 + i) * a.ldx + n];
 #pragma unroll
             for (int i = 0; i < 32; i++) {
-              float* xp = a.x + (size_t)(t0 + i) * a.ldx + n;
-              const float xn = *xp + y[i];
-              *xp = xn;
+              const float xn = xo[i] + y[i];
+              a.x[(size_t)(t0 + i) * a.ldx + n] = xn;
               y[i] = xn;
             }
             if (a.act_next != nullptr) {
@@ -290,6 +304,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
             const int partner = r ^ 64;
             if (head < a.NH + a.NKV) {
               const float invf = a.inv[idx];
+#pragma unroll 8
               for (int i = 0; i < 32; i++) {
                 const int t = t0 + i;
                 float sn, cs;
@@ -304,6 +319,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
               }
             } else {
               const int vh = head - a.NH - a.NKV;
+#pragma unroll 8
               for (int i = 0; i < 32; i++) {
                 const int t = t0 + i;
                 if (t < a.P) a.kv[(((size_t)(a.NKV + vh)) * a.S + t) * 128 + r] = f2bf_bits(y[i]);
@@ -315,6 +331,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
             pf_sync();
             if (r < 64) {
               const int fcol = mt * 64 + r;
+#pragma unroll 8
               for (int i = 0; i < 32; i++) {
                 const float g = y[i], uu = ys[(r + 64) * P_YS_LD + i];
                 const float act = g / (1.0f + expf(-g)) * uu;
@@ -484,13 +501,14 @@ static int launch_pf(const void* W, int L, int layer, int N, int K, const void* 
 template <int EPI>
 static int launch_pf_any(const void* W, int L, int layer, int N, int K, const void* act, int ld, PArgs a,
                          cudaStream_t s) {
-  if (a.C % 256 == 0) return launch_pf<EPI, 256>(W, L, layer, N, K, act, ld, a, s);
+  // 128-token tiles: a 48 KB stage (weights + hi + lo) leaves room for 4 stages in flight,
+  // which measured faster than 256-token tiles with 2 stages at every bucket width
   return launch_pf<EPI, 128>(W, L, layer, N, K, act, ld, a, s);
 }
 
 // scratch of one GEMM shape
 static void pf_shape_ws(int N, int K, int C, size_t* pf, size_t* ct) {
-  const int NT = C % 256 == 0 ? 256 : 128;
+  const int NT = 128;
   const long units = (long)(N / PBM) * (C / NT), nkb = K / PBK;
   const int ms = pf_maxseg(units, nkb, pf_grid(units * nkb));
   *pf = ms > 1 ? (size_t)units * ms * NT * PBM : 0;
