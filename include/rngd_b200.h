@@ -143,10 +143,10 @@ typedef struct rngd_prefill_io {
   void* kv;             /* bf16 [kv_layers][2][NKV][S][HD], first layer = layer0 of the call */
   const int32_t* toks;  /* device [C] token ids (the prompt, padded) */
   float* x;             /* fp32 [C][H] residual stream */
-  float* q;             /* fp32 [C][NH*HD] rotated queries */
+  float* q;             /* C*NH*HD*4 bytes: the rotated queries as bf16 hi/lo rows [2][C][NH*HD] */
   void* act;            /* bf16 [2C][max(H, NH*HD)] operand of x * norm weight */
   void* act_o;          /* bf16 [2C][NH*HD] attention-output operand */
-  void* act2;           /* bf16 [2C][M] down-projection operand */
+  void* act2;           /* bf16 [2C][M] down-projection operand (also V^T scratch during attention) */
   float* ss;            /* fp32 [H/128][C] per-128-column sums of squares of x */
   float* partial;       /* fp32 split-K scratch, rngd_prefill_workspace() floats */
   int32_t* counters;    /* int32 tile counters, rngd_prefill_workspace() entries, zeroed once */

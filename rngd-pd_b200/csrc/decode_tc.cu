@@ -623,6 +623,21 @@ int get_operand_map(const void* act, int K, int ld, int rows, int box_rows, CUte
   return RNGD_OK;
 }
 
+int get_map3_bf16(const void* base, const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                  CUtensorMap* out) {
+  MapKey key{base, dims[0] | (dims[1] << 32), dims[2] | ((uint64_t)box[0] << 32) | ((uint64_t)box[1] << 48),
+             (uint64_t)box[2] | (strides_bytes[0] << 8) | (0x3Dull << 56)};
+  std::lock_guard<std::mutex> g(g_map_mu);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return RNGD_OK;
+  }
+  RNGD_TRY(encode_tmap_bf16(out, base, 3, dims, strides_bytes, box));
+  g_maps[key] = *out;
+  return RNGD_OK;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {

@@ -58,6 +58,7 @@ struct PArgs {
   float* q;
   int ldq;
   uint16_t* kv;  // this layer's [2][NKV][S][HD]
+  uint16_t* vt;  // V^T scratch [NKV][HD][C] for the attention (the act2 buffer, idle until the MLP)
   int NH, NKV, S;
   // RESID
   float* x;
@@ -311,19 +312,30 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
                 sincosf((float)t * invf, &sn, &cs);
                 const float other = ys[partner * P_YS_LD + i];
                 const float o = lo_half ? y[i] * cs - other * sn : y[i] * cs + other * sn;
-                if (head < a.NH) {
-                  a.q[(size_t)t * a.ldq + n] = o;
+                if (head < a.NH) {  // q as the attention's hi/lo bf16 operand [2][C][NH*HD]
+                  uint16_t* qb = reinterpret_cast<uint16_t*>(a.q);
+                  const uint16_t hi = f2bf_bits(o);
+                  qb[(size_t)t * a.ldq + n] = hi;
+                  qb[(size_t)(a.C + t) * a.ldq + n] = f2bf_bits(o - bf2f(hi));
                 } else if (t < a.P) {
                   a.kv[(((size_t)(head - a.NH)) * a.S + t) * 128 + r] = f2bf_bits(o);
                 }
               }
             } else {
               const int vh = head - a.NH - a.NKV;
-#pragma unroll 8
-              for (int i = 0; i < 32; i++) {
+              uint32_t packed[16];  // this dimension's 32 tokens for V^T (zero past the prompt)
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
                 const int t = t0 + i;
-                if (t < a.P) a.kv[(((size_t)(a.NKV + vh)) * a.S + t) * 128 + r] = f2bf_bits(y[i]);
+                const uint16_t v0 = t < a.P ? f2bf_bits(y[i]) : 0, v1 = t + 1 < a.P ? f2bf_bits(y[i + 1]) : 0;
+                packed[i / 2] = (uint32_t)v0 | ((uint32_t)v1 << 16);
+                if (t < a.P) a.kv[(((size_t)(a.NKV + vh)) * a.S + t) * 128 + r] = v0;
+                if (t + 1 < a.P) a.kv[(((size_t)(a.NKV + vh)) * a.S + t + 1) * 128 + r] = v1;
               }
+              uint4* vrow = reinterpret_cast<uint4*>(a.vt + ((size_t)vh * 128 + r) * a.C + t0);
+#pragma unroll
+              for (int k4 = 0; k4 < 4; k4++)
+                vrow[k4] = make_uint4(packed[4 * k4], packed[4 * k4 + 1], packed[4 * k4 + 2], packed[4 * k4 + 3]);
             }
           } else if constexpr (EPI == PEPI_SWIGLU) {
 #pragma unroll
@@ -358,104 +370,215 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
   if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
 }
 
-// ------------------------------------------------------- causal attention
+// ------------------------------------------------- causal attention on tcgen05
 // Within-prompt causal attention (kernels/prefill_full.py:64-70 with the mask of
-// prefill_full.py:188 / cpu_layer_p :119): query t attends keys 0..t.  One CTA =
-// (32-query tile, query head); 4 threads per query row, 32 dims each.  Keys and
-// values are read from the bf16 cache this layer just emitted (the values decode
-// will see), staged 32 keys at a time into padded shared memory with cp.async.
-// fp32 online softmax; the result goes out as the hi/lo operand of the O GEMM.
-constexpr int kPQT = 32, kPKC = 32, kPRow = 272;
+// prefill_full.py:188 / cpu_layer_p :119): query t attends keys 0..t.
+//
+// One CTA = (32-query tile, kv head).  The 4 query heads of the kv head are packed into
+// the MMA's M = 128 rows (row r = token qt*32 + r/4, head 4*kvh + r%4), so K and V are
+// read once per group.  Per 128-key chunk:
+//   S = Q K^T           tcgen05, M=128, N=128 keys, K=HD: Q enters as bf16 hi + lo rows
+//                       (two MMAs into one TMEM accumulator: fp32-level q), K as bf16;
+//   softmax             epilogue warps, thread r = row r: scale, causal mask, running max /
+//                       sum (fp32), P = exp(S - m) written to shared memory as bf16 hi + lo
+//                       in the 128-byte-swizzled K-major layout TMA would produce;
+//   O_c = P V           tcgen05, M=128, N=HD, K=128 keys, B = V^T (written by the QKV
+//                       epilogue into a scratch buffer so that it is K-major too);
+//   o = o * corr + O_c  registers, fp32.
+// Operands arrive by TMA: Q hi/lo boxes (64 d, 4 heads, 32 tokens), K boxes (64 d, 128
+// keys) from the layer's cache, V^T boxes (64 keys, 128 d).  The output o / l goes out as
+// the hi/lo bf16 operand of the O projection.
+constexpr int kAQ = 32;               // query tokens per CTA (x 4 heads = 128 MMA rows)
+constexpr int kAK = 128;              // keys per chunk
+constexpr int kABox = 16384;          // one 128-row x 128-byte swizzled box
+constexpr size_t kAttnTcSmem = 1024 + 12 * (size_t)kABox + 8 * 8 + 64;
 
-__device__ __forceinline__ void pf_cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
+__global__ void __launch_bounds__(192, 1) pf_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                            const __grid_constant__ CUtensorMap tmK,
+                                                            const __grid_constant__ CUtensorMap tmV, int C,
+                                                            uint16_t* __restrict__ act_o, int ld_act) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = base;                  // [hi d0-63, hi d64-127, lo d0-63, lo d64-127]
+  uint8_t* sK = sQ + 4 * kABox;        // [d0-63, d64-127]
+  uint8_t* sV = sK + 2 * kABox;        // V^T: [keys 0-63, keys 64-127] of the chunk, rows = d
+  uint8_t* sP = sV + 2 * kABox;        // [hi keys 0-63, hi keys 64-127, lo keys 0-63, lo keys 64-127]
+  uint64_t* bar = (uint64_t*)(sP + 4 * kABox);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;
+  uint64_t* s_full = bar + 2;
+  uint64_t* p_full = bar + 3;
+  uint64_t* o_full = bar + 4;
+  uint64_t* epi_done = bar + 5;        // the 128 softmax threads are past their last TMEM read
+  uint32_t* tmem_slot = (uint32_t*)(bar + 8);
 
-__global__ void __launch_bounds__(128) pf_attn_kernel(const float* __restrict__ q, int ldq,
-                                                      const uint16_t* __restrict__ kv, int NH, int NKV, int S,
-                                                      int C, uint16_t* __restrict__ act_o, int ld_act) {
-  __shared__ __align__(16) uint8_t sK[kPKC * kPRow];
-  __shared__ __align__(16) uint8_t sV[kPKC * kPRow];
-  grid_dep_wait();
-  grid_dep_launch();
-  const int qt = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
-  const int row = t >> 2, part = t & 3;  // query row within the tile, 32-dim slice
-  const int tq = qt * kPQT + row;        // query token
-  const int kvh = h / (NH / NKV);
-  const uint8_t* kg = (const uint8_t*)(kv + ((size_t)kvh * S) * 128);
-  const uint8_t* vg = (const uint8_t*)(kv + ((size_t)(NKV + kvh) * S) * 128);
-  const float scale = 0.08838834764831845f;  // 1/sqrt(128)
-  float qv[32], o[32];
-  const float* qp = q + (size_t)tq * ldq + (size_t)h * 128 + part * 32;
-#pragma unroll
-  for (int d = 0; d < 32; d++) {
-    qv[d] = qp[d];
-    o[d] = 0.f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, kvh = blockIdx.y;
+  const int kend = qt * kAQ + kAQ;               // keys 0 .. kend-1 are needed
+  const int nchunk = (kend + kAK - 1) / kAK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(kv_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    mbar_init(epi_done, 128);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
   }
-  float m = -INFINITY, l = 0.f;
-  const int kend = qt * kPQT + kPQT;  // keys needed by the tile: 0 .. kend-1
-  for (int k0 = 0; k0 < kend; k0 += kPKC) {
-    __syncthreads();  // the previous chunk is consumed
-    for (int i = t; i < kPKC * 16; i += 128) {
-      const int j = i >> 4, c16 = (i & 15) * 16;
-      pf_cp_async16(sK + j * kPRow + c16, kg + (size_t)(k0 + j) * 256 + c16);
-      pf_cp_async16(sV + j * kPRow + c16, vg + (size_t)(k0 + j) * 256 + c16);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    float sc[kPKC];
-    float cmax = -INFINITY;
-#pragma unroll 4
-    for (int j = 0; j < kPKC; j++) {
-      const uint8_t* kr = sK + j * kPRow + part * 64;
-      float acc = 0.f;
-#pragma unroll
-      for (int v4 = 0; v4 < 4; v4++) {
-        float kf[8];
-        unpack8(*reinterpret_cast<const uint4*>(kr + v4 * 16), kf);
-#pragma unroll
-        for (int e = 0; e < 8; e++) acc = fmaf(qv[v4 * 8 + e], kf[e], acc);
-      }
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      const float s = (k0 + j <= tq) ? acc * scale : -INFINITY;
-      sc[j] = s;
-      cmax = fmaxf(cmax, s);
-    }
-    const float mnew = fmaxf(m, cmax);
-    if (mnew != -INFINITY) {
-      const float corr = expf(m - mnew);
-      l *= corr;
-#pragma unroll
-      for (int d = 0; d < 32; d++) o[d] *= corr;
-      m = mnew;
-#pragma unroll 4
-      for (int j = 0; j < kPKC; j++) {
-        if (sc[j] == -INFINITY) continue;
-        const float p = expf(sc[j] - m);
-        l += p;
-        const uint8_t* vr = sV + j * kPRow + part * 64;
-#pragma unroll
-        for (int v4 = 0; v4 < 4; v4++) {
-          float vf[8];
-          unpack8(*reinterpret_cast<const uint4*>(vr + v4 * 16), vf);
-#pragma unroll
-          for (int e = 0; e < 8; e++) o[v4 * 8 + e] = fmaf(p, vf[e], o[v4 * 8 + e]);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);  // S: columns 0-127, O_c: 128-255
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      grid_dep_wait();  // q, K and V^T are written by the QKV GEMM
+      mbar_arrive_expect_tx(q_full, 4 * kABox);
+      for (int hl = 0; hl < 2; hl++)
+        for (int bx = 0; bx < 2; bx++)
+          tma_load_3d(sQ + (hl * 2 + bx) * kABox, &tmQ, q_full, bx * 64, kvh * 4, hl * C + qt * kAQ);
+      for (int c = 0; c < nchunk; c++) {
+        if (c > 0 && !mbar_wait(o_full, (uint32_t)(c - 1) & 1u, ST_TMA_WAIT, &g_status_prefill)) break;
+        mbar_arrive_expect_tx(kv_full, 4 * kABox);
+        for (int bx = 0; bx < 2; bx++) {
+          tma_load_3d(sK + bx * kABox, &tmK, kv_full, bx * 64, c * kAK, kvh);
+          tma_load_3d(sV + bx * kABox, &tmV, kv_full, c * kAK + bx * 64, 0, kvh);
         }
       }
+      grid_dep_launch();
     }
-  }
-  const float inv_l = 1.0f / l;
-  uint16_t* dh = act_o + (size_t)tq * ld_act + (size_t)h * 128 + part * 32;
-  uint16_t* dl = act_o + (size_t)(C + tq) * ld_act + (size_t)h * 128 + part * 32;
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, 128);
+      bool ok = mbar_wait(q_full, 0, ST_MMA_WAIT, &g_status_prefill);
+      for (int c = 0; c < nchunk && ok; c++) {
+        ok = mbar_wait(kv_full, (uint32_t)c & 1u, ST_MMA_WAIT, &g_status_prefill);
+        if (!ok) break;
+        tc_fence_after();
+        // S = (Qhi + Qlo) K^T over HD = 2 boxes x 4 K-steps
+        for (int kk = 0; kk < 8; kk++) {
+          const uint32_t off = (uint32_t)((kk >> 2) * kABox + (kk & 3) * 32);
+          const uint64_t kd = sw128_kmajor_desc(smem_u32(sK) + off);
+          umma_bf16(tS, sw128_kmajor_desc(smem_u32(sQ) + off), kd, idesc, kk != 0 ? 1u : 0u);
+          umma_bf16(tS, sw128_kmajor_desc(smem_u32(sQ) + 2 * kABox + off), kd, idesc, 1u);
+        }
+        umma_commit(s_full);
+        ok = mbar_wait(p_full, (uint32_t)c & 1u, ST_MMA_WAIT, &g_status_prefill);
+        if (!ok) break;
+        tc_fence_after();
+        // O_c = (Phi + Plo) V over the chunk's 128 keys = 2 boxes x 4 K-steps
+        for (int kk = 0; kk < 8; kk++) {
+          const uint32_t off = (uint32_t)((kk >> 2) * kABox + (kk & 3) * 32);
+          const uint64_t vd = sw128_kmajor_desc(smem_u32(sV) + off);
+          umma_bf16(tO, sw128_kmajor_desc(smem_u32(sP) + off), vd, idesc, kk != 0 ? 1u : 0u);
+          umma_bf16(tO, sw128_kmajor_desc(smem_u32(sP) + 2 * kABox + off), vd, idesc, 1u);
+        }
+        umma_commit(o_full);
+      }
+      // TMEM is freed below only after every softmax thread has read its last accumulator
+      mbar_wait(epi_done, 0u, ST_EPI_WAIT, &g_status_prefill);
+      tc_fence_after();
+    }
+    __syncwarp();
+    tmem_dealloc(tmem, 256);
+  } else {
+    // softmax / output warps: thread r owns MMA row r = (token qt*32 + r/4, head 4*kvh + r%4)
+    const int r = ((warp & 3) << 5) | lane;
+    const int tok = qt * kAQ + (r >> 2);
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const float scale = 0.08838834764831845f;  // 1/sqrt(128)
+    float o[128];
 #pragma unroll
-  for (int d = 0; d < 32; d++) {
-    const float v = o[d] * inv_l;
-    const uint16_t hi = f2bf_bits(v);
-    dh[d] = hi;
-    dl[d] = f2bf_bits(v - bf2f(hi));
+    for (int j = 0; j < 128; j++) o[j] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    uint8_t* prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
+    for (int c = 0; c < nchunk; c++) {
+      if (!mbar_wait(s_full, (uint32_t)c & 1u, ST_EPI_WAIT, &g_status_prefill)) break;
+      __syncwarp();
+      tc_fence_after();
+      float cm = -INFINITY;
+#pragma unroll
+      for (int qq = 0; qq < 4; qq++) {
+        float v[32];
+        tmem_ld_32x32b_x32(tS + lane_base + qq * 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (c * kAK + qq * 32 + j <= tok) cm = fmaxf(cm, v[j] * scale);
+      }
+      const float mnew = fmaxf(m, cm);
+      const float corr = m == -INFINITY ? 0.f : expf(m - mnew);
+      float lsum = 0.f;
+#pragma unroll
+      for (int qq = 0; qq < 4; qq++) {
+        float v[32];
+        tmem_ld_32x32b_x32(tS + lane_base + qq * 32, v);
+#pragma unroll
+        for (int g8 = 0; g8 < 4; g8++) {  // 8 keys = one 16-byte chunk of the swizzled row
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            float pp[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+              const int j = g8 * 8 + e + u;
+              pp[u] = c * kAK + qq * 32 + j <= tok ? expf(v[j] * scale - mnew) : 0.f;
+              lsum += pp[u];
+            }
+            const uint16_t h0 = f2bf_bits(pp[0]), h1 = f2bf_bits(pp[1]);
+            hw[e / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+            lw[e / 2] = (uint32_t)f2bf_bits(pp[0] - bf2f(h0)) | ((uint32_t)f2bf_bits(pp[1] - bf2f(h1)) << 16);
+          }
+          const int key16 = qq * 4 + g8;                 // 16-byte chunk index within the 256-byte row
+          const int bx = key16 >> 3, ch = (key16 & 7) ^ (r & 7);
+          *reinterpret_cast<uint4*>(prow + bx * kABox + (ch << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(prow + (2 + bx) * kABox + (ch << 4)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      }
+      l = l * corr + lsum;
+      m = mnew;
+      fence_proxy_async_smem();  // P is read by the tensor cores
+      tc_fence_before();
+      pf_arrive(p_full);
+      if (!mbar_wait(o_full, (uint32_t)c & 1u, ST_EPI_WAIT, &g_status_prefill)) break;
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll
+      for (int qq = 0; qq < 4; qq++) {
+        float v[32];
+        tmem_ld_32x32b_x32(tO + lane_base + qq * 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; j++) o[qq * 32 + j] = fmaf(o[qq * 32 + j], corr, v[j]);
+      }
+    }
+    tc_fence_before();
+    pf_arrive(epi_done);
+    const float inv_l = 1.0f / l;
+    const int head = kvh * 4 + (r & 3);
+    uint16_t* dh = act_o + (size_t)tok * ld_act + (size_t)head * 128;
+    uint16_t* dl = act_o + (size_t)(C + tok) * ld_act + (size_t)head * 128;
+#pragma unroll
+    for (int d8 = 0; d8 < 16; d8++) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float v0 = o[d8 * 8 + e] * inv_l, v1 = o[d8 * 8 + e + 1] * inv_l;
+        const uint16_t h0 = f2bf_bits(v0), h1 = f2bf_bits(v1);
+        hw[e / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        lw[e / 2] = (uint32_t)f2bf_bits(v0 - bf2f(h0)) | ((uint32_t)f2bf_bits(v1 - bf2f(h1)) << 16);
+      }
+      *reinterpret_cast<uint4*>(dh + d8 * 8) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(dl + d8 * 8) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
   }
 }
 
@@ -563,6 +686,28 @@ extern "C" int rngd_prefill_embed(const rngd_model_t* m, const rngd_prefill_io_t
   return launch_operand_ex(io->x, H, io->C, H, m->n1, io->act, ld, io->C, io->ss, io->C, nullptr, s);
 }
 
+// Causal attention of one layer on tcgen05 (pf_attn_tc_kernel): Q hi/lo from io->q, K from
+// the layer's cache block, V^T from the act2 scratch, output into io->act_o.
+static int launch_pf_attn(const rngd_model_t* m, const rngd_prefill_io_t* io, const uint16_t* kv, cudaStream_t s) {
+  const int C = io->C, NKV = m->NKV, NH = m->NH;
+  CUtensorMap tq, tk, tv;
+  const uint64_t qd[3] = {128, (uint64_t)NH, (uint64_t)2 * C}, qs[2] = {256, (uint64_t)NH * 256};
+  const uint32_t qb[3] = {64, 4, (uint32_t)kAQ};
+  RNGD_TRY(get_map3_bf16(io->q, qd, qs, qb, &tq));
+  // the cache block belongs to one request: encoded per call rather than cached
+  const uint64_t kd[3] = {128, (uint64_t)io->S, (uint64_t)NKV}, ks[2] = {256, (uint64_t)io->S * 256};
+  const uint32_t kb[3] = {64, (uint32_t)kAK, 1};
+  RNGD_TRY(encode_tmap_bf16(&tk, kv, 3, kd, ks, kb));
+  const uint64_t vd[3] = {(uint64_t)C, 128, (uint64_t)NKV}, vs[2] = {(uint64_t)C * 2, (uint64_t)C * 256};
+  const uint32_t vb[3] = {64, 128, 1};
+  RNGD_TRY(get_map3_bf16(io->act2, vd, vs, vb, &tv));
+  static std::atomic<unsigned long long> attr_set{0};
+  RNGD_TRY(set_smem_limit_once((const void*)pf_attn_tc_kernel, (int)kAttnTcSmem, &attr_set,
+                               "cudaFuncSetAttribute(pf_attn_tc_kernel)"));
+  return launch_pdl(pf_attn_tc_kernel, dim3(C / kAQ, NKV), dim3(192), kAttnTcSmem, s, "pf_attn_tc_kernel", tq, tk,
+                    tv, C, (uint16_t*)io->act_o, NH * 128);
+}
+
 extern "C" int rngd_prefill_layers(const rngd_model_t* m, const rngd_prefill_io_t* io, int layer0, int layer1,
                                    rngd_stream_t stream) {
   RNGD_TRY(check_pio(m, io));
@@ -586,11 +731,10 @@ extern "C" int rngd_prefill_layers(const rngd_model_t* m, const rngd_prefill_io_
     a.inv_h = 1.0f / (float)H;
     a.inv = m->inv_freq; a.q = io->q; a.ldq = QN;
     a.kv = (uint16_t*)io->kv + (size_t)(l - layer0) * layer_elems;
+    a.vt = (uint16_t*)io->act2;
     a.NH = m->NH; a.NKV = m->NKV; a.S = io->S;
     RNGD_TRY(launch_pf_any<PEPI_QKV>(m->wqkv, m->L, l, NQKV, H, io->act, ld, a, s));
-    RNGD_TRY(launch_pdl(pf_attn_kernel, dim3(io->C / kPQT, m->NH), dim3(128), 0, s, "pf_attn_kernel",
-                        (const float*)io->q, QN, (const uint16_t*)a.kv, m->NH, m->NKV, io->S, io->C,
-                        (uint16_t*)io->act_o, QN));
+    RNGD_TRY(launch_pf_attn(m, io, a.kv, s));
     a.x = io->x; a.ldx = H;
     a.w_next = m->n2 + (size_t)l * H; a.act_next = (uint16_t*)io->act; a.ld_next = ld; a.ss_out = io->ss;
     RNGD_TRY(launch_pf_any<PEPI_RESID>(m->wo, m->L, l, H, QN, io->act_o, QN, a, s));

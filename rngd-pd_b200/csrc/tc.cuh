@@ -161,6 +161,12 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy
+// reads of them (a tcgen05.mma operand written by threads rather than by TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Programmatic dependent launch: wait until the preceding grid's memory is visible.
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
@@ -205,6 +211,10 @@ int read_status_prefill(int* st, int reset);
 int num_sms();
 int get_weight_map(const void* w, int L, int N, int K, CUtensorMap* out);
 int get_operand_map(const void* act, int K, int ld, int rows, int box_rows, CUtensorMap* out);
+// Cached 3-D bf16 tensor map with 128-byte swizzle: dims / box innermost first, strides of
+// dims 1 and 2 in bytes (box[0] * 2 must be 128).
+int get_map3_bf16(const void* base, const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                  CUtensorMap* out);
 
 // CTA owning flattened work item f under an equal split of `total` items over `grid` CTAs.
 __host__ __device__ __forceinline__ int owner_of(long f, long total, int grid) {
