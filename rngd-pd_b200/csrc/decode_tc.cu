@@ -592,7 +592,11 @@ static std::mutex g_map_mu;
 static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
 int get_weight_map(const void* w, int L, int N, int K, CUtensorMap* out) {
-  MapKey key{w, (uint64_t)L, (uint64_t)N, (uint64_t)K};
+  return get_weight_map_rows(w, L, N, K, BM, out);
+}
+
+int get_weight_map_rows(const void* w, int L, int N, int K, int rows, CUtensorMap* out) {
+  MapKey key{w, (uint64_t)L | ((uint64_t)rows << 32), (uint64_t)N, (uint64_t)K};
   std::lock_guard<std::mutex> g(g_map_mu);
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
@@ -601,7 +605,7 @@ int get_weight_map(const void* w, int L, int N, int K, CUtensorMap* out) {
   }
   const uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)L};
   const uint64_t strides[2] = {(uint64_t)K * 2, (uint64_t)K * 2 * N};
-  const uint32_t box[3] = {BK, BM, 1};
+  const uint32_t box[3] = {BK, (uint32_t)rows, 1};
   RNGD_TRY(encode_tmap_bf16(out, w, 3, dims, strides, box));
   g_maps[key] = *out;
   return RNGD_OK;

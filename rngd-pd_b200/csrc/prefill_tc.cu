@@ -32,13 +32,16 @@ __device__ int g_status_prefill = 0;
 constexpr int PBM = 128, PBK = 64;
 constexpr int P_YS_LD = 33;
 
-template <int NT>
+// MT weight tiles (128 rows each) share every token tile: with MT = 2 a 64 KB stage
+// carries 32 KB of weights and 32 KB of activations (hi + lo) for twice the MMA work of
+// MT = 1, halving the activation traffic per FLOP.
+template <int NT, int MT>
 struct PCfg {
-  static constexpr int A_BYTES = PBM * PBK * 2;   // 16 KB weight tile
-  static constexpr int B_BYTES = NT * PBK * 2;    // one token tile (hi or lo)
+  static constexpr int A_BYTES = MT * PBM * PBK * 2;  // MT x 16 KB of weight rows
+  static constexpr int B_BYTES = NT * PBK * 2;        // one token tile (hi or lo)
   static constexpr int STAGE = A_BYTES + 2 * B_BYTES;
-  static constexpr int STAGES = NT == 256 ? 2 : 4;
-  static constexpr int TMEM_COLS = 2 * NT;        // double-buffered accumulator
+  static constexpr int STAGES = MT == 2 ? 3 : 4;
+  static constexpr int TMEM_COLS = 2 * MT * NT;       // MT accumulators, double-buffered
   static constexpr size_t BAR_BYTES = (2 * STAGES + 4) * 8;
   static constexpr size_t SMEM = 1024 + STAGES * STAGE + BAR_BYTES + 64 + NT * 4 + PBM * P_YS_LD * 4 + 4 * 32 * 4;
 };
@@ -77,10 +80,10 @@ __device__ __forceinline__ void pf_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-template <int EPI, int NT>
+template <int EPI, int NT, int MT>
 __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ CUtensorMap tmW,
                                                         const __grid_constant__ CUtensorMap tmX, PArgs a) {
-  using Cfg = PCfg<NT>;
+  using Cfg = PCfg<NT, MT>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -127,10 +130,10 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       for (long i = 0; i < pre; i++) {
         const long f = f0 + i;
         const long u = f / a.nkb;
-        const int kb = (int)(f - u * a.nkb), mt = (int)(u / a.ntok);
+        const int kb = (int)(f - u * a.nkb), mg = (int)(u / a.ntok);
         uint8_t* st = base + i * Cfg::STAGE;
         mbar_arrive_expect_tx(&full[i], Cfg::STAGE);
-        tma_load_3d(st, &tmW, &full[i], kb * PBK, mt * PBM, a.layer);
+        tma_load_3d(st, &tmW, &full[i], kb * PBK, mg * MT * PBM, a.layer);
       }
       grid_dep_wait();
       for (long i = 0; i < pre; i++) {
@@ -147,10 +150,10 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
         if (!mbar_wait(&empty[s], ph ^ 1u, ST_TMA_WAIT, &g_status_prefill)) break;
         const long f = f0 + i;
         const long u = f / a.nkb;
-        const int kb = (int)(f - u * a.nkb), mt = (int)(u / a.ntok), jt = (int)(u % a.ntok);
+        const int kb = (int)(f - u * a.nkb), mg = (int)(u / a.ntok), jt = (int)(u % a.ntok);
         uint8_t* st = base + s * Cfg::STAGE;
         mbar_arrive_expect_tx(&full[s], Cfg::STAGE);
-        tma_load_3d(st, &tmW, &full[s], kb * PBK, mt * PBM, a.layer);
+        tma_load_3d(st, &tmW, &full[s], kb * PBK, mg * MT * PBM, a.layer);
         tma_load_2d(st + Cfg::A_BYTES, &tmX, &full[s], kb * PBK, jt * NT);
         tma_load_2d(st + Cfg::A_BYTES + Cfg::B_BYTES, &tmX, &full[s], kb * PBK, a.C + jt * NT);
       }
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
         const int buf = seg & 1;
         ok = mbar_wait(&acc_empty[buf], ((uint32_t)(seg >> 1) & 1u) ^ 1u, ST_MMA_WAIT, &g_status_prefill);
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * NT);
+        const uint32_t d = tmem + (uint32_t)(buf * MT * NT);
         for (long g = f; g < fend && ok; g++, i++) {
           const int s = (int)(i % STAGES);
           const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
@@ -180,9 +183,14 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
           const uint32_t sh = sa + Cfg::A_BYTES, sl = sh + Cfg::B_BYTES;
 #pragma unroll
           for (int kk = 0; kk < PBK / 16; kk++) {
-            const uint64_t ad = sw128_kmajor_desc(sa + kk * 32);
-            umma_bf16(d, ad, sw128_kmajor_desc(sh + kk * 32), idesc, (g != f || kk != 0) ? 1u : 0u);
-            umma_bf16(d, ad, sw128_kmajor_desc(sl + kk * 32), idesc, 1u);
+            const uint64_t hd = sw128_kmajor_desc(sh + kk * 32), ld_ = sw128_kmajor_desc(sl + kk * 32);
+#pragma unroll
+            for (int tt = 0; tt < MT; tt++) {  // tile tt: weight rows 128*tt.. of the stage, accumulator tt
+              const uint64_t ad = sw128_kmajor_desc(sa + tt * PBM * 128 + kk * 32);
+              const uint32_t dt = d + (uint32_t)(tt * NT);
+              umma_bf16(dt, ad, hd, idesc, (g != f || kk != 0) ? 1u : 0u);
+              umma_bf16(dt, ad, ld_, idesc, 1u);
+            }
           }
           umma_commit(&empty[s]);
         }
@@ -201,8 +209,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       const long u = f / a.nkb;
       const long ustart = u * a.nkb;
       const long fend = ustart + a.nkb < f1 ? ustart + a.nkb : f1;
-      const int mt = (int)(u / a.ntok), jt = (int)(u % a.ntok);
-      const int n = mt * PBM + r;
+      const int mg = (int)(u / a.ntok), jt = (int)(u % a.ntok);
       const int buf = seg & 1;
       // RMS scales of this unit's NT tokens, read while the accumulator is still being built:
       // token jt*NT + i's sum over the ss tiles in tile order, loads batched 16 at a time
@@ -227,16 +234,18 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       tc_fence_after();
       const int first = owner_of(ustart, a.total, G), last = owner_of(ustart + a.nkb - 1, a.total, G);
       const int nseg = last - first + 1;
-      const uint32_t tbase = tmem + lane_base + (uint32_t)(buf * NT);
+      const uint32_t tbase0 = tmem + lane_base + (uint32_t)(buf * MT * NT);
       bool run = true;
       if (nseg > 1) {
         const int slot = cta - first;
-        float* pdst = a.partial + ((size_t)u * a.maxseg + slot) * NT * PBM;
-        for (int cc = 0; cc < NT / 32; cc++) {
-          float v[32];
-          tmem_ld_32x32b_x32(tbase + cc * 32, v);
+        for (int tt = 0; tt < MT; tt++) {
+          float* pdst = a.partial + (((size_t)u * a.maxseg + slot) * MT + tt) * NT * PBM;
+          for (int cc = 0; cc < NT / 32; cc++) {
+            float v[32];
+            tmem_ld_32x32b_x32(tbase0 + tt * NT + cc * 32, v);
 #pragma unroll
-          for (int i = 0; i < 32; i++) __stcg(pdst + (size_t)(cc * 32 + i) * PBM + r, v[i]);
+            for (int i = 0; i < 32; i++) __stcg(pdst + (size_t)(cc * 32 + i) * PBM + r, v[i]);
+          }
         }
         tc_fence_before();
         pf_arrive(&acc_empty[buf]);
@@ -248,18 +257,22 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
         if (run) __threadfence();
       }
       if (run) {
+       for (int tt = 0; tt < MT; tt++) {
+        const int mt = mg * MT + tt;  // weight tile of this accumulator
+        const int n = mt * PBM + r;
         for (int cc = 0; cc < NT / 32; cc++) {
           float y[32];
           if (nseg > 1) {
 #pragma unroll
             for (int i = 0; i < 32; i++) y[i] = 0.f;
             for (int sl = 0; sl < nseg; sl++) {
-              const float* src = a.partial + ((size_t)u * a.maxseg + sl) * NT * PBM + (size_t)(cc * 32) * PBM + r;
+              const float* src =
+                  a.partial + (((size_t)u * a.maxseg + sl) * MT + tt) * NT * PBM + (size_t)(cc * 32) * PBM + r;
 #pragma unroll
               for (int i = 0; i < 32; i++) y[i] += __ldcg(src + (size_t)i * PBM);
             }
           } else {
-            tmem_ld_32x32b_x32(tbase + cc * 32, y);
+            tmem_ld_32x32b_x32(tbase0 + tt * NT + cc * 32, y);
           }
           const int t0 = jt * NT + cc * 32;  // first token of the chunk
           if (EPI != PEPI_RESID && a.ss_in != nullptr) {
@@ -355,6 +368,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
           }
           pf_sync();  // ys / s_scale / s_red reused by the next chunk
         }
+       }
         if (nseg > 1) {
           if (et == 0) a.counters[u] = 0;
         } else {
@@ -598,43 +612,54 @@ static int pf_maxseg(long units, long nkb, int grid) {
   return mx;
 }
 
-template <int EPI, int NT>
+template <int EPI, int NT, int MT>
 static int launch_pf(const void* W, int L, int layer, int N, int K, const void* act, int ld, PArgs a, cudaStream_t s) {
-  RNGD_REQUIRE(K % PBK == 0 && N % PBM == 0, "prefill GEMM: N=%d K=%d must be multiples of 128 / 64", N, K);
+  RNGD_REQUIRE(K % PBK == 0 && N % (MT * PBM) == 0, "prefill GEMM: N=%d K=%d must be multiples of %d / 64", N, K,
+               MT * PBM);
   RNGD_REQUIRE(a.C % NT == 0, "prefill GEMM: C=%d must be a multiple of %d", a.C, NT);
   CUtensorMap tw, tx;
-  RNGD_TRY(get_weight_map(W, L, N, K, &tw));
+  RNGD_TRY(get_weight_map_rows(W, L, N, K, MT * PBM, &tw));
   RNGD_TRY(get_operand_map(act, K, ld, 2 * a.C, NT, &tx));
   a.N = N;
   a.K = K;
   a.nkb = K / PBK;
   a.ntok = a.C / NT;
-  const long units = (long)(N / PBM) * a.ntok;
+  const long units = (long)(N / (MT * PBM)) * a.ntok;
   a.total = (int)(units * a.nkb);
   const int grid = pf_grid(a.total);
   a.maxseg = pf_maxseg(units, a.nkb, grid);
   a.layer = layer;
   RNGD_REQUIRE(a.maxseg == 1 || (a.partial && a.counters), "prefill GEMM: split tiles need partial/counters");
   static std::atomic<unsigned long long> attr_set{0};
-  RNGD_TRY(set_smem_limit_once((const void*)pfgemm_kernel<EPI, NT>, (int)PCfg<NT>::SMEM, &attr_set,
+  RNGD_TRY(set_smem_limit_once((const void*)pfgemm_kernel<EPI, NT, MT>, (int)PCfg<NT, MT>::SMEM, &attr_set,
                                "cudaFuncSetAttribute(pfgemm)"));
-  return launch_pdl(pfgemm_kernel<EPI, NT>, dim3(grid), dim3(192), PCfg<NT>::SMEM, s, "pfgemm_kernel", tw, tx, a);
+  return launch_pdl(pfgemm_kernel<EPI, NT, MT>, dim3(grid), dim3(192), PCfg<NT, MT>::SMEM, s, "pfgemm_kernel", tw,
+                    tx, a);
+}
+
+// Two weight tiles per work unit halve the activation traffic per FLOP, but also halve
+// the number of units; a GEMM with fewer units than SMs then splits every unit across
+// several CTAs and its tail (partial sums, reduction) grows.  So: two tiles per unit when
+// that still leaves at least one whole unit per SM.
+static int pf_choose_mt(int N, int C) {
+  const long pairs = (N / PBM) % 2 == 0 ? (long)(N / (2 * PBM)) * (C / 128) : 0;
+  return pairs >= num_sms() ? 2 : 1;
 }
 
 template <int EPI>
 static int launch_pf_any(const void* W, int L, int layer, int N, int K, const void* act, int ld, PArgs a,
                          cudaStream_t s) {
-  // 128-token tiles: a 48 KB stage (weights + hi + lo) leaves room for 4 stages in flight,
-  // which measured faster than 256-token tiles with 2 stages at every bucket width
-  return launch_pf<EPI, 128>(W, L, layer, N, K, act, ld, a, s);
+  // 128-token tiles (measured faster than 256-token tiles with fewer stages)
+  if (pf_choose_mt(N, a.C) == 2) return launch_pf<EPI, 128, 2>(W, L, layer, N, K, act, ld, a, s);
+  return launch_pf<EPI, 128, 1>(W, L, layer, N, K, act, ld, a, s);
 }
 
 // scratch of one GEMM shape
 static void pf_shape_ws(int N, int K, int C, size_t* pf, size_t* ct) {
-  const int NT = 128;
-  const long units = (long)(N / PBM) * (C / NT), nkb = K / PBK;
+  const int NT = 128, MT = pf_choose_mt(N, C);  // as launch_pf_any chooses
+  const long units = (long)(N / (MT * PBM)) * (C / NT), nkb = K / PBK;
   const int ms = pf_maxseg(units, nkb, pf_grid(units * nkb));
-  *pf = ms > 1 ? (size_t)units * ms * NT * PBM : 0;
+  *pf = ms > 1 ? (size_t)units * ms * MT * NT * PBM : 0;
   *ct = ms > 1 ? (size_t)units : 0;
 }
 

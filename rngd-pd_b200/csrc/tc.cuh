@@ -210,6 +210,8 @@ int read_status_prefill(int* st, int reset);
 // blocks [L][N][K] (box 64 x 128) and operand buffers [rows][K] (box 64 x box_rows).
 int num_sms();
 int get_weight_map(const void* w, int L, int N, int K, CUtensorMap* out);
+// The same with a box of `rows` weight rows (<= 256) per load.
+int get_weight_map_rows(const void* w, int L, int N, int K, int rows, CUtensorMap* out);
 int get_operand_map(const void* act, int K, int ld, int rows, int box_rows, CUtensorMap* out);
 // Cached 3-D bf16 tensor map with 128-byte swizzle: dims / box innermost first, strides of
 // dims 1 and 2 in bytes (box[0] * 2 must be 128).
