@@ -434,6 +434,50 @@ def handoff_one_process(dsts, reps, warmup):
     return out
 
 
+def prefill_flops(cfg, C):
+    """Useful FLOPs of one prefill_full pass over C tokens (config 2): the layer GEMMs, causal
+    attention (QK^T and PV over the lower triangle) and the last position's lm_head."""
+    layer_params = (cfg.hidden * (cfg.n_heads + 2 * cfg.n_kv) * cfg.head_dim + cfg.n_heads * cfg.head_dim * cfg.hidden
+                    + 3 * cfg.hidden * cfg.inter)
+    gemm = 2 * C * layer_params * cfg.n_layers
+    attn = cfg.n_layers * 4 * cfg.n_heads * cfg.head_dim * (C // 2) * C
+    return gemm + attn + 2 * cfg.hidden * cfg.vocab
+
+
+def prefill_measure(eng, reps=5, warmup=2):
+    """Config 2 on the decode engine's card and weights: one 256-token prompt (ids U[0, V),
+    seed 4) through FullPrefillEngine.prefill_kv_device, CUDA events on the prefill stream."""
+    import torch
+    from rngd_pd import synth
+    from rngd_pd.engines.prefill_full import FullPrefillEngine
+    C = 256
+    pf = FullPrefillEngine(eng.cfg, eng.w, C=C, group=2, S=S)
+    toks = synth.tokens(C, seed=4)
+    for _ in range(warmup):
+        pf.prefill_kv_device(toks)
+    ms = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(pf.stream)
+        kv, nxt = pf.prefill_kv_device(toks)
+        e1.record(pf.stream)
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    t = statistics.median(ms)
+    flops = prefill_flops(eng.cfg, C)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    peak = peaks.get("bf16_tflops", 1590.0)
+    tf = flops / (t / 1e3) / 1e12
+    del pf
+    return {"workload": "config2: prefill_full, one prompt of C=256 tokens, Llama-3.1-8B shape", "ms": t,
+            "tflops_useful": tf, "peak_tflops": peak, "frac": tf / peak,
+            "flops_per_pass": flops, "note": "GEMMs issue hi and lo activation halves: tensor work is ~2x the useful"}
+
+
 def handoff_pairs(rank, world, dev, reps, warmup):
     """Config 3 across processes: GPU 2i prefills (seeded caches) and pushes into GPU 2i+1's
     decode cache, mapped through CUDA IPC; 1/4/16 requests per batch.  Returns, on every rank,
@@ -510,6 +554,15 @@ def run_micro(args):
         return run_micro_attn(args)
     if args.micro == "handoff":
         return run_micro_handoff(args)
+    if args.micro == "prefill":
+        from rngd_pd.engines.decode_batch import BatchDecodeEngine
+        from rngd_pd.engines.model import ModelConfig
+        torch.cuda.set_device(0)
+        cfg = ModelConfig.llama31_8b()
+        eng = BatchDecodeEngine(cfg, synth.SyntheticState(cfg, seed=0), B=B, S=S, group=8)
+        print(json.dumps({"micro": "prefill", **prefill_measure(eng, reps=args.steps, warmup=args.warmup)}),
+              flush=True)
+        return
     if args.micro.startswith("pf_"):
         return run_micro_prefill(args)
     shapes = {"gate_up": (28672, 4096), "qkv": (6144, 4096), "o": (4096, 4096), "down": (4096, 14336),
@@ -613,6 +666,7 @@ def run_ours(args):
     e2e_s = float(t.item())
 
     roof = gemm_roofline(eng) if rank == 0 else None
+    prefill = prefill_measure(eng) if rank == 0 else None
 
     # ------------------------------------------------- KV handoff (config 3)
     from rngd_pd.engines.model import ModelConfig as _MC
@@ -677,6 +731,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": B * 4},
         "gpu_launches": eng.launches_per_step * K,
         "handoff": handoff,
+        "prefill": prefill,
     }
     print(json.dumps(line), flush=True)
 
@@ -689,7 +744,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn", "pf_gate_up", "pf_qkv", "pf_o",
-                                        "pf_down", "handoff"],
+                                        "pf_down", "handoff", "prefill"],
                     help="time one decode GEMM shape alone (small footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:

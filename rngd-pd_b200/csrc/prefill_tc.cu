@@ -100,6 +100,10 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   const long f0 = (long)cta * a.total / G, f1 = (long)(cta + 1) * a.total / G;
+  // unit u = (weight-tile group u % ngrp, token tile u / ngrp): the token tiles of one group
+  // are far apart in u, so different CTAs stream the same weights at about the same time
+  // and the second read hits L2 instead of HBM
+  const int ngrp = a.N / (MT * PBM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -130,7 +134,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       for (long i = 0; i < pre; i++) {
         const long f = f0 + i;
         const long u = f / a.nkb;
-        const int kb = (int)(f - u * a.nkb), mg = (int)(u / a.ntok);
+        const int kb = (int)(f - u * a.nkb), mg = (int)(u % ngrp);
         uint8_t* st = base + i * Cfg::STAGE;
         mbar_arrive_expect_tx(&full[i], Cfg::STAGE);
         tma_load_3d(st, &tmW, &full[i], kb * PBK, mg * MT * PBM, a.layer);
@@ -139,7 +143,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       for (long i = 0; i < pre; i++) {
         const long f = f0 + i;
         const long u = f / a.nkb;
-        const int kb = (int)(f - u * a.nkb), jt = (int)(u % a.ntok);
+        const int kb = (int)(f - u * a.nkb), jt = (int)(u / ngrp);
         uint8_t* st = base + i * Cfg::STAGE;
         tma_load_2d(st + Cfg::A_BYTES, &tmX, &full[i], kb * PBK, jt * NT);
         tma_load_2d(st + Cfg::A_BYTES + Cfg::B_BYTES, &tmX, &full[i], kb * PBK, a.C + jt * NT);
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
         if (!mbar_wait(&empty[s], ph ^ 1u, ST_TMA_WAIT, &g_status_prefill)) break;
         const long f = f0 + i;
         const long u = f / a.nkb;
-        const int kb = (int)(f - u * a.nkb), mg = (int)(u / a.ntok), jt = (int)(u % a.ntok);
+        const int kb = (int)(f - u * a.nkb), mg = (int)(u % ngrp), jt = (int)(u / ngrp);
         uint8_t* st = base + s * Cfg::STAGE;
         mbar_arrive_expect_tx(&full[s], Cfg::STAGE);
         tma_load_3d(st, &tmW, &full[s], kb * PBK, mg * MT * PBM, a.layer);
@@ -209,7 +213,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       const long u = f / a.nkb;
       const long ustart = u * a.nkb;
       const long fend = ustart + a.nkb < f1 ? ustart + a.nkb : f1;
-      const int mg = (int)(u / a.ntok), jt = (int)(u % a.ntok);
+      const int mg = (int)(u % ngrp), jt = (int)(u / ngrp);
       const int buf = seg & 1;
       // RMS scales of this unit's NT tokens, read while the accumulator is still being built:
       // token jt*NT + i's sum over the ss tiles in tile order, loads batched 16 at a time
