@@ -49,7 +49,9 @@ constexpr int A_BYTES = BM * BK * 2;   // 16 KB weight tile per stage
 constexpr int B_BYTES = BNC * BK * 2;  // 4 KB activation tile per stage
 constexpr int STAGES = 5;
 constexpr int YS_LD = 17;
-constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int EPI_THREADS = 256;       // two warpgroups, each 8 of the 16 streams
+constexpr int SPG = MAXB / 2;          // streams per epilogue warpgroup
+constexpr int THREADS = 64 + EPI_THREADS;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int TMEM_COLS = 64;          // two 32-column accumulators
 constexpr int kRedBatch = 6;           // split-tile pieces whose partials are loaded together
 
@@ -102,7 +104,7 @@ __device__ __forceinline__ uint32_t orderable(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -140,9 +142,9 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], EPI_THREADS);
     }
-    mbar_init(epi_done, 128);
+    mbar_init(epi_done, EPI_THREADS);
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
@@ -231,35 +233,38 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
     __syncwarp();
     tmem_dealloc(tmem, TMEM_COLS);
   } else {
-    // ---------------- epilogue warps 2..5: thread r owns row r of the tile (TMEM lane r)
+    // ---------------- epilogue warps 2..9: two warpgroups over the same 128 TMEM lanes.  Thread
+    // (group g, row r) owns row r of the tile (TMEM lane r) for the streams 8g .. 8g+7, which
+    // halves each thread's serial work on the GEMM's tail.
     grid_dep_wait();
     const int r = ((warp & 3) << 5) | lane;
-    const int et = threadIdx.x - 64;  // 0..127 index among the epilogue threads
+    const int ep = threadIdx.x - 64;   // 0..255 among the epilogue threads
+    const int sb = (ep >> 7) * SPG;    // first stream of this thread's group
     // Per-launch constants, read once with independent loads: a chain of dependent global
     // loads inside each segment's epilogue was most of the GEMM's tail.  The RMS sums are
     // added in the same order as ever (t = 0, 1, ...), so the scale is bit-identical.
-    if (EPI != EPI_RESID && a.ss_in != nullptr && et < MAXB) {
+    if (EPI != EPI_RESID && a.ss_in != nullptr && ep < MAXB) {
       float ssum = 0.f;
       for (int t0 = 0; t0 < a.ss_tiles; t0 += 16) {
         float v16[16];
 #pragma unroll
-        for (int j = 0; j < 16; j++) v16[j] = t0 + j < a.ss_tiles ? a.ss_in[(t0 + j) * MAXB + et] : 0.f;
+        for (int j = 0; j < 16; j++) v16[j] = t0 + j < a.ss_tiles ? a.ss_in[(t0 + j) * MAXB + ep] : 0.f;
 #pragma unroll
         for (int j = 0; j < 16; j++)
           if (t0 + j < a.ss_tiles) ssum += v16[j];
       }
-      s_scale[et] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
+      s_scale[ep] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
     }
-    // RoPE factors of this step for this thread's frequency (r mod 64), computed while the
-    // weights stream rather than on the GEMM's tail: (cos, sin) of pos[b] * inv[r mod 64]
-    float rcos[MAXB], rsin[MAXB];
+    // RoPE factors of this step for this thread's frequency (r mod 64) and streams, computed
+    // while the weights stream rather than on the GEMM's tail
+    float rcos[SPG], rsin[SPG];
     if constexpr (EPI == EPI_QKV) {
-      if (et < MAXB) s_pos[et] = et < a.B ? a.pos[et] : -1;
+      if (ep < MAXB) s_pos[ep] = ep < a.B ? a.pos[ep] : -1;
       const float invf = a.inv[r & 63];
 #pragma unroll
-      for (int b = 0; b < MAXB; b++) {
-        const int p = b < a.B ? a.pos[b] : -1;
-        sincosf((float)p * invf, &rsin[b], &rcos[b]);
+      for (int i = 0; i < SPG; i++) {
+        const int p = sb + i < a.B ? a.pos[sb + i] : -1;
+        sincosf((float)p * invf, &rsin[i], &rcos[i]);
       }
     }
     epi_sync();
@@ -272,42 +277,43 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       const int n = tile * BM + r;
       // the residual row and norm weight do not depend on this GEMM: fetch them while the
       // accumulator is still being computed (only the tile's reducing CTA writes x[.][n])
-      float xo[MAXB];
+      float xo[SPG];
       float wn = 0.f;
       if constexpr (EPI == EPI_RESID) {
 #pragma unroll
-        for (int b = 0; b < MAXB; b++) xo[b] = b < a.B ? a.x[(size_t)b * a.ldx + n] : 0.f;
+        for (int i = 0; i < SPG; i++) xo[i] = sb + i < a.B ? a.x[(size_t)(sb + i) * a.ldx + n] : 0.f;
         if (a.act_next != nullptr) wn = a.w_next[n];
       }
       mbar_wait(&acc_full[buf], (uint32_t)(seg >> 1) & 1u, ST_EPI_WAIT, &g_status_decode);
-      if (tr != nullptr && et == 0 && fend == f1) tr[5] = globaltimer();
+      if (tr != nullptr && ep == 0 && fend == f1) tr[5] = globaltimer();
       __syncwarp();
       tc_fence_after();
-      float v[32];
-      tmem_ld_32x32b_x32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * BNC), v);
+      float vh[SPG], vl[SPG];  // the hi and lo operand columns of this group's streams
+      const uint32_t tb = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * BNC);
+      tmem_ld_32x32b_2x8(tb + sb, tb + MAXB + sb, vh, vl);
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
-      const bool tlast = tr != nullptr && et == 0 && fend == f1;
+      const bool tlast = tr != nullptr && ep == 0 && fend == f1;
       if (tlast) tr[8] = globaltimer();
-      float y[MAXB];
+      float y[SPG];
 #pragma unroll
-      for (int b = 0; b < MAXB; b++) y[b] = v[b] + v[MAXB + b];
+      for (int i = 0; i < SPG; i++) y[i] = vh[i] + vl[i];
 
       const int first = owner_of(tstart, a.total, G), last = owner_of(tstart + a.nkb - 1, a.total, G);
       const int nseg = last - first + 1;
       bool run = true;
       if (nseg > 1) {
         const int slot = cta - first;
-        float4* dst = reinterpret_cast<float4*>(a.partial + (((size_t)tile * a.maxseg + slot) * BM + r) * MAXB);
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-          __stcg(dst + j, make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]));
+        float4* dst =
+            reinterpret_cast<float4*>(a.partial + (((size_t)tile * a.maxseg + slot) * BM + r) * MAXB + sb);
+        __stcg(dst, make_float4(y[0], y[1], y[2], y[3]));
+        __stcg(dst + 1, make_float4(y[4], y[5], y[6], y[7]));
         // The barrier orders every epilogue thread's partial stores before thread 0's counter
         // update, whose release (gpu scope) publishes them; the last arriver's acquire on the
         // same update, followed by the barrier, orders its threads' partial reads after all
         // pieces were written.  No full fence on either side.
         epi_sync();
-        if (et == 0) {
+        if (ep == 0) {
           int old;
           asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
                        : "=r"(old)
@@ -320,164 +326,163 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
         if (tlast) tr[9] = globaltimer();
         if (run) {
 #pragma unroll
-          for (int b = 0; b < MAXB; b++) y[b] = 0.f;
+          for (int i = 0; i < SPG; i++) y[i] = 0.f;
           // pieces summed in K order; every piece's loads issued before the first add (one L2
           // round trip for up to kRedBatch pieces instead of one per piece)
           for (int s0 = 0; s0 < nseg; s0 += kRedBatch) {
-            float4 tp[kRedBatch][4];
+            float4 tp[kRedBatch][2];
 #pragma unroll
             for (int q = 0; q < kRedBatch; q++) {
               if (s0 + q < nseg) {
                 const float4* src = reinterpret_cast<const float4*>(
-                    a.partial + (((size_t)tile * a.maxseg + s0 + q) * BM + r) * MAXB);
-#pragma unroll
-                for (int j = 0; j < 4; j++) tp[q][j] = __ldcg(src + j);
+                    a.partial + (((size_t)tile * a.maxseg + s0 + q) * BM + r) * MAXB + sb);
+                tp[q][0] = __ldcg(src);
+                tp[q][1] = __ldcg(src + 1);
               }
             }
 #pragma unroll
             for (int q = 0; q < kRedBatch; q++) {
               if (s0 + q < nseg) {
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
+                for (int j = 0; j < 2; j++) {
                   y[4 * j] += tp[q][j].x; y[4 * j + 1] += tp[q][j].y;
                   y[4 * j + 2] += tp[q][j].z; y[4 * j + 3] += tp[q][j].w;
                 }
               }
             }
           }
-          if (et == 0) a.counters[tile] = 0;  // ready for the next launch
+          if (ep == 0) a.counters[tile] = 0;  // ready for the next launch
           if (tlast) tr[10] = globaltimer();
         }
       }
       if (run) {
         if (EPI != EPI_RESID && a.ss_in != nullptr) {
 #pragma unroll
-          for (int b = 0; b < MAXB; b++) y[b] *= s_scale[b];
+          for (int i = 0; i < SPG; i++) y[i] *= s_scale[sb + i];
         }
         if constexpr (EPI == EPI_RESID) {
-          // All 16 streams are computed unconditionally (streams >= B hold zeros) so the
-          // per-stream chains interleave; only the stores are predicated on B.
-          float xs[MAXB];
+          // every stream of the group is computed (streams >= B hold zeros) so the per-stream
+          // chains interleave; only the stores are predicated on B
+          float xs[SPG];
 #pragma unroll
-          for (int b = 0; b < MAXB; b++) {
-            xs[b] = xo[b] + y[b];
-            if (b < a.B) a.x[(size_t)b * a.ldx + n] = xs[b];
+          for (int i = 0; i < SPG; i++) {
+            xs[i] = xo[i] + y[i];
+            if (sb + i < a.B) a.x[(size_t)(sb + i) * a.ldx + n] = xs[i];
           }
           if (tlast) tr[13] = globaltimer();
           if (a.act_next != nullptr) {
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) {
-              const float h = xs[b] * wn;
+            for (int i = 0; i < SPG; i++) {
+              const float h = xs[i] * wn;
               const uint16_t hi = f2bf_bits(h);
               const uint16_t lo = f2bf_bits(h - bf2f(hi));
-              if (b < a.B) {
-                a.act_next[(size_t)b * a.ld_next + n] = hi;
-                a.act_next[(size_t)(MAXB + b) * a.ld_next + n] = lo;
+              if (sb + i < a.B) {
+                a.act_next[(size_t)(sb + i) * a.ld_next + n] = hi;
+                a.act_next[(size_t)(MAXB + sb + i) * a.ld_next + n] = lo;
               }
             }
             if (tlast) tr[14] = globaltimer();
             // per-tile sum of squares of the new x: the same xor butterfly for every stream,
-            // 16 of them interleaved
-            float sq[MAXB];
+            // the group's 8 interleaved
+            float sq[SPG];
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) sq[b] = xs[b] * xs[b];
+            for (int i = 0; i < SPG; i++) sq[i] = xs[i] * xs[i];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-              for (int b = 0; b < MAXB; b++) sq[b] += __shfl_xor_sync(0xffffffffu, sq[b], o);
+              for (int i = 0; i < SPG; i++) sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], o);
             }
             if (lane == 0) {
 #pragma unroll
-              for (int b = 0; b < MAXB; b++) ys[(warp & 3) * YS_LD + b] = sq[b];
+              for (int i = 0; i < SPG; i++) ys[(warp & 3) * YS_LD + sb + i] = sq[i];
             }
             if (tlast) tr[15] = globaltimer();
             epi_sync();
-            if (et < a.B) {
-              const float t4 = (ys[0 * YS_LD + et] + ys[1 * YS_LD + et]) + (ys[2 * YS_LD + et] + ys[3 * YS_LD + et]);
-              a.ss_out[tile * MAXB + et] = t4;
+            if (ep < a.B) {
+              const float t4 = (ys[0 * YS_LD + ep] + ys[1 * YS_LD + ep]) + (ys[2 * YS_LD + ep] + ys[3 * YS_LD + ep]);
+              a.ss_out[tile * MAXB + ep] = t4;
             }
           }
         } else if constexpr (EPI == EPI_QKV) {
 #pragma unroll
-          for (int b = 0; b < MAXB; b++) ys[r * YS_LD + b] = y[b];
+          for (int i = 0; i < SPG; i++) ys[r * YS_LD + sb + i] = y[i];
           epi_sync();
           const int head = tile;  // one 128-row tile = one head
           const bool lo_half = r < 64;
           const int partner = r ^ 64;
           if (head < a.NH + a.NKV) {
             if (tlast) tr[13] = globaltimer();
-            float o[MAXB];
+            float o[SPG];
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) {  // all streams (pos -1 past B), stores predicated
-              const float cs = rcos[b], sn = rsin[b];
-              const float other = ys[partner * YS_LD + b];
-              o[b] = lo_half ? y[b] * cs - other * sn : y[b] * cs + other * sn;
+            for (int i = 0; i < SPG; i++) {  // all streams (pos -1 past B), stores predicated
+              const float other = ys[partner * YS_LD + sb + i];
+              o[i] = lo_half ? y[i] * rcos[i] - other * rsin[i] : y[i] * rcos[i] + other * rsin[i];
             }
             if (tlast) tr[14] = globaltimer();
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) {
-              const int p = s_pos[b];
+            for (int i = 0; i < SPG; i++) {
+              const int b = sb + i, p = s_pos[b];
               if (b < a.B) {
                 if (head < a.NH) {
-                  a.q[(size_t)b * a.ldq + n] = o[b];
+                  a.q[(size_t)b * a.ldq + n] = o[i];
                 } else if (p >= 0 && p < a.S) {
-                  a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o[b]);
+                  a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o[i]);
                 }
               }
             }
           } else {
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) {
-              const int p = s_pos[b];
+            for (int i = 0; i < SPG; i++) {
+              const int b = sb + i, p = s_pos[b];
               if (b < a.B && p >= 0 && p < a.S)
-                a.vc[(((size_t)b * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[b]);
+                a.vc[(((size_t)b * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[i]);
             }
           }
         } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll
-          for (int b = 0; b < MAXB; b++) ys[r * YS_LD + b] = y[b];
+          for (int i = 0; i < SPG; i++) ys[r * YS_LD + sb + i] = y[i];
           epi_sync();
           if (r < 64) {
             const int fcol = tile * 64 + r;
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) {
-              const float g = y[b], u = ys[(r + 64) * YS_LD + b];
+            for (int i = 0; i < SPG; i++) {
+              const float g = y[i], u = ys[(r + 64) * YS_LD + sb + i];
               const float act = g / (1.0f + expf(-g)) * u;
               const uint16_t hi = f2bf_bits(act);
               const uint16_t lo = f2bf_bits(act - bf2f(hi));
-              if (b < a.B) {
-                a.act_out[(size_t)b * a.ld_act + fcol] = hi;
-                a.act_out[(size_t)(MAXB + b) * a.ld_act + fcol] = lo;
+              if (sb + i < a.B) {
+                a.act_out[(size_t)(sb + i) * a.ld_act + fcol] = hi;
+                a.act_out[(size_t)(MAXB + sb + i) * a.ld_act + fcol] = lo;
               }
             }
           }
         } else if constexpr (EPI == EPI_LOGITS) {
-          unsigned long long key[MAXB];
+          unsigned long long key[SPG];
 #pragma unroll
-          for (int b = 0; b < MAXB; b++) {
-            key[b] = 0;
+          for (int i = 0; i < SPG; i++) {
+            key[i] = 0;
             if (n < a.V) {
-              if (b < a.B) a.logits[(size_t)b * a.V + n] = y[b];
-              key[b] = ((unsigned long long)orderable(y[b]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
+              if (sb + i < a.B) a.logits[(size_t)(sb + i) * a.V + n] = y[i];
+              key[i] = ((unsigned long long)orderable(y[i]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
             }
           }
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) {
-              const unsigned long long t = __shfl_xor_sync(0xffffffffu, key[b], o);
-              key[b] = t > key[b] ? t : key[b];
+            for (int i = 0; i < SPG; i++) {
+              const unsigned long long t = __shfl_xor_sync(0xffffffffu, key[i], o);
+              key[i] = t > key[i] ? t : key[i];
             }
           }
           if (lane == 0) {
 #pragma unroll
-            for (int b = 0; b < MAXB; b++) s_red[(warp & 3) * MAXB + b] = key[b];
+            for (int i = 0; i < SPG; i++) s_red[(warp & 3) * MAXB + sb + i] = key[i];
           }
           epi_sync();
-          if (et < a.B) {
-            unsigned long long k = s_red[et];
-            for (int w = 1; w < 4; w++) k = s_red[w * MAXB + et] > k ? s_red[w * MAXB + et] : k;
-            atomicMax(&a.best[et], k);
+          if (ep < a.B) {
+            unsigned long long k = s_red[ep];
+            for (int w = 1; w < 4; w++) k = s_red[w * MAXB + ep] > k ? s_red[w * MAXB + ep] : k;
+            atomicMax(&a.best[ep], k);
           }
         }
         if (tlast) tr[11] = globaltimer();
@@ -486,7 +491,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       }
       f = fend;
     }
-    if (tr != nullptr && et == 0) tr[6] = globaltimer();
+    if (tr != nullptr && ep == 0) tr[6] = globaltimer();
     tc_fence_before();
     mbar_arrive(epi_done);
   }

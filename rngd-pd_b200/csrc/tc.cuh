@@ -167,6 +167,24 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Two 8-column pieces of the 32x32b layout (columns [c0, c0+8) and [c1, c1+8) of this warp's
+// 32 lanes), one wait for both.
+__device__ __forceinline__ void tmem_ld_32x32b_2x8(uint32_t taddr0, uint32_t taddr1, float* v0, float* v1) {
+  uint32_t a[8], b[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7])
+               : "r"(taddr0));
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7])
+               : "r"(taddr1));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    v0[i] = __uint_as_float(a[i]);
+    v1[i] = __uint_as_float(b[i]);
+  }
+}
+
 // Programmatic dependent launch: wait until the preceding grid's memory is visible.
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
