@@ -664,6 +664,15 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_s = float(t.item())
+    # a bounded device wait that ran out leaves a wrong result and a step cut short by it
+    from rngd_pd import _lib
+    t = torch.tensor([_lib.device_status()], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    status = int(t.item())
+    if status != 0:
+        raise RuntimeError(f"device status {status} after the timed steps: a bounded wait ran out, "
+                           "so these timings are not valid")
 
     roof = gemm_roofline(eng) if rank == 0 else None
     prefill = prefill_measure(eng) if rank == 0 else None

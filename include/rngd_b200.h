@@ -88,8 +88,9 @@ typedef struct rngd_decode_io {
   float* ss;            /* fp32 [H/128][16] per-128-column sums of squares of x (RMSNorm) */
   float* logits;        /* fp32 [B][V] */
   float* attn_part;     /* fp32 scratch [B][NH][S/128][HD+2] */
-  float* partial;       /* fp32 split-K scratch, rngd_decode_workspace() floats */
-  int32_t* counters;    /* int32 tile counters, rngd_decode_workspace() entries, zeroed once */
+  float* partial;       /* split-tile scratch, rngd_decode_workspace() 4-byte units (16-byte aligned),
+                           zeroed once */
+  int32_t* counters;    /* split-tile epochs, rngd_decode_workspace() int32 entries, zeroed once */
   uint64_t* best;       /* [16] argmax keys */
   int32_t* next;        /* device [B] greedy next tokens */
 } rngd_decode_io_t;
@@ -124,7 +125,7 @@ int rngd_decode_advance(const rngd_decode_io_t* io, rngd_stream_t stream);
  * row stride ldx), e.g. the last prompt position of a prefill
  * (engines/prefill_full.py:265-270 _next_token).  act: zeroed bf16 [32][H];
  * ss: fp32 [H/128][16]; logits [rows][V]; best [16]; next [rows]; partial /
- * counters from rngd_lmhead_workspace (counters zeroed once). */
+ * counters from rngd_lmhead_workspace (both zeroed once, one pair per caller). */
 int rngd_lmhead_rows(const rngd_model_t* m, const float* x, int ldx, int rows, void* act, float* ss, float* logits,
                      uint64_t* best, int32_t* next, float* partial, int32_t* counters, rngd_stream_t stream);
 int rngd_lmhead_workspace(const rngd_model_t* m, size_t* partial_floats, size_t* counters);
@@ -221,7 +222,8 @@ int rngd_gemv_bf16(const void* W, int N, int K, const float* X, int ldx, int B, 
 /* Tensor-core form of the same op (the one the decode step uses): Y[b][n] +=
  * sum_k W[n][k] * X[b][k] through tcgen05 with the fp32 X split into bf16
  * hi + lo operand rows.  act: zeroed bf16 scratch [32][K]; partial/counters:
- * split-K scratch of rngd_tc_gemv_workspace() (counters zeroed once).
+ * split-K scratch of rngd_tc_gemv_workspace() (both zeroed once; one pair
+ * per (N, K) shape).
  * prep = 0 reuses the operand already in act (X is not read).
  * N % 128 == 0, K % 64 == 0, B <= 16. */
 int rngd_tc_gemv(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy, void* act,

@@ -12,8 +12,15 @@
 // Scheduling (stream-K).  One CTA per SM.  The GEMM's tiles x K-blocks are laid
 // end to end and cut into one equal contiguous range per CTA, so every SM
 // streams the same number of weight bytes and the TMA ring never drains between
-// tiles.  A tile cut between CTAs leaves one fp32 partial per piece; the CTA
-// that finishes a tile's last piece sums the pieces in K order.  The cut
+// tiles.  A tile cut between CTAs is summed by its first owner (the CTA holding
+// the tile's first K blocks, which it reaches at the end of its range, when
+// the other owners are finishing too).  Each other owner stores its piece as
+// 64-bit words {fp32 value, flag}; a single-copy-atomic word needs no fence,
+// so the first owner polls the words of the pieces it misses and adds them in
+// K order.  The flag is (shape tag, tile epoch + 1): the epoch is a per-shape,
+// per-tile counter that the first owner advances once it has every piece, so
+// a word left by an earlier launch (older epoch) or another shape sharing the
+// scratch (other tag) never reads as ready and nothing needs clearing.  The cut
 // depends only on (N, K, CTA count), never on B, so a stream's result is
 // deterministic and independent of what else is batched with it.
 //
@@ -53,14 +60,15 @@ constexpr int EPI_THREADS = 256;       // two warpgroups, each 8 of the 16 strea
 constexpr int SPG = MAXB / 2;          // streams per epilogue warpgroup
 constexpr int THREADS = 64 + EPI_THREADS;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int TMEM_COLS = 64;          // two 32-column accumulators
-constexpr int kRedBatch = 6;           // split-tile pieces whose partials are loaded together
+constexpr int kRedBatch = 5;           // split-tile pieces whose partials are loaded together
 
 enum Epi : int { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
 
 struct GemmArgs {
   int N, K, nkb, tiles, total, maxseg, layer, B;
-  float* partial;   // [tiles][maxseg][128][16]
-  int* counters;    // [tiles]
+  float* partial;   // [tiles][maxseg][8 stream pairs][128 rows][2] words {fp32 value, flag}, zeroed once
+  int* counters;    // [tiles] epochs of this shape's split tiles, zeroed once
+  int tag;          // 1..15, distinct for GEMM shapes sharing `partial`
   // rms scale of the result (QKV, SWIGLU, LOGITS); ss_in == nullptr -> no scaling
   const float* ss_in;  // [ss_tiles][16] per-128-column sums of squares of x
   int ss_tiles;
@@ -89,7 +97,8 @@ struct GemmArgs {
   int V;
   // optional per-CTA timeline (ns, %globaltimer), 16 entries per CTA: start, operand ready, last
   // TMA issued, last stage arrived, last MMA committed, last accumulator ready, epilogue done,
-  // end; then for the last segment: accumulator read, split-tile count done, partials summed,
+  // end; then for the last segment: accumulator read, poll rounds of a split tile's first owner
+// (a count, not a time), later pieces summed,
   // epilogue stores issued, segment done; nullptr = off
   unsigned long long* trace;
 };
@@ -105,6 +114,18 @@ __device__ __forceinline__ uint32_t orderable(float f) {
 }
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// One 16-byte store of two {value, flag} words of a split-tile piece.  Each 64-bit word is
+// single-copy atomic, so a reader that sees the flag sees the value stored with it.
+__device__ __forceinline__ void st_piece(unsigned long long* p, uint32_t flag, float v0, float v1) {
+  const unsigned long long w0 = ((unsigned long long)flag << 32) | __float_as_uint(v0);
+  const unsigned long long w1 = ((unsigned long long)flag << 32) | __float_as_uint(v1);
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+}
+__device__ __forceinline__ void ld_piece(const unsigned long long* p, unsigned long long& w0,
+                                         unsigned long long& w1) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+}
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -123,7 +144,6 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
   uint64_t* acc_empty = acc_full + 2;    // [2]
   uint64_t* epi_done = acc_empty + 2;    // the 128 epilogue threads are past their last TMEM read
   uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + kBarBytes);
-  int* s_last = (int*)(tmem_slot + 1);
   float* s_scale = (float*)((uint8_t*)full + kBarBytes + 64);  // [16]
   int* s_pos = (int*)((uint8_t*)full + kBarBytes + 128);       // [16]
   float* ys = (float*)((uint8_t*)full + kBarBytes + 192);
@@ -279,10 +299,35 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
       // accumulator is still being computed (only the tile's reducing CTA writes x[.][n])
       float xo[SPG];
       float wn = 0.f;
+      // epoch of the tile's split (read before the accumulator wait; only the tile's first owner
+      // advances it, after every piece of this launch was stored under the value read here)
+      const int epoch = a.maxseg > 1 ? __ldcg(a.counters + tile) : 0;
       if constexpr (EPI == EPI_RESID) {
 #pragma unroll
         for (int i = 0; i < SPG; i++) xo[i] = sb + i < a.B ? a.x[(size_t)(sb + i) * a.ldx + n] : 0.f;
         if (a.act_next != nullptr) wn = a.w_next[n];
+      }
+      const int first = owner_of(tstart, a.total, G), last = owner_of(tstart + a.nkb - 1, a.total, G);
+      const int nseg = last - first + 1;
+      const int slot = cta - first;
+      // piece layout [stream pair][row][2 words]: the 32 rows of a warp read or write 512
+      // contiguous bytes per instruction.  This thread's pairs are sb/2 .. sb/2 + SPG/2 - 1.
+      constexpr size_t kPieceWords = (size_t)BM * MAXB;
+      constexpr size_t kPairWords = (size_t)BM * 2;
+      unsigned long long* pw = reinterpret_cast<unsigned long long*>(a.partial) +
+                               (size_t)tile * a.maxseg * kPieceWords + ((size_t)(sb / 2) * BM + r) * 2;
+      // a tile's first owner reads the first batch of later pieces while its own accumulator is
+      // still being computed: pieces already stored cost no round trip after it
+      unsigned long long w[kRedBatch][SPG];
+      if (nseg > 1 && slot == 0) {
+#pragma unroll
+        for (int q = 0; q < kRedBatch; q++) {
+          if (1 + q < nseg) {
+#pragma unroll
+            for (int j = 0; j < SPG / 2; j++)
+              ld_piece(pw + (size_t)(1 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
+          }
+        }
       }
       mbar_wait(&acc_full[buf], (uint32_t)(seg >> 1) & 1u, ST_EPI_WAIT, &g_status_decode);
       if (tr != nullptr && ep == 0 && fend == f1) tr[5] = globaltimer();
@@ -299,59 +344,75 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
 #pragma unroll
       for (int i = 0; i < SPG; i++) y[i] = vh[i] + vl[i];
 
-      const int first = owner_of(tstart, a.total, G), last = owner_of(tstart + a.nkb - 1, a.total, G);
-      const int nseg = last - first + 1;
       bool run = true;
       if (nseg > 1) {
-        const int slot = cta - first;
-        float4* dst =
-            reinterpret_cast<float4*>(a.partial + (((size_t)tile * a.maxseg + slot) * BM + r) * MAXB + sb);
-        __stcg(dst, make_float4(y[0], y[1], y[2], y[3]));
-        __stcg(dst + 1, make_float4(y[4], y[5], y[6], y[7]));
-        // The barrier orders every epilogue thread's partial stores before thread 0's counter
-        // update, whose release (gpu scope) publishes them; the last arriver's acquire on the
-        // same update, followed by the barrier, orders its threads' partial reads after all
-        // pieces were written.  No full fence on either side.
-        epi_sync();
-        if (ep == 0) {
-          int old;
-          asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
-                       : "=r"(old)
-                       : "l"(a.counters + tile)
-                       : "memory");
-          *s_last = (old == nseg - 1);
-        }
-        epi_sync();
-        run = *s_last != 0;
-        if (tlast) tr[9] = globaltimer();
-        if (run) {
+        const uint32_t flag = ((uint32_t)a.tag << 28) | ((uint32_t)(epoch + 1) & 0x0FFFFFFFu);
+        if (slot > 0) {
+          // a later piece of the tile: publish it, no wait
+          unsigned long long* dst = pw + (size_t)slot * kPieceWords;
 #pragma unroll
-          for (int i = 0; i < SPG; i++) y[i] = 0.f;
-          // pieces summed in K order; every piece's loads issued before the first add (one L2
-          // round trip for up to kRedBatch pieces instead of one per piece)
-          for (int s0 = 0; s0 < nseg; s0 += kRedBatch) {
-            float4 tp[kRedBatch][2];
+          for (int j = 0; j < SPG / 2; j++) st_piece(dst + j * kPairWords, flag, y[2 * j], y[2 * j + 1]);
+          run = false;
+        } else {
+          // the tile's first piece is this CTA's own: wait (bounded) until all of this thread's
+          // words of the later pieces carry the flag, re-reading every missing piece together
+          // (one L2 round trip per poll, not per piece), then add them in K order
+          bool ok = true;
+          for (int s0 = 1; s0 < nseg; s0 += kRedBatch) {
+            uint32_t pend = 0;
 #pragma unroll
             for (int q = 0; q < kRedBatch; q++) {
               if (s0 + q < nseg) {
-                const float4* src = reinterpret_cast<const float4*>(
-                    a.partial + (((size_t)tile * a.maxseg + s0 + q) * BM + r) * MAXB + sb);
-                tp[q][0] = __ldcg(src);
-                tp[q][1] = __ldcg(src + 1);
-              }
-            }
+                pend |= 1u << q;
+                if (s0 > 1) {  // the first batch was read before the accumulator wait
 #pragma unroll
-            for (int q = 0; q < kRedBatch; q++) {
-              if (s0 + q < nseg) {
-#pragma unroll
-                for (int j = 0; j < 2; j++) {
-                  y[4 * j] += tp[q][j].x; y[4 * j + 1] += tp[q][j].y;
-                  y[4 * j + 2] += tp[q][j].z; y[4 * j + 3] += tp[q][j].w;
+                  for (int j = 0; j < SPG / 2; j++)
+                    ld_piece(pw + (size_t)(s0 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
                 }
               }
             }
+            uint64_t t0 = 0;
+            int polls = 0;
+            while (true) {
+#pragma unroll
+              for (int q = 0; q < kRedBatch; q++) {
+                if (pend & (1u << q)) {
+                  bool ready = true;
+#pragma unroll
+                  for (int i = 0; i < SPG; i++) ready &= (uint32_t)(w[q][i] >> 32) == flag;
+                  if (ready) pend &= ~(1u << q);
+                }
+              }
+              if (pend == 0 || !ok) break;
+              polls++;
+              const uint64_t now = globaltimer();
+              if (t0 == 0) {
+                t0 = now;
+              } else if (now - t0 > kWaitTimeoutNs) {
+                atomicCAS(&g_status_decode, 0, ST_PIECE_WAIT);
+                ok = false;
+                break;
+              }
+#pragma unroll
+              for (int q = 0; q < kRedBatch; q++) {
+                if (pend & (1u << q)) {
+#pragma unroll
+                  for (int j = 0; j < SPG / 2; j++)
+                    ld_piece(pw + (size_t)(s0 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
+                }
+              }
+            }
+            if (tlast) tr[9] = (unsigned long long)polls;
+#pragma unroll
+            for (int q = 0; q < kRedBatch; q++) {
+              if (s0 + q < nseg) {
+#pragma unroll
+                for (int i = 0; i < SPG; i++) y[i] += __uint_as_float((uint32_t)w[q][i]);
+              }
+            }
           }
-          if (ep == 0) a.counters[tile] = 0;  // ready for the next launch
+          // every piece of this launch is in: the next launch uses the next epoch
+          if (ep == 0) a.counters[tile] = epoch + 1;
           if (tlast) tr[10] = globaltimer();
         }
       }
@@ -706,6 +767,7 @@ static int launch_skgemm(const void* W, int L, int layer, int N, int K, const vo
   a.layer = layer;
   RNGD_REQUIRE(a.total >= grid, "decode GEMM: %d K blocks cannot feed %d CTAs", a.total, grid);
   RNGD_REQUIRE(a.maxseg == 1 || (a.partial && a.counters), "decode GEMM: split tiles need partial/counters");
+  RNGD_REQUIRE(a.tag >= 1 && a.tag <= 15, "decode GEMM: shape tag %d outside 1..15", a.tag);
   seq_trace(&a);
   static std::atomic<unsigned long long> attr_set{0};  // one per EPI instantiation
   RNGD_TRY(set_smem_limit_once((const void*)skgemm_kernel<EPI>, (int)kSmemBytes, &attr_set,
@@ -732,7 +794,7 @@ int launch_embed(const void* emb, const int32_t* toks, int H, int V, float* x, i
 static void shape_workspace(int N, int K, size_t* pf, size_t* ct) {
   const int ms = max_segments(N, K, gemm_grid(N, K));
   const size_t tiles = (size_t)(N + BM - 1) / BM;
-  *pf = ms > 1 ? tiles * ms * BM * MAXB : 0;
+  *pf = ms > 1 ? 2 * tiles * ms * BM * MAXB : 0;  // 4-byte units of the 64-bit piece words
   *ct = ms > 1 ? tiles : 0;
 }
 
@@ -754,18 +816,30 @@ static int check_tc_io(const rngd_model_t* m, const rngd_decode_io_t* io) {
   return RNGD_OK;
 }
 
-extern "C" int rngd_decode_workspace(const rngd_model_t* m, int S, size_t* partial_floats, size_t* counters,
-                                     size_t* act_cols, size_t* act2_cols) {
-  RNGD_REQUIRE(m && partial_floats && counters && act_cols && act2_cols, "workspace: null argument");
+// The decode step's GEMM shapes: QKV, O, gate/up, down, LM head.  They share one partial
+// scratch (their flags carry tag = index + 1) and each has its own run of tile epochs in the
+// counters array, starting at off[index].
+static void decode_shapes(const rngd_model_t* m, size_t off[5], size_t* pf_max, size_t* ct_sum) {
   const int QN = m->NH * m->HD, KN = m->NKV * m->HD;
   const int shapes[5][2] = {{QN + 2 * KN, m->H}, {m->H, QN}, {2 * m->M, m->H}, {m->H, m->M}, {m->V, m->H}};
   size_t pf = 0, ct = 0;
-  for (auto& sh : shapes) {
+  for (int i = 0; i < 5; i++) {
     size_t p, c;
-    shape_workspace(sh[0], sh[1], &p, &c);
+    shape_workspace(shapes[i][0], shapes[i][1], &p, &c);
+    off[i] = ct;
     pf = pf > p ? pf : p;
-    ct = ct > c ? ct : c;
+    ct += c;
   }
+  *pf_max = pf;
+  *ct_sum = ct;
+}
+
+extern "C" int rngd_decode_workspace(const rngd_model_t* m, int S, size_t* partial_floats, size_t* counters,
+                                     size_t* act_cols, size_t* act2_cols) {
+  RNGD_REQUIRE(m && partial_floats && counters && act_cols && act2_cols, "workspace: null argument");
+  const int QN = m->NH * m->HD;
+  size_t off[5], pf, ct;
+  decode_shapes(m, off, &pf, &ct);
   *partial_floats = pf;
   *counters = ct;
   *act_cols = (size_t)(m->H > QN ? m->H : QN);
@@ -800,6 +874,7 @@ extern "C" int rngd_tc_gemv(const void* W, int N, int K, const float* X, int ldx
   a.B = B;
   a.partial = partial;
   a.counters = counters;
+  a.tag = 6;
   a.x = Y;
   a.ldx = ldy;
   a.trace = g_trace;
@@ -824,6 +899,8 @@ extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t*
   const int B = io->B;
   const int ld_act = H > QN ? H : QN;
   const size_t lane_elems = (size_t)m->NKV * io->S * m->HD;
+  size_t off[5], pf, ct;
+  decode_shapes(m, off, &pf, &ct);
   for (int l = layer0; l < layer1; l++) {
     uint16_t* kc = (uint16_t*)io->kcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
     uint16_t* vc = (uint16_t*)io->vcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
@@ -838,18 +915,22 @@ extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t*
     // attention block: io->act holds x * n1[l] (written by the prologue or the previous layer)
     a.pos = io->pos; a.inv = m->inv_freq; a.q = io->q; a.ldq = QN; a.kc = kc; a.vc = vc;
     a.NH = m->NH; a.NKV = m->NKV; a.S = io->S;
+    a.counters = io->counters + off[0]; a.tag = 1;
     RNGD_TRY(launch_skgemm<EPI_QKV>(m->wqkv, m->L, l, NQKV, H, io->act, ld_act, a, s));
     RNGD_TRY(launch_attn_decode_act(io->q, QN, kc, vc, io->pos, B, m->NH, m->NKV, m->HD, io->S, io->attn_part,
                                     io->act_o, QN, s));
     // O projection + residual; writes x * n2[l] for the MLP
     a.x = io->x; a.ldx = H;
     a.w_next = m->n2 + (size_t)l * H; a.act_next = (uint16_t*)io->act; a.ld_next = ld_act; a.ss_out = io->ss;
+    a.counters = io->counters + off[1]; a.tag = 2;
     RNGD_TRY(launch_skgemm<EPI_RESID>(m->wo, m->L, l, H, QN, io->act_o, QN, a, s));
     // MLP block
     a.act_out = (uint16_t*)io->act2; a.ld_act = Mi;
+    a.counters = io->counters + off[2]; a.tag = 3;
     RNGD_TRY(launch_skgemm<EPI_SWIGLU>(m->wgu, m->L, l, 2 * Mi, H, io->act, ld_act, a, s));
     // down projection + residual; writes x * n1[l+1] (or the final norm) for what follows
     a.w_next = l + 1 < m->L ? m->n1 + (size_t)(l + 1) * H : m->norm;
+    a.counters = io->counters + off[3]; a.tag = 4;
     RNGD_TRY(launch_skgemm<EPI_RESID>(m->wd, m->L, l, H, Mi, io->act2, Mi, a, s));
   }
   return RNGD_OK;
@@ -862,9 +943,12 @@ extern "C" int rngd_decode_lmhead(const rngd_model_t* m, const rngd_decode_io_t*
   const int ld_act = H > QN ? H : QN;
   // io->act holds x * norm from the last layer's residual epilogue
   GemmArgs a = {};
+  size_t off[5], pf, ct;
+  decode_shapes(m, off, &pf, &ct);
   a.B = io->B;
   a.partial = io->partial;
-  a.counters = io->counters;
+  a.counters = io->counters + off[4];
+  a.tag = 5;
   a.ss_in = io->ss;
   a.ss_tiles = H / BM;
   a.eps = m->eps;
@@ -902,6 +986,7 @@ extern "C" int rngd_lmhead_rows(const rngd_model_t* m, const float* x, int ldx, 
   a.B = rows;
   a.partial = partial;
   a.counters = counters;
+  a.tag = 5;
   a.ss_in = ss;
   a.ss_tiles = H / BM;
   a.eps = m->eps;
