@@ -87,7 +87,7 @@ typedef struct rngd_decode_io {
   void* act2;           /* bf16 [32][M] down-projection operand (zeroed at allocation) */
   float* ss;            /* fp32 [H/128][16] per-128-column sums of squares of x (RMSNorm) */
   float* logits;        /* fp32 [B][V] */
-  float* attn_part;     /* fp32 scratch [B][NH][S/128][HD+2] */
+  float* attn_part;     /* attention scratch, rngd_decode_attn_workspace() 4-byte units, zeroed once */
   float* partial;       /* split-tile scratch, rngd_decode_workspace() 4-byte units (16-byte aligned),
                            zeroed once */
   int32_t* counters;    /* split-tile epochs, rngd_decode_workspace() int32 entries, zeroed once */
@@ -98,6 +98,9 @@ typedef struct rngd_decode_io {
 /* Sizes of the decode scratch buffers for a model (shape-only; independent of B). */
 int rngd_decode_workspace(const rngd_model_t* m, int S, size_t* partial_floats, size_t* counters,
                           size_t* act_cols, size_t* act2_cols);
+/* Size of io->attn_part for streams 0..Bcap-1 (Bcap <= 16) of S cache positions: chunk
+ * records of the fused decode attention plus an epoch per (stream, kv head). */
+int rngd_decode_attn_workspace(const rngd_model_t* m, int Bcap, int S, size_t* attn_units);
 /* Device status word of the bounded waits (0 = none timed out); reset clears it. */
 int rngd_device_status(int* status, int reset);
 

@@ -181,15 +181,40 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
                : "memory");
 }
 
+__device__ int g_status_attn = 0;  // this file's bounded-wait status word
+
+// One 64-bit {value, flag} word of a fused-attention chunk record; single-copy atomic, so a
+// reader that sees the flag sees the value stored with it.
+__device__ __forceinline__ void st_rec(unsigned long long* p, float v, uint32_t flag) {
+  const unsigned long long w = ((unsigned long long)flag << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_rec(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+constexpr int kRecChunks = 3;  // chunk records the fused combine reads per poll round
+
 // One CTA = (128-position chunk, kv head, stream) and the G=4 query heads of the kv head.
-// The chunk's K and V rows are staged into shared memory with cp.async first (all loads in
-// flight at once), then scores (one position per thread), softmax statistics and P.V run
-// from shared memory.
-__global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restrict__ q, int ldq,
-                                                           const uint16_t* __restrict__ kc,
-                                                           const uint16_t* __restrict__ vc,
-                                                           const int32_t* __restrict__ pos, int NH,
-                                                           int NKV, int S, float* __restrict__ part) {
+// The chunk's K rows, then its V rows, are staged into shared memory with cp.async (two
+// groups, all loads in flight at once); the scores (one position per thread) and softmax
+// statistics run as soon as K has landed, P.V once V has.
+//
+// FUSED = false writes a partial record (o[HD], m, l per head) for attn_combine_kernel.
+// FUSED = true (the decode step) ends with the combine in the same grid: chunks 1.. store their
+// records as {value, flag} words, flag = epoch of (stream, kv head) + 1; chunk 0 (the lowest
+// CTA index of the group, so it only ever waits on CTAs dispatched after it) polls them with a
+// bounded wait, combines every chunk in chunk order exactly as attn_combine_kernel does, writes
+// the hi/lo operand of the O projection and advances the epoch, so records of earlier launches
+// (older epochs) never read as ready and nothing needs clearing.
+template <bool FUSED>
+__device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq, const uint16_t* __restrict__ kc,
+                                           const uint16_t* __restrict__ vc, const int32_t* __restrict__ pos,
+                                           int NH, int NKV, int S, float* __restrict__ part,
+                                           unsigned long long* __restrict__ recw, int* __restrict__ epochs,
+                                           uint16_t* __restrict__ act, int ld_act) {
   extern __shared__ __align__(16) uint8_t attn_smem[];
   uint8_t* sK = attn_smem;
   uint8_t* sV = sK + kChunk * kRowBytes;
@@ -206,14 +231,18 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
   grid_dep_launch();  // every CTA of this grid is running: the next kernel may start its prologue
   const int P = min(pos[b] + 1, S);
   const int s0 = c * kChunk;
-  float* rec0 = part + (((size_t)b * NH + kvh * kG) * nchunk + c) * PS;
+  float* rec0 = FUSED ? nullptr : part + (((size_t)b * NH + kvh * kG) * nchunk + c) * PS;
+  int epoch = 0;
+  if constexpr (FUSED) epoch = __ldcg(epochs + (size_t)b * NKV + kvh);
   if (s0 >= P) {
-    if (t < kG) {
-      float* rec = rec0 + (size_t)t * nchunk * PS;
-      rec[kHD] = -INFINITY;
-      rec[kHD + 1] = 0.f;
+    if constexpr (!FUSED) {
+      if (t < kG) {
+        float* rec = rec0 + (size_t)t * nchunk * PS;
+        rec[kHD] = -INFINITY;
+        rec[kHD + 1] = 0.f;
+      }
     }
-    return;
+    return;  // fused: chunk 0 reads only the chunks that hold positions
   }
   const int n = min(kChunk, P - s0);
   const size_t head_base = ((size_t)b * NKV + kvh) * (size_t)S * kHD;
@@ -222,12 +251,16 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
   for (int i = t; i < n * 16; i += 128) {
     const int j = i >> 4, c16 = (i & 15) * 16;
     cp_async16(sK + j * kRowBytes + c16, kg + (size_t)j * 256 + c16);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int i = t; i < n * 16; i += 128) {
+    const int j = i >> 4, c16 = (i & 15) * 16;
     cp_async16(sV + j * kRowBytes + c16, vg + (size_t)j * 256 + c16);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   const float scale = 0.08838834764831845f;  // 1/sqrt(128) in fp32
   for (int i = t; i < kG * kHD; i += 128) qs[i] = q[(size_t)b * ldq + (size_t)(kvh * kG) * kHD + i];
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  asm volatile("cp.async.wait_group 1;" ::: "memory");  // the K rows (V may still be in flight)
   __syncthreads();
 
   // scores: thread t = position s0 + t
@@ -268,6 +301,7 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
     const float ssum = warp_sum(p);
     if (lane == 0) red[g * 4 + warp] = ssum;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // the V rows
   __syncthreads();
   // P.V: thread t owns dims dg*8..dg*8+7 for positions pg, pg+8, ...; partials reduced over pg
   const int dg = t & 15, pg = t >> 4;
@@ -294,18 +328,155 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
     *reinterpret_cast<float4*>(dst + 4) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
   }
   __syncthreads();
+  float acc[kG], lsum[kG];
 #pragma unroll
   for (int g = 0; g < kG; g++) {
-    float acc = 0.f;
+    float a = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; k++) acc += ored[(k * kG + g) * kHD + t];
-    float* rec = rec0 + (size_t)g * nchunk * PS;
-    rec[t] = acc;
-    if (t == 0) {
-      rec[kHD] = mx[g];
-      rec[kHD + 1] = (red[g * 4 + 0] + red[g * 4 + 1]) + (red[g * 4 + 2] + red[g * 4 + 3]);
-    }
+    for (int k = 0; k < 8; k++) a += ored[(k * kG + g) * kHD + t];
+    acc[g] = a;
+    lsum[g] = (red[g * 4 + 0] + red[g * 4 + 1]) + (red[g * 4 + 2] + red[g * 4 + 3]);
   }
+  if constexpr (!FUSED) {
+#pragma unroll
+    for (int g = 0; g < kG; g++) {
+      float* rec = rec0 + (size_t)g * nchunk * PS;
+      rec[t] = acc[g];
+      if (t == 0) {
+        rec[kHD] = mx[g];
+        rec[kHD + 1] = lsum[g];
+      }
+    }
+  } else {
+    const uint32_t flag = (uint32_t)epoch + 1u;
+    // records of this (stream, kv head): [chunk][g][PS] words
+    unsigned long long* grp = recw + ((size_t)b * NKV + kvh) * nchunk * kG * PS;
+    if (c > 0) {
+      unsigned long long* rc = grp + (size_t)c * kG * PS;
+#pragma unroll
+      for (int g = 0; g < kG; g++) {
+        st_rec(rc + g * PS + t, acc[g], flag);
+        if (t == 0) {
+          st_rec(rc + g * PS + kHD, mx[g], flag);
+          st_rec(rc + g * PS + kHD + 1, lsum[g], flag);
+        }
+      }
+      return;
+    }
+    // chunk 0: the combine needs the max of m over all chunks before the weighted sums, so it
+    // polls the records of chunks 1..nc-1 (kRecChunks per round) for the max, then adds them
+    // in chunk order from the words already read (re-read in batches for longer caches)
+    const int nc = (P + kChunk - 1) / kChunk;
+    float M[kG], L[kG], O[kG];
+#pragma unroll
+    for (int g = 0; g < kG; g++) M[g] = fmaxf(-INFINITY, mx[g]);
+    unsigned long long w[kRecChunks][kG][3];
+    auto load_batch = [&](int c0, uint32_t mask) {
+#pragma unroll
+      for (int k = 0; k < kRecChunks; k++) {
+        if (mask & (1u << k)) {
+          const unsigned long long* rc = grp + (size_t)(c0 + k) * kG * PS;
+#pragma unroll
+          for (int g = 0; g < kG; g++) {
+            w[k][g][0] = ld_rec(rc + g * PS + t);
+            w[k][g][1] = ld_rec(rc + g * PS + kHD);
+            w[k][g][2] = ld_rec(rc + g * PS + kHD + 1);
+          }
+        }
+      }
+    };
+    bool ok = true;
+    for (int c0 = 1; c0 < nc; c0 += kRecChunks) {  // pass 1: wait (bounded) and take the max
+      uint32_t pend = 0;
+#pragma unroll
+      for (int k = 0; k < kRecChunks; k++)
+        if (c0 + k < nc) pend |= 1u << k;
+      load_batch(c0, pend);
+      uint64_t t0 = 0;
+      while (true) {
+#pragma unroll
+        for (int k = 0; k < kRecChunks; k++) {
+          if (pend & (1u << k)) {
+            bool ready = true;
+#pragma unroll
+            for (int g = 0; g < kG; g++)
+#pragma unroll
+              for (int e = 0; e < 3; e++) ready &= (uint32_t)(w[k][g][e] >> 32) == flag;
+            if (ready) pend &= ~(1u << k);
+          }
+        }
+        if (pend == 0 || !ok) break;
+        const uint64_t now = globaltimer();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kWaitTimeoutNs) {
+          atomicCAS(&g_status_attn, 0, ST_ATTN_WAIT);
+          ok = false;
+          break;
+        }
+        load_batch(c0, pend);
+      }
+#pragma unroll
+      for (int k = 0; k < kRecChunks; k++)
+        if (c0 + k < nc)
+#pragma unroll
+          for (int g = 0; g < kG; g++) M[g] = fmaxf(M[g], __uint_as_float((uint32_t)w[k][g][1]));
+    }
+    // pass 2: exp-weighted sums in chunk order, chunk 0 from registers
+#pragma unroll
+    for (int g = 0; g < kG; g++) {
+      const float f = expf(mx[g] - M[g]);
+      L[g] = fmaf(lsum[g], f, 0.f);
+      O[g] = fmaf(acc[g], f, 0.f);
+    }
+    for (int c0 = 1; c0 < nc; c0 += kRecChunks) {
+      uint32_t have = 0;
+#pragma unroll
+      for (int k = 0; k < kRecChunks; k++)
+        if (c0 + k < nc) have |= 1u << k;
+      if (nc > 1 + kRecChunks) load_batch(c0, have);  // else w still holds this (only) batch
+#pragma unroll
+      for (int k = 0; k < kRecChunks; k++) {
+        if (have & (1u << k)) {
+#pragma unroll
+          for (int g = 0; g < kG; g++) {
+            const float m = __uint_as_float((uint32_t)w[k][g][1]);
+            if (m == -INFINITY) continue;
+            const float f = expf(m - M[g]);
+            L[g] = fmaf(__uint_as_float((uint32_t)w[k][g][2]), f, L[g]);
+            O[g] = fmaf(__uint_as_float((uint32_t)w[k][g][0]), f, O[g]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kG; g++) {
+      const float ov = O[g] / L[g];
+      const size_t col = (size_t)(kvh * kG + g) * kHD + t;
+      const uint16_t hi = f2bf_bits(ov);
+      act[(size_t)b * ld_act + col] = hi;
+      act[(size_t)(16 + b) * ld_act + col] = f2bf_bits(ov - bf2f(hi));
+    }
+    if (t == 0) epochs[(size_t)b * NKV + kvh] = epoch + 1;  // read by the next launch only
+  }
+}
+
+__global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restrict__ q, int ldq,
+                                                           const uint16_t* __restrict__ kc,
+                                                           const uint16_t* __restrict__ vc,
+                                                           const int32_t* __restrict__ pos, int NH,
+                                                           int NKV, int S, float* __restrict__ part) {
+  attn_chunk<false>(q, ldq, kc, vc, pos, NH, NKV, S, part, nullptr, nullptr, nullptr, 0);
+}
+
+__global__ void __launch_bounds__(128) attn_fused_kernel(const float* __restrict__ q, int ldq,
+                                                         const uint16_t* __restrict__ kc,
+                                                         const uint16_t* __restrict__ vc,
+                                                         const int32_t* __restrict__ pos, int NH, int NKV,
+                                                         int S, unsigned long long* __restrict__ recw,
+                                                         int* __restrict__ epochs, uint16_t* __restrict__ act,
+                                                         int ld_act) {
+  attn_chunk<true>(q, ldq, kc, vc, pos, NH, NKV, S, nullptr, recw, epochs, act, ld_act);
 }
 
 // Combines the chunk partials of one (stream, head) in chunk order.
@@ -360,9 +531,39 @@ int launch_attn_decode(const float* q, int ldq, const void* kc, const void* vc, 
   return launch_attn(q, ldq, kc, vc, pos, B, NH, NKV, HD, S, part, ao, ldao, nullptr, 0, s);
 }
 
+// Fused-attention scratch of the decode step (4-byte units): [16][NKV] int32 epochs (padded to
+// 16 bytes), then [B][NKV][S/128][4][HD+2] 64-bit record words.  Zeroed once.
+static size_t attn_epoch_units(int NKV) { return ((size_t)16 * NKV + 3) / 4 * 4; }
+
+size_t attn_fused_scratch_units(int Bcap, int NKV, int S) {
+  return attn_epoch_units(NKV) + 2 * (size_t)Bcap * NKV * (S / kChunk) * kG * (kHD + 2);
+}
+
+// The decode step's attention: one fused grid (chunks, combine, hi/lo operand of the O GEMM).
 int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B,
                            int NH, int NKV, int HD, int S, float* part, void* act, int ld_act, cudaStream_t s) {
-  return launch_attn(q, ldq, kc, vc, pos, B, NH, NKV, HD, S, part, nullptr, 0, (uint16_t*)act, ld_act, s);
+  RNGD_REQUIRE(q && kc && vc && pos && part && act, "attn_decode: null pointer");
+  RNGD_REQUIRE(HD == kHD && NH == kG * NKV, "attn_decode: built for HD=128 and 4 query heads per kv head");
+  RNGD_REQUIRE(S % kChunk == 0 && S > 0 && S <= 8192, "attn_decode: S=%d must be a multiple of 128", S);
+  RNGD_REQUIRE(B >= 1 && B <= 16, "attn_decode: B=%d outside 1..16", B);
+  const int nchunk = S / kChunk;
+  static std::atomic<unsigned long long> smem_set{0};
+  RNGD_TRY(set_smem_limit_once((const void*)attn_fused_kernel, (int)kAttnSmem, &smem_set,
+                               "cudaFuncSetAttribute(attn_fused_kernel)"));
+  int* epochs = (int*)part;
+  unsigned long long* recw = (unsigned long long*)(part + attn_epoch_units(NKV));
+  return launch_pdl(attn_fused_kernel, dim3(nchunk, NKV, B), dim3(128), kAttnSmem, s, "attn_fused_kernel", q, ldq,
+                    (const uint16_t*)kc, (const uint16_t*)vc, pos, NH, NKV, S, recw, epochs, (uint16_t*)act,
+                    ld_act);
+}
+
+int read_status_attn(int* st, int reset) {
+  RNGD_TRY(check_cuda(cudaMemcpyFromSymbol(st, g_status_attn, sizeof(int)), "read device status"));
+  if (reset) {
+    const int zero = 0;
+    RNGD_TRY(check_cuda(cudaMemcpyToSymbol(g_status_attn, &zero, sizeof(int)), "reset device status"));
+  }
+  return RNGD_OK;
 }
 
 // ----------------------------------------------------------- SwiGLU

@@ -848,6 +848,13 @@ extern "C" int rngd_decode_workspace(const rngd_model_t* m, int S, size_t* parti
   return RNGD_OK;
 }
 
+extern "C" int rngd_decode_attn_workspace(const rngd_model_t* m, int Bcap, int S, size_t* attn_units) {
+  RNGD_REQUIRE(m && attn_units, "attn_workspace: null argument");
+  RNGD_REQUIRE(Bcap >= 1 && Bcap <= 16 && S % 128 == 0 && S > 0, "attn_workspace: Bcap=%d S=%d", Bcap, S);
+  *attn_units = attn_fused_scratch_units(Bcap, m->NKV, S);
+  return RNGD_OK;
+}
+
 static unsigned long long* g_trace = nullptr;  // set by rngd_tc_gemv_trace (diagnostics)
 
 extern "C" int rngd_tc_gemv_trace(uint64_t* trace) {
@@ -1016,9 +1023,10 @@ int rngd::read_status_decode(int* st, int reset) {
 
 extern "C" int rngd_device_status(int* status, int reset) {
   RNGD_REQUIRE(status != nullptr, "device_status: null output");
-  int st = 0, sp = 0;
+  int st = 0, sp = 0, sa = 0;
   RNGD_TRY(read_status_decode(&st, reset));
   RNGD_TRY(read_status_prefill(&sp, reset));
-  *status = st != 0 ? st : sp;
+  RNGD_TRY(read_status_attn(&sa, reset));
+  *status = st != 0 ? st : (sp != 0 ? sp : sa);
   return RNGD_OK;
 }

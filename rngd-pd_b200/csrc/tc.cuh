@@ -17,7 +17,7 @@ namespace rngd {
 
 
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
-enum : int { ST_TMA_WAIT = 1, ST_MMA_WAIT = 2, ST_EPI_WAIT = 3, ST_FLAG_WAIT = 4, ST_PIECE_WAIT = 5 };
+enum : int { ST_TMA_WAIT = 1, ST_MMA_WAIT = 2, ST_EPI_WAIT = 3, ST_FLAG_WAIT = 4, ST_PIECE_WAIT = 5, ST_ATTN_WAIT = 6 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -223,6 +223,8 @@ static int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 // Status words of the translation units that hold bounded waits.
 int read_status_decode(int* st, int reset);
 int read_status_prefill(int* st, int reset);
+int read_status_attn(int* st, int reset);
+size_t attn_fused_scratch_units(int Bcap, int NKV, int S);
 
 // Shared host helpers (decode_tc.cu): SM count, cached tensor maps for weight
 // blocks [L][N][K] (box 64 x 128) and operand buffers [rows][K] (box 64 x box_rows).

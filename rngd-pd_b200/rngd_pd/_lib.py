@@ -82,6 +82,7 @@ _sig("rngd_decode_lmhead", _MP, _IOP, _vp)
 _sig("rngd_decode_advance", _IOP, _vp)
 _szp = ctypes.POINTER(ctypes.c_size_t)
 _sig("rngd_decode_workspace", _MP, ctypes.c_int, _szp, _szp, _szp, _szp)
+_sig("rngd_decode_attn_workspace", _MP, ctypes.c_int, ctypes.c_int, _szp)
 _sig("rngd_tc_gemv", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp,
      _vp, _vp, ctypes.c_int, _vp)
 _sig("rngd_tc_gemv_workspace", ctypes.c_int, ctypes.c_int, _szp, _szp)
@@ -167,6 +168,12 @@ def decode_workspace(model, S):
     out = [ctypes.c_size_t(0) for _ in range(4)]
     call("rngd_decode_workspace", ctypes.byref(model), S, *[ctypes.byref(o) for o in out])
     return [o.value for o in out]
+
+
+def decode_attn_workspace(model, Bcap, S):
+    out = ctypes.c_size_t(0)
+    call("rngd_decode_attn_workspace", ctypes.byref(model), Bcap, S, ctypes.byref(out))
+    return out.value
 
 
 def exported_symbols():

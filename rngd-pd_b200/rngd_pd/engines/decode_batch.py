@@ -89,7 +89,8 @@ class BatchDecodeEngine:
         self._act2 = torch.zeros((2 * MAXB, act2_cols), dtype=BF, device=d)
         self._ss = torch.zeros((H // 128, MAXB), **f32)
         self._logits = torch.zeros((B, self.V), **f32)
-        self._part = torch.zeros((B, c.n_heads, S // ATTN_CHUNK, c.head_dim + 2), **f32)
+        # fused attention: chunk records ({value, flag} words) and per-(stream, kv head) epochs
+        self._part = torch.zeros(_lib.decode_attn_workspace(self._m, B, S), **f32)
         self._partial = torch.zeros(max(partial_floats, 1), **f32)
         self._counters = torch.zeros(max(counters, 1), dtype=torch.int32, device=d)
         self._best = torch.zeros(MAXB, dtype=torch.int64, device=d)
@@ -102,9 +103,9 @@ class BatchDecodeEngine:
         self.use_graph = os.environ.get("RNGD_CUDA_GRAPH", "1") != "0"
         self._graphs = {}
         self._copied = torch.cuda.Event()
-        # embed + operand; per layer: QKV gemm, attn partial, attn combine, O gemm, gate/up gemm,
-        # down gemm; lm_head gemm, argmax finalize; advance
-        self.launches_per_step = 2 + self.nl * 6 + 2 + 1
+        # embed + operand; per layer: QKV gemm, fused attention, O gemm, gate/up gemm, down gemm;
+        # lm_head gemm, argmax finalize; advance
+        self.launches_per_step = 2 + self.nl * 5 + 2 + 1
 
     # ------------------------------------------------------------ buffers
     def _io(self, Kg, Vg):
