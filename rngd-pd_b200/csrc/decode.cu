@@ -197,18 +197,28 @@ __device__ __forceinline__ unsigned long long ld_rec(const unsigned long long* p
 
 constexpr int kRecChunks = 3;  // chunk records the fused combine reads per poll round
 
-// One CTA = (128-position chunk, kv head, stream) and the G=4 query heads of the kv head.
-// The chunk's K rows, then its V rows, are staged into shared memory with cp.async (two
-// groups, all loads in flight at once); the scores (one position per thread) and softmax
-// statistics run as soon as K has landed, P.V once V has.
+constexpr int kAttnThreads = 256;  // two halves of 128 threads, one per pair of query heads
+
+// One CTA = (128-position chunk, kv head, stream) and the G=4 query heads of the kv head;
+// thread t works on query heads 2*(t/128), 2*(t/128)+1 at position / dimension t % 128.
+// The chunk's K rows, then its V rows, are staged into shared memory with cp.async (all loads
+// in flight at once); the scores (one position per thread) and softmax statistics run as soon
+// as K has landed, P.V once V has.  Every per-head sum runs in the same order whatever the
+// thread split, so both forms below give the same bits.
 //
 // FUSED = false writes a partial record (o[HD], m, l per head) for attn_combine_kernel.
-// FUSED = true (the decode step) ends with the combine in the same grid: chunks 1.. store their
-// records as {value, flag} words, flag = epoch of (stream, kv head) + 1; chunk 0 (the lowest
-// CTA index of the group, so it only ever waits on CTAs dispatched after it) polls them with a
-// bounded wait, combines every chunk in chunk order exactly as attn_combine_kernel does, writes
-// the hi/lo operand of the O projection and advances the epoch, so records of earlier launches
-// (older epochs) never read as ready and nothing needs clearing.
+// FUSED = true (the decode step, launched right after the QKV GEMM that appends K/V at
+// pos[b]):
+//  * rows before pos[b] were written by earlier steps and every kernel before the QKV GEMM
+//    has completed once this grid is running (the GEMM signals its dependants only after its
+//    own dependency wait), so they are staged BEFORE the wait, overlapping the GEMM's tail;
+//    the row at pos[b] and q are read after it;
+//  * the combine runs in the same grid: chunks 1.. store their records as {value, flag} words,
+//    flag = epoch of (stream, kv head) + 1; chunk 0 (the lowest CTA index of the group, so it
+//    only ever waits on CTAs dispatched after it) polls them with a bounded wait, combines
+//    every chunk in chunk order exactly as attn_combine_kernel does, writes the hi/lo operand
+//    of the O projection and advances the epoch, so records of earlier launches (older
+//    epochs) never read as ready and nothing needs clearing.
 template <bool FUSED>
 __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq, const uint16_t* __restrict__ kc,
                                            const uint16_t* __restrict__ vc, const int32_t* __restrict__ pos,
@@ -224,127 +234,149 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
   float* ored = (float*)sK;                        // [8][kG][kHD], reuses the K rows after the scores
 
   const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
-  const int warp = t >> 5, lane = t & 31;
+  const int hp = t >> 7, tt = t & 127;             // head pair, position / dimension
+  const int lane = t & 31, w4 = tt >> 5;           // warp within the head pair's 4 warps
   const int nchunk = gridDim.x;
   const int PS = kHD + 2;  // partial record: o[HD], m, l
+  const int s0 = c * kChunk;
+  const size_t head_base = ((size_t)b * NKV + kvh) * (size_t)S * kHD;
+  const uint8_t* kg = (const uint8_t*)(kc + head_base + (size_t)s0 * kHD);
+  const uint8_t* vg = (const uint8_t*)(vc + head_base + (size_t)s0 * kHD);
+  int P, n, old = 0;  // positions < P are attended; rows [0, old) of the chunk staged early
+  if constexpr (FUSED) {
+    const int pb = pos[b];
+    P = min(pb + 1, S);
+    n = min(kChunk, P - s0);
+    if (n <= 0) return;  // no positions in this chunk: chunk 0 reads only chunks that hold some
+    old = max(0, min(n, pb - s0));
+    for (int i = t; i < old * 16; i += kAttnThreads) {
+      const int j = i >> 4, c16 = (i & 15) * 16;
+      cp_async16(sK + j * kRowBytes + c16, kg + (size_t)j * 256 + c16);
+      cp_async16(sV + j * kRowBytes + c16, vg + (size_t)j * 256 + c16);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   grid_dep_wait();
   grid_dep_launch();  // every CTA of this grid is running: the next kernel may start its prologue
-  const int P = min(pos[b] + 1, S);
-  const int s0 = c * kChunk;
-  float* rec0 = FUSED ? nullptr : part + (((size_t)b * NH + kvh * kG) * nchunk + c) * PS;
+  float* rec0 = nullptr;
   int epoch = 0;
-  if constexpr (FUSED) epoch = __ldcg(epochs + (size_t)b * NKV + kvh);
-  if (s0 >= P) {
-    if constexpr (!FUSED) {
+  if constexpr (FUSED) {
+    epoch = __ldcg(epochs + (size_t)b * NKV + kvh);
+  } else {
+    P = min(pos[b] + 1, S);
+    n = min(kChunk, P - s0);
+    rec0 = part + (((size_t)b * NH + kvh * kG) * nchunk + c) * PS;
+    if (n <= 0) {
       if (t < kG) {
         float* rec = rec0 + (size_t)t * nchunk * PS;
         rec[kHD] = -INFINITY;
         rec[kHD + 1] = 0.f;
       }
+      return;
     }
-    return;  // fused: chunk 0 reads only the chunks that hold positions
   }
-  const int n = min(kChunk, P - s0);
-  const size_t head_base = ((size_t)b * NKV + kvh) * (size_t)S * kHD;
-  const uint8_t* kg = (const uint8_t*)(kc + head_base + (size_t)s0 * kHD);
-  const uint8_t* vg = (const uint8_t*)(vc + head_base + (size_t)s0 * kHD);
-  for (int i = t; i < n * 16; i += 128) {
+  for (int i = old * 16 + t; i < n * 16; i += kAttnThreads) {
     const int j = i >> 4, c16 = (i & 15) * 16;
     cp_async16(sK + j * kRowBytes + c16, kg + (size_t)j * 256 + c16);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
-  for (int i = t; i < n * 16; i += 128) {
+  for (int i = old * 16 + t; i < n * 16; i += kAttnThreads) {
     const int j = i >> 4, c16 = (i & 15) * 16;
     cp_async16(sV + j * kRowBytes + c16, vg + (size_t)j * 256 + c16);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   const float scale = 0.08838834764831845f;  // 1/sqrt(128) in fp32
-  for (int i = t; i < kG * kHD; i += 128) qs[i] = q[(size_t)b * ldq + (size_t)(kvh * kG) * kHD + i];
-  asm volatile("cp.async.wait_group 1;" ::: "memory");  // the K rows (V may still be in flight)
+  for (int i = t; i < kG * kHD; i += kAttnThreads) qs[i] = q[(size_t)b * ldq + (size_t)(kvh * kG) * kHD + i];
+  asm volatile("cp.async.wait_group 1;" ::: "memory");  // all but the last group (V rows from row `old`)
   __syncthreads();
 
-  // scores: thread t = position s0 + t
-  float sc[kG] = {0.f, 0.f, 0.f, 0.f};
-  if (t < n) {
-    const uint8_t* krow = sK + t * kRowBytes;
+  // scores: thread = position s0 + tt for heads 2hp, 2hp+1
+  float sc[2] = {0.f, 0.f};
+  if (tt < n) {
+    const uint8_t* krow = sK + tt * kRowBytes;
 #pragma unroll 4
     for (int d = 0; d < kHD; d += 8) {
       float kf[8];
       unpack8(*reinterpret_cast<const uint4*>(krow + d * 2), kf);
 #pragma unroll
-      for (int g = 0; g < kG; g++) {
+      for (int gg = 0; gg < 2; gg++) {
+        const int g = 2 * hp + gg;
         const float4 qa = *reinterpret_cast<const float4*>(&qs[g * kHD + d]);
         const float4 qb = *reinterpret_cast<const float4*>(&qs[g * kHD + d + 4]);
-        float a = sc[g];
+        float a = sc[gg];
         a = fmaf(qa.x, kf[0], a); a = fmaf(qa.y, kf[1], a); a = fmaf(qa.z, kf[2], a); a = fmaf(qa.w, kf[3], a);
         a = fmaf(qb.x, kf[4], a); a = fmaf(qb.y, kf[5], a); a = fmaf(qb.z, kf[6], a); a = fmaf(qb.w, kf[7], a);
-        sc[g] = a;
+        sc[gg] = a;
       }
     }
   }
-  float mx[kG];
+  float mx[2];
 #pragma unroll
-  for (int g = 0; g < kG; g++) {
-    sc[g] = t < n ? sc[g] * scale : -INFINITY;
-    const float m = warp_max(sc[g]);
-    if (lane == 0) red[g * 4 + warp] = m;
+  for (int gg = 0; gg < 2; gg++) {
+    sc[gg] = tt < n ? sc[gg] * scale : -INFINITY;
+    const float m = warp_max(sc[gg]);
+    if (lane == 0) red[(2 * hp + gg) * 4 + w4] = m;
   }
   __syncthreads();
 #pragma unroll
-  for (int g = 0; g < kG; g++)
-    mx[g] = fmaxf(fmaxf(red[g * 4 + 0], red[g * 4 + 1]), fmaxf(red[g * 4 + 2], red[g * 4 + 3]));
+  for (int gg = 0; gg < 2; gg++) {
+    const int g = 2 * hp + gg;
+    mx[gg] = fmaxf(fmaxf(red[g * 4 + 0], red[g * 4 + 1]), fmaxf(red[g * 4 + 2], red[g * 4 + 3]));
+  }
   __syncthreads();
 #pragma unroll
-  for (int g = 0; g < kG; g++) {
-    const float p = t < n ? expf(sc[g] - mx[g]) : 0.f;
-    ps[g * kChunk + t] = p;
+  for (int gg = 0; gg < 2; gg++) {
+    const int g = 2 * hp + gg;
+    const float p = tt < n ? expf(sc[gg] - mx[gg]) : 0.f;
+    ps[g * kChunk + tt] = p;
     const float ssum = warp_sum(p);
-    if (lane == 0) red[g * 4 + warp] = ssum;
+    if (lane == 0) red[g * 4 + w4] = ssum;
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");  // the V rows
   __syncthreads();
-  // P.V: thread t owns dims dg*8..dg*8+7 for positions pg, pg+8, ...; partials reduced over pg
-  const int dg = t & 15, pg = t >> 4;
-  float o[kG][8];
+  // P.V: thread owns dims dg*8..dg*8+7 for positions pg, pg+8, ...; partials reduced over pg
+  const int dg = tt & 15, pg = tt >> 4;
+  float o[2][8];
 #pragma unroll
-  for (int g = 0; g < kG; g++)
+  for (int gg = 0; gg < 2; gg++)
 #pragma unroll
-    for (int d = 0; d < 8; d++) o[g][d] = 0.f;
+    for (int d = 0; d < 8; d++) o[gg][d] = 0.f;
 #pragma unroll 4
   for (int j = pg; j < n; j += 8) {
     float vf[8];
     unpack8(*reinterpret_cast<const uint4*>(sV + j * kRowBytes + dg * 16), vf);
 #pragma unroll
-    for (int g = 0; g < kG; g++) {
-      const float p = ps[g * kChunk + j];
+    for (int gg = 0; gg < 2; gg++) {
+      const float p = ps[(2 * hp + gg) * kChunk + j];
 #pragma unroll
-      for (int d = 0; d < 8; d++) o[g][d] = fmaf(p, vf[d], o[g][d]);
+      for (int d = 0; d < 8; d++) o[gg][d] = fmaf(p, vf[d], o[gg][d]);
     }
   }
 #pragma unroll
-  for (int g = 0; g < kG; g++) {
-    float* dst = ored + (pg * kG + g) * kHD + dg * 8;
-    *reinterpret_cast<float4*>(dst) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
+  for (int gg = 0; gg < 2; gg++) {
+    float* dst = ored + (pg * kG + 2 * hp + gg) * kHD + dg * 8;
+    *reinterpret_cast<float4*>(dst) = make_float4(o[gg][0], o[gg][1], o[gg][2], o[gg][3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(o[gg][4], o[gg][5], o[gg][6], o[gg][7]);
   }
   __syncthreads();
-  float acc[kG], lsum[kG];
+  float acc[2], lsum[2];
 #pragma unroll
-  for (int g = 0; g < kG; g++) {
+  for (int gg = 0; gg < 2; gg++) {
+    const int g = 2 * hp + gg;
     float a = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; k++) a += ored[(k * kG + g) * kHD + t];
-    acc[g] = a;
-    lsum[g] = (red[g * 4 + 0] + red[g * 4 + 1]) + (red[g * 4 + 2] + red[g * 4 + 3]);
+    for (int k = 0; k < 8; k++) a += ored[(k * kG + g) * kHD + tt];
+    acc[gg] = a;
+    lsum[gg] = (red[g * 4 + 0] + red[g * 4 + 1]) + (red[g * 4 + 2] + red[g * 4 + 3]);
   }
   if constexpr (!FUSED) {
 #pragma unroll
-    for (int g = 0; g < kG; g++) {
-      float* rec = rec0 + (size_t)g * nchunk * PS;
-      rec[t] = acc[g];
-      if (t == 0) {
-        rec[kHD] = mx[g];
-        rec[kHD + 1] = lsum[g];
+    for (int gg = 0; gg < 2; gg++) {
+      float* rec = rec0 + (size_t)(2 * hp + gg) * nchunk * PS;
+      rec[tt] = acc[gg];
+      if (tt == 0) {
+        rec[kHD] = mx[gg];
+        rec[kHD + 1] = lsum[gg];
       }
     }
   } else {
@@ -354,11 +386,12 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
     if (c > 0) {
       unsigned long long* rc = grp + (size_t)c * kG * PS;
 #pragma unroll
-      for (int g = 0; g < kG; g++) {
-        st_rec(rc + g * PS + t, acc[g], flag);
-        if (t == 0) {
-          st_rec(rc + g * PS + kHD, mx[g], flag);
-          st_rec(rc + g * PS + kHD + 1, lsum[g], flag);
+      for (int gg = 0; gg < 2; gg++) {
+        unsigned long long* rg = rc + (2 * hp + gg) * PS;
+        st_rec(rg + tt, acc[gg], flag);
+        if (tt == 0) {
+          st_rec(rg + kHD, mx[gg], flag);
+          st_rec(rg + kHD + 1, lsum[gg], flag);
         }
       }
       return;
@@ -367,20 +400,21 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
     // polls the records of chunks 1..nc-1 (kRecChunks per round) for the max, then adds them
     // in chunk order from the words already read (re-read in batches for longer caches)
     const int nc = (P + kChunk - 1) / kChunk;
-    float M[kG], L[kG], O[kG];
+    float M[2], L[2], O[2];
 #pragma unroll
-    for (int g = 0; g < kG; g++) M[g] = fmaxf(-INFINITY, mx[g]);
-    unsigned long long w[kRecChunks][kG][3];
+    for (int gg = 0; gg < 2; gg++) M[gg] = fmaxf(-INFINITY, mx[gg]);
+    unsigned long long w[kRecChunks][2][3];
     auto load_batch = [&](int c0, uint32_t mask) {
 #pragma unroll
       for (int k = 0; k < kRecChunks; k++) {
         if (mask & (1u << k)) {
           const unsigned long long* rc = grp + (size_t)(c0 + k) * kG * PS;
 #pragma unroll
-          for (int g = 0; g < kG; g++) {
-            w[k][g][0] = ld_rec(rc + g * PS + t);
-            w[k][g][1] = ld_rec(rc + g * PS + kHD);
-            w[k][g][2] = ld_rec(rc + g * PS + kHD + 1);
+          for (int gg = 0; gg < 2; gg++) {
+            const unsigned long long* rg = rc + (2 * hp + gg) * PS;
+            w[k][gg][0] = ld_rec(rg + tt);
+            w[k][gg][1] = ld_rec(rg + kHD);
+            w[k][gg][2] = ld_rec(rg + kHD + 1);
           }
         }
       }
@@ -399,9 +433,9 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
           if (pend & (1u << k)) {
             bool ready = true;
 #pragma unroll
-            for (int g = 0; g < kG; g++)
+            for (int gg = 0; gg < 2; gg++)
 #pragma unroll
-              for (int e = 0; e < 3; e++) ready &= (uint32_t)(w[k][g][e] >> 32) == flag;
+              for (int e = 0; e < 3; e++) ready &= (uint32_t)(w[k][gg][e] >> 32) == flag;
             if (ready) pend &= ~(1u << k);
           }
         }
@@ -420,14 +454,14 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
       for (int k = 0; k < kRecChunks; k++)
         if (c0 + k < nc)
 #pragma unroll
-          for (int g = 0; g < kG; g++) M[g] = fmaxf(M[g], __uint_as_float((uint32_t)w[k][g][1]));
+          for (int gg = 0; gg < 2; gg++) M[gg] = fmaxf(M[gg], __uint_as_float((uint32_t)w[k][gg][1]));
     }
     // pass 2: exp-weighted sums in chunk order, chunk 0 from registers
 #pragma unroll
-    for (int g = 0; g < kG; g++) {
-      const float f = expf(mx[g] - M[g]);
-      L[g] = fmaf(lsum[g], f, 0.f);
-      O[g] = fmaf(acc[g], f, 0.f);
+    for (int gg = 0; gg < 2; gg++) {
+      const float f = expf(mx[gg] - M[gg]);
+      L[gg] = fmaf(lsum[gg], f, 0.f);
+      O[gg] = fmaf(acc[gg], f, 0.f);
     }
     for (int c0 = 1; c0 < nc; c0 += kRecChunks) {
       uint32_t have = 0;
@@ -439,20 +473,20 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
       for (int k = 0; k < kRecChunks; k++) {
         if (have & (1u << k)) {
 #pragma unroll
-          for (int g = 0; g < kG; g++) {
-            const float m = __uint_as_float((uint32_t)w[k][g][1]);
+          for (int gg = 0; gg < 2; gg++) {
+            const float m = __uint_as_float((uint32_t)w[k][gg][1]);
             if (m == -INFINITY) continue;
-            const float f = expf(m - M[g]);
-            L[g] = fmaf(__uint_as_float((uint32_t)w[k][g][2]), f, L[g]);
-            O[g] = fmaf(__uint_as_float((uint32_t)w[k][g][0]), f, O[g]);
+            const float f = expf(m - M[gg]);
+            L[gg] = fmaf(__uint_as_float((uint32_t)w[k][gg][2]), f, L[gg]);
+            O[gg] = fmaf(__uint_as_float((uint32_t)w[k][gg][0]), f, O[gg]);
           }
         }
       }
     }
 #pragma unroll
-    for (int g = 0; g < kG; g++) {
-      const float ov = O[g] / L[g];
-      const size_t col = (size_t)(kvh * kG + g) * kHD + t;
+    for (int gg = 0; gg < 2; gg++) {
+      const float ov = O[gg] / L[gg];
+      const size_t col = (size_t)(kvh * kG + 2 * hp + gg) * kHD + tt;
       const uint16_t hi = f2bf_bits(ov);
       act[(size_t)b * ld_act + col] = hi;
       act[(size_t)(16 + b) * ld_act + col] = f2bf_bits(ov - bf2f(hi));
@@ -461,7 +495,7 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
   }
 }
 
-__global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restrict__ q, int ldq,
+__global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const float* __restrict__ q, int ldq,
                                                            const uint16_t* __restrict__ kc,
                                                            const uint16_t* __restrict__ vc,
                                                            const int32_t* __restrict__ pos, int NH,
@@ -469,7 +503,7 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const float* __restri
   attn_chunk<false>(q, ldq, kc, vc, pos, NH, NKV, S, part, nullptr, nullptr, nullptr, 0);
 }
 
-__global__ void __launch_bounds__(128) attn_fused_kernel(const float* __restrict__ q, int ldq,
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_fused_kernel(const float* __restrict__ q, int ldq,
                                                          const uint16_t* __restrict__ kc,
                                                          const uint16_t* __restrict__ vc,
                                                          const int32_t* __restrict__ pos, int NH, int NKV,
@@ -520,7 +554,7 @@ static int launch_attn(const float* q, int ldq, const void* kc, const void* vc, 
   static std::atomic<unsigned long long> smem_set{0};
   RNGD_TRY(set_smem_limit_once((const void*)attn_partial_kernel, (int)kAttnSmem, &smem_set,
                                "cudaFuncSetAttribute(attn_partial_kernel)"));
-  RNGD_TRY(launch_pdl(attn_partial_kernel, dim3(nchunk, NKV, B), dim3(128), kAttnSmem, s, "attn_partial_kernel", q, ldq,
+  RNGD_TRY(launch_pdl(attn_partial_kernel, dim3(nchunk, NKV, B), dim3(kAttnThreads), kAttnSmem, s, "attn_partial_kernel", q, ldq,
                       (const uint16_t*)kc, (const uint16_t*)vc, pos, NH, NKV, S, part));
   return launch_pdl(attn_combine_kernel, dim3(NH, B), dim3(kHD), 0, s, "attn_combine_kernel", (const float*)part,
                     nchunk, ao, ldao, NH, act, ld_act);
@@ -552,7 +586,7 @@ int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* 
                                "cudaFuncSetAttribute(attn_fused_kernel)"));
   int* epochs = (int*)part;
   unsigned long long* recw = (unsigned long long*)(part + attn_epoch_units(NKV));
-  return launch_pdl(attn_fused_kernel, dim3(nchunk, NKV, B), dim3(128), kAttnSmem, s, "attn_fused_kernel", q, ldq,
+  return launch_pdl(attn_fused_kernel, dim3(nchunk, NKV, B), dim3(kAttnThreads), kAttnSmem, s, "attn_fused_kernel", q, ldq,
                     (const uint16_t*)kc, (const uint16_t*)vc, pos, NH, NKV, S, recw, epochs, (uint16_t*)act,
                     ld_act);
 }
