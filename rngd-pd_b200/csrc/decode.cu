@@ -174,11 +174,39 @@ constexpr int kG = 4;
 constexpr int kHD = 128;
 
 constexpr int kRowBytes = 272;  // smem pitch of a staged K/V row: 256 B + 16 B pad (bank-conflict free)
-constexpr size_t kAttnSmem = 2 * kChunk * kRowBytes + kG * kHD * 4 + kG * kChunk * 4 + kG * 4 * 4 + 128;
+constexpr int kPhlLd = kRowBytes / 2;  // bf16 pitch of the P operand rows (same bank spread as K/V)
+// smem: K rows | V rows | P operand [8][kPhlLd] bf16 | per-warp max and sum [2][kG][8]
+constexpr size_t kAttnSmem = 2 * kChunk * kRowBytes + 8 * kRowBytes + 2 * kG * 8 * 4 + 128;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
+}
+
+// Warp-level bf16 tensor-core pieces (16x8x16 tiles, fp32 accumulation) for the small
+// decode-attention contractions: 4 query heads x {hi, lo} bf16 halves make the 8 columns.
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// hi or lo bf16 half (part 0 / 1) of two fp32 values, packed low index first
+__device__ __forceinline__ uint32_t pack_hilo(float x0, float x1, int part) {
+  const uint16_t h0 = f2bf_bits(x0), h1 = f2bf_bits(x1);
+  if (part == 0) return (uint32_t)h0 | ((uint32_t)h1 << 16);
+  return (uint32_t)f2bf_bits(x0 - bf2f(h0)) | ((uint32_t)f2bf_bits(x1 - bf2f(h1)) << 16);
 }
 
 __device__ int g_status_attn = 0;  // this file's bounded-wait status word
@@ -228,14 +256,14 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
   extern __shared__ __align__(16) uint8_t attn_smem[];
   uint8_t* sK = attn_smem;
   uint8_t* sV = sK + kChunk * kRowBytes;
-  float* qs = (float*)(sV + kChunk * kRowBytes);   // [kG][kHD]
-  float* ps = qs + kG * kHD;                       // [kG][kChunk]
-  float* red = ps + kG * kChunk;                   // [kG][4]
-  float* ored = (float*)sK;                        // [8][kG][kHD], reuses the K rows after the scores
+  uint16_t* phl = (uint16_t*)(sV + kChunk * kRowBytes);  // [8][kPhlLd]: p hi (heads 0-3), p lo (0-3)
+  float* red_max = (float*)(phl + 8 * kPhlLd);           // [kG][8 warps]
+  float* red_sum = red_max + kG * 8;                     // [kG][8 warps]
+  float* ored = (float*)sK;                              // [kG][kHD], reuses the K rows after the scores
 
   const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
   const int hp = t >> 7, tt = t & 127;             // head pair, position / dimension
-  const int lane = t & 31, w4 = tt >> 5;           // warp within the head pair's 4 warps
+  const int lane = t & 31;
   const int nchunk = gridDim.x;
   const int PS = kHD + 2;  // partial record: o[HD], m, l
   const int s0 = c * kChunk;
@@ -286,88 +314,121 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   const float scale = 0.08838834764831845f;  // 1/sqrt(128) in fp32
-  for (int i = t; i < kG * kHD; i += kAttnThreads) qs[i] = q[(size_t)b * ldq + (size_t)(kvh * kG) * kHD + i];
+  const int warp = t >> 5, gid = lane >> 2, tig = lane & 3;
+  const int nt = (n + 15) >> 4;  // 16-position tiles that hold positions
+  // rows [n, 16*nt) of V enter the last P.V tile with p = 0: make them zeros, not stale bits
+  for (int i = t; i < (16 * nt - n) * 16; i += kAttnThreads)
+    *reinterpret_cast<uint4*>(sV + (n + (i >> 4)) * kRowBytes + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
+  // q as the B operand of the scores, column gid = head (gid & 3), half (gid >> 2), all 128 dims
+  uint32_t qb[8][2];
+  {
+    const float* qr = q + (size_t)b * ldq + (size_t)(kvh * kG + (gid & 3)) * kHD;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+      const float2 x0 = *reinterpret_cast<const float2*>(qr + ks * 16 + tig * 2);
+      const float2 x1 = *reinterpret_cast<const float2*>(qr + ks * 16 + 8 + tig * 2);
+      qb[ks][0] = pack_hilo(x0.x, x0.y, gid >> 2);
+      qb[ks][1] = pack_hilo(x1.x, x1.y, gid >> 2);
+    }
+  }
   asm volatile("cp.async.wait_group 1;" ::: "memory");  // all but the last group (V rows from row `old`)
   __syncthreads();
 
-  // scores: thread = position s0 + tt for heads 2hp, 2hp+1
-  float sc[2] = {0.f, 0.f};
-  if (tt < n) {
-    const uint8_t* krow = sK + tt * kRowBytes;
-#pragma unroll 4
-    for (int d = 0; d < kHD; d += 8) {
-      float kf[8];
-      unpack8(*reinterpret_cast<const uint4*>(krow + d * 2), kf);
+  // scores S[pos][col] = K[pos] . qcol: warp w takes positions 16w .. 16w+15; after adding the
+  // lo column to the hi one (lane ^ 2), lanes with tig&1 == j hold heads 2j, 2j+1 for
+  // positions 16w+gid (s[0][.]) and 16w+gid+8 (s[1][.])
+  const int hb = (tig & 1) * 2;
+  float s_[2][2];
+  {
+    float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (warp < nt) {
+      const uint8_t* arow = sK + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kRowBytes + (lane >> 4) * 16;
 #pragma unroll
-      for (int gg = 0; gg < 2; gg++) {
-        const int g = 2 * hp + gg;
-        const float4 qa = *reinterpret_cast<const float4*>(&qs[g * kHD + d]);
-        const float4 qb = *reinterpret_cast<const float4*>(&qs[g * kHD + d + 4]);
-        float a = sc[gg];
-        a = fmaf(qa.x, kf[0], a); a = fmaf(qa.y, kf[1], a); a = fmaf(qa.z, kf[2], a); a = fmaf(qa.w, kf[3], a);
-        a = fmaf(qb.x, kf[4], a); a = fmaf(qb.y, kf[5], a); a = fmaf(qb.z, kf[6], a); a = fmaf(qb.w, kf[7], a);
-        sc[gg] = a;
+      for (int ks = 0; ks < 8; ks++) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(arow + ks * 32, a0, a1, a2, a3);
+        mma_bf16_16816(cacc, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
       }
     }
-  }
-  float mx[2];
 #pragma unroll
-  for (int gg = 0; gg < 2; gg++) {
-    sc[gg] = tt < n ? sc[gg] * scale : -INFINITY;
-    const float m = warp_max(sc[gg]);
-    if (lane == 0) red[(2 * hp + gg) * 4 + w4] = m;
+    for (int i = 0; i < 4; i++) cacc[i] += __shfl_xor_sync(0xffffffffu, cacc[i], 2);
+    const int p0 = warp * 16 + gid, p1 = p0 + 8;
+    s_[0][0] = p0 < n ? cacc[0] * scale : -INFINITY;
+    s_[0][1] = p0 < n ? cacc[1] * scale : -INFINITY;
+    s_[1][0] = p1 < n ? cacc[2] * scale : -INFINITY;
+    s_[1][1] = p1 < n ? cacc[3] * scale : -INFINITY;
+  }
+  // per-head max and sum: rows, then the 8 gid lanes, then the 8 warps in order
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    float m = fmaxf(s_[0][j], s_[1][j]);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane < 2) red_max[(hb + j) * 8 + warp] = m;
   }
   __syncthreads();
+  float Mh[2];
 #pragma unroll
-  for (int gg = 0; gg < 2; gg++) {
-    const int g = 2 * hp + gg;
-    mx[gg] = fmaxf(fmaxf(red[g * 4 + 0], red[g * 4 + 1]), fmaxf(red[g * 4 + 2], red[g * 4 + 3]));
+  for (int j = 0; j < 2; j++) {
+    float m = red_max[(hb + j) * 8];
+#pragma unroll
+    for (int w = 1; w < 8; w++) m = fmaxf(m, red_max[(hb + j) * 8 + w]);
+    Mh[j] = m;
   }
-  __syncthreads();
 #pragma unroll
-  for (int gg = 0; gg < 2; gg++) {
-    const int g = 2 * hp + gg;
-    const float p = tt < n ? expf(sc[gg] - mx[gg]) : 0.f;
-    ps[g * kChunk + tt] = p;
-    const float ssum = warp_sum(p);
-    if (lane == 0) red[g * 4 + w4] = ssum;
+  for (int j = 0; j < 2; j++) {
+    const float e0 = expf(s_[0][j] - Mh[j]), e1 = expf(s_[1][j] - Mh[j]);  // exp(-inf) = 0
+    float sm = e0 + e1;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    if (lane < 2) red_sum[(hb + j) * 8 + warp] = sm;
+    if (tig < 2 && warp < nt) {  // P operand rows: hi of head h at row h, lo at row h + 4
+      const int p0 = warp * 16 + gid;
+      const uint16_t h0 = f2bf_bits(e0), h1 = f2bf_bits(e1);
+      phl[(hb + j) * kPhlLd + p0] = h0;
+      phl[(hb + j) * kPhlLd + p0 + 8] = h1;
+      phl[(hb + j + 4) * kPhlLd + p0] = f2bf_bits(e0 - bf2f(h0));
+      phl[(hb + j + 4) * kPhlLd + p0 + 8] = f2bf_bits(e1 - bf2f(h1));
+    }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");  // the V rows
   __syncthreads();
-  // P.V: thread owns dims dg*8..dg*8+7 for positions pg, pg+8, ...; partials reduced over pg
-  const int dg = tt & 15, pg = tt >> 4;
-  float o[2][8];
+  // P.V: O^T[d][col] = V^T[d] . P[col]; warp w takes dims 16w .. 16w+15 over the nt tiles
+  {
+    float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint8_t* vrow = sV + ((lane & 7) + (lane >> 4) * 8) * kRowBytes + warp * 32 + ((lane >> 3) & 1) * 16;
+    const uint16_t* prow = phl + gid * kPhlLd + tig * 2;
+    for (int ks = 0; ks < nt; ks++) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vrow + ks * 16 * kRowBytes, a0, a1, a2, a3);
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(prow + ks * 16);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(prow + ks * 16 + 8);
+      mma_bf16_16816(cacc, a0, a1, a2, a3, b0, b1);
+    }
 #pragma unroll
-  for (int gg = 0; gg < 2; gg++)
-#pragma unroll
-    for (int d = 0; d < 8; d++) o[gg][d] = 0.f;
-#pragma unroll 4
-  for (int j = pg; j < n; j += 8) {
-    float vf[8];
-    unpack8(*reinterpret_cast<const uint4*>(sV + j * kRowBytes + dg * 16), vf);
-#pragma unroll
-    for (int gg = 0; gg < 2; gg++) {
-      const float p = ps[(2 * hp + gg) * kChunk + j];
-#pragma unroll
-      for (int d = 0; d < 8; d++) o[gg][d] = fmaf(p, vf[d], o[gg][d]);
+    for (int i = 0; i < 4; i++) cacc[i] += __shfl_xor_sync(0xffffffffu, cacc[i], 2);
+    if (tig < 2) {
+      const int d0 = warp * 16 + gid;
+      ored[hb * kHD + d0] = cacc[0];
+      ored[(hb + 1) * kHD + d0] = cacc[1];
+      ored[hb * kHD + d0 + 8] = cacc[2];
+      ored[(hb + 1) * kHD + d0 + 8] = cacc[3];
     }
   }
-#pragma unroll
-  for (int gg = 0; gg < 2; gg++) {
-    float* dst = ored + (pg * kG + 2 * hp + gg) * kHD + dg * 8;
-    *reinterpret_cast<float4*>(dst) = make_float4(o[gg][0], o[gg][1], o[gg][2], o[gg][3]);
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(o[gg][4], o[gg][5], o[gg][6], o[gg][7]);
-  }
   __syncthreads();
-  float acc[2], lsum[2];
+  float acc[2], lsum[2], mx[2];
 #pragma unroll
   for (int gg = 0; gg < 2; gg++) {
     const int g = 2 * hp + gg;
-    float a = 0.f;
+    acc[gg] = ored[g * kHD + tt];
+    float m = red_max[g * 8], l = red_sum[g * 8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) a += ored[(k * kG + g) * kHD + tt];
-    acc[gg] = a;
-    lsum[gg] = (red[g * 4 + 0] + red[g * 4 + 1]) + (red[g * 4 + 2] + red[g * 4 + 3]);
+    for (int w = 1; w < 8; w++) {
+      m = fmaxf(m, red_max[g * 8 + w]);
+      l += red_sum[g * 8 + w];
+    }
+    mx[gg] = m;
+    lsum[gg] = l;
   }
   if constexpr (!FUSED) {
 #pragma unroll
