@@ -285,7 +285,9 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
   grid_dep_wait();
-  grid_dep_launch();  // every CTA of this grid is running: the next kernel may start its prologue
+  // the next kernel (a weight-streaming GEMM) may start its prologue: at once here, after this
+  // CTA's K/V rows have landed in the fused form, so its weight prefetch does not compete with them
+  if constexpr (!FUSED) grid_dep_launch();
   float* rec0 = nullptr;
   int epoch = 0;
   if constexpr (FUSED) {
@@ -393,6 +395,7 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");  // the V rows
   __syncthreads();
+  if constexpr (FUSED) grid_dep_launch();
   // P.V: O^T[d][col] = V^T[d] . P[col]; warp w takes dims 16w .. 16w+15 over the nt tiles
   {
     float cacc[4] = {0.f, 0.f, 0.f, 0.f};
