@@ -45,12 +45,17 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
 
-def lengths_and_tokens():
-    # the same integer recipe as rngd_pd.synth (numpy copy so the reference arm needs no GPU)
-    from oracle import synth_np as sy
-    lens = [64 + int(v) for v in sy.uniform_ints(3, sy.T_CTXLEN, B, 384 - 64 + 1)]
-    toks = [int(v) for v in sy.uniform_ints(2, sy.T_TOKENS, B, 128256)]
-    return lens, toks
+def lengths_and_tokens(cpu=False):
+    """Config 4's past lengths U[64, 384] (seed 3) and first tokens (seed 2).  The GPU arm draws
+    them with the package's device generator; the CPU reference arm (no GPU) with the test
+    oracle's numpy copy of the same integer recipe."""
+    if cpu:
+        from oracle import synth_np as sy
+        lens = [64 + int(v) for v in sy.uniform_ints(3, sy.T_CTXLEN, B, 384 - 64 + 1)]
+        toks = [int(v) for v in sy.uniform_ints(2, sy.T_TOKENS, B, 128256)]
+        return lens, toks
+    from rngd_pd import synth
+    return synth.context_lengths(B, 3, 64, 384), synth.tokens(B, 2, 128256)
 
 
 class Clocks:
@@ -93,7 +98,7 @@ def cpu_reference_steps(n_steps, warmup):
     """The CPU fp32 path (C restatement of the reference's cpu_layer) on all host cores."""
     from oracle import corc
     from oracle.ref_np import LLAMA8B
-    lens, toks = lengths_and_tokens()
+    lens, toks = lengths_and_tokens(cpu=True)
     corc.set_threads(len(os.sched_getaffinity(0)))
     m = corc.CModel(LLAMA8B, seed=0)
     Kc, Vc = m.new_cache(B, S)
@@ -546,12 +551,48 @@ def handoff_pairs(rank, world, dev, reps, warmup):
     return out, bool(ok.item())
 
 
+def run_micro_step_small(args):
+    """Config 4's decode step (B=16, S=512, same lengths and per-layer shapes) on a 2-layer model
+    of the Llama-3.1-8B shape: ~3 GB on the device, for ncu captures of any decode-step kernel
+    (the fused attention, the GEMM epilogues) on a small case.  Eager launches, one per kernel."""
+    import torch
+    from rngd_pd import synth
+    from rngd_pd.engines.decode_batch import BatchDecodeEngine
+    from rngd_pd.engines.model import ModelConfig
+    os.environ["RNGD_CUDA_GRAPH"] = "0"
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig.from_dims(L=2)
+    eng = BatchDecodeEngine(cfg, synth.SyntheticState(cfg, seed=0), B=B, S=S, group=2)
+    lens, toks = lengths_and_tokens()
+    Ks, Vs = zip(*[synth.request_kv(cfg, S, 100 + b, lens[b], device=dev) for b in range(B)])
+    Kd, Vd = eng.adopt_kv_device(list(Ks), list(Vs))
+    del Ks, Vs
+    pos = list(lens)
+    for _ in range(args.warmup):
+        toks, Kd, Vd = eng.step(toks, pos, Kd, Vd)
+        pos = [p + 1 for p in pos]
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(eng.stream)
+    for _ in range(args.steps):
+        toks, Kd, Vd = eng.step(toks, pos, Kd, Vd)
+        pos = [p + 1 for p in pos]
+    e1.record(eng.stream)
+    torch.cuda.synchronize()
+    from rngd_pd import _lib
+    print(json.dumps({"micro": "step_small", "layers": 2, "B": B, "S": S, "ms_per_step": e0.elapsed_time(e1) / args.steps,
+                      "status": _lib.device_status()}), flush=True)
+
+
 def run_micro(args):
     """One decode GEMM shape alone (small device footprint; for ncu captures of skgemm_kernel)."""
     import torch
     from rngd_pd import synth
     if args.micro == "attn":
         return run_micro_attn(args)
+    if args.micro == "step_small":
+        return run_micro_step_small(args)
     if args.micro == "handoff":
         return run_micro_handoff(args)
     if args.micro == "prefill":
@@ -753,7 +794,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn", "pf_gate_up", "pf_qkv", "pf_o",
-                                        "pf_down", "handoff", "prefill"],
+                                        "pf_down", "handoff", "prefill", "step_small"],
                     help="time one decode GEMM shape alone (small footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
