@@ -54,7 +54,10 @@ __device__ int g_status_decode = 0;  // this file's bounded-wait status word
 constexpr int BM = 128, BK = 64, BNC = 32, MAXB = 16;
 constexpr int A_BYTES = BM * BK * 2;   // 16 KB weight tile per stage
 constexpr int B_BYTES = BNC * BK * 2;  // 4 KB activation tile per stage
-constexpr int STAGES = 5;
+// 8 x 20 KB stages: what a CTA prefetches before the previous kernel's output is readable covers
+// most of that kernel's tail (measured best among 5..10 stages; deeper rings slowed the
+// short QKV and O GEMMs)
+constexpr int STAGES = 8;
 constexpr int YS_LD = 17;
 constexpr int EPI_THREADS = 256;       // two warpgroups, each 8 of the 16 streams
 constexpr int SPG = MAXB / 2;          // streams per epilogue warpgroup
