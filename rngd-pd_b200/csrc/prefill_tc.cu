@@ -30,7 +30,10 @@ namespace rngd {
 __device__ int g_status_prefill = 0;
 
 constexpr int PBM = 128, PBK = 64;
-constexpr int P_YS_LD = 33;
+constexpr int P_EPI = 256;     // epilogue threads: two warpgroups, each half of every 32-token chunk
+constexpr int P_HALF = 16;     // tokens of a chunk per warpgroup
+constexpr int P_YS_LD = 17;    // smem pitch of a warpgroup's [128][16] exchange buffer
+constexpr int P_MAXPIECE = 4;  // split-unit pieces whose loads are issued together
 
 // MT weight tiles (128 rows each) share every token tile: with MT = 2 a 64 KB stage
 // carries 32 KB of weights and 32 KB of activations (hi + lo) for twice the MMA work of
@@ -42,8 +45,10 @@ struct PCfg {
   static constexpr int STAGE = A_BYTES + 2 * B_BYTES;
   static constexpr int STAGES = MT == 2 ? 3 : 4;
   static constexpr int TMEM_COLS = 2 * MT * NT;       // MT accumulators, double-buffered
-  static constexpr size_t BAR_BYTES = (2 * STAGES + 4) * 8;
-  static constexpr size_t SMEM = 1024 + STAGES * STAGE + BAR_BYTES + 64 + NT * 4 + PBM * P_YS_LD * 4 + 4 * 32 * 4;
+  static constexpr size_t BAR_BYTES = (2 * STAGES + 5) * 8;
+  // ring | barriers | tmem slot, flag | s_scale [NT] | ys [2][128][P_YS_LD] | s_red [2][4][16]
+  static constexpr size_t SMEM =
+      1024 + STAGES * STAGE + BAR_BYTES + 64 + NT * 4 + 2 * PBM * P_YS_LD * 4 + 2 * 4 * P_HALF * 4;
 };
 
 enum PEpi : int { PEPI_QKV = 0, PEPI_RESID = 1, PEPI_SWIGLU = 2 };
@@ -75,14 +80,16 @@ struct PArgs {
   int ld_act;
 };
 
-__device__ __forceinline__ void pf_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barriers: 1 + g = epilogue warpgroup g (128 threads), 3 = both warpgroups
+__device__ __forceinline__ void pf_sync_g(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
+__device__ __forceinline__ void pf_sync_all() { asm volatile("bar.sync 3, %0;" ::"n"(P_EPI) : "memory"); }
 __device__ __forceinline__ void pf_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 template <int EPI, int NT, int MT>
-__global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                        const __grid_constant__ CUtensorMap tmX, PArgs a) {
+__global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                              const __grid_constant__ CUtensorMap tmX, PArgs a) {
   using Cfg = PCfg<NT, MT>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -91,11 +98,12 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* epi_done = acc_empty + 2;   // the epilogue threads are past their last TMEM read
   uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + Cfg::BAR_BYTES);
   int* s_last = (int*)(tmem_slot + 1);
   float* s_scale = (float*)((uint8_t*)full + Cfg::BAR_BYTES + 64);   // [NT] RMS scale of the unit's tokens
-  float* ys = s_scale + NT;                                          // [128][33]
-  float* s_red = ys + PBM * P_YS_LD;                                  // [4][32]
+  float* ys_all = s_scale + NT;                                      // [2][128][P_YS_LD]
+  float* s_red_all = ys_all + 2 * PBM * P_YS_LD;                     // [2][4][16]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -112,8 +120,9 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], P_EPI);
     }
+    mbar_init(epi_done, P_EPI);
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
@@ -204,9 +213,17 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
     }
     __syncwarp();
   } else {
+    // ---------------- epilogue warps 2..9: two warpgroups over the same 128 TMEM lanes.  Thread
+    // (group g, row r) owns row r of the tile for tokens 16g .. 16g+15 of every 32-token chunk,
+    // so each thread's serial work on the tail is half a chunk, with its global loads issued
+    // together (one L2 round trip per half chunk).
     grid_dep_wait();
     const int r = ((warp & 3) << 5) | lane;
-    const int et = threadIdx.x - 64;
+    const int et = threadIdx.x - 64;   // 0 .. P_EPI-1
+    const int g = et >> 7;             // warpgroup
+    const int eg = et & 127;           // index within the warpgroup
+    float* ys = ys_all + g * PBM * P_YS_LD;
+    float* s_red = s_red_all + g * 4 * P_HALF;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     int seg = 0;
     for (long f = f0; f < f1; seg++) {
@@ -218,7 +235,8 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       // RMS scales of this unit's NT tokens, read while the accumulator is still being built:
       // token jt*NT + i's sum over the ss tiles in tile order, loads batched 16 at a time
       if (EPI != PEPI_RESID && a.ss_in != nullptr) {
-        for (int i = et; i < NT; i += 128) {
+        pf_sync_all();  // both warpgroups are past the previous unit's scales
+        for (int i = et; i < NT; i += P_EPI) {
           const int tok = jt * NT + i;
           float ssum = 0.f;
           for (int t0 = 0; t0 < a.ss_tiles; t0 += 16) {
@@ -231,7 +249,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
           }
           s_scale[i] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
         }
-        pf_sync();
+        pf_sync_all();
       }
       mbar_wait(&acc_full[buf], (uint32_t)(seg >> 1) & 1u, ST_EPI_WAIT, &g_status_prefill);
       __syncwarp();
@@ -245,18 +263,18 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
         for (int tt = 0; tt < MT; tt++) {
           float* pdst = a.partial + (((size_t)u * a.maxseg + slot) * MT + tt) * NT * PBM;
           for (int cc = 0; cc < NT / 32; cc++) {
-            float v[32];
-            tmem_ld_32x32b_x32(tbase0 + tt * NT + cc * 32, v);
+            float v[P_HALF];
+            tmem_ld_32x32b_x16(tbase0 + tt * NT + cc * 32 + g * P_HALF, v);
 #pragma unroll
-            for (int i = 0; i < 32; i++) __stcg(pdst + (size_t)(cc * 32 + i) * PBM + r, v[i]);
+            for (int i = 0; i < P_HALF; i++) __stcg(pdst + (size_t)(cc * 32 + g * P_HALF + i) * PBM + r, v[i]);
           }
         }
         tc_fence_before();
         pf_arrive(&acc_empty[buf]);
         __threadfence();
-        pf_sync();
+        pf_sync_all();
         if (et == 0) *s_last = (atomicAdd(&a.counters[u], 1) == nseg - 1);
-        pf_sync();
+        pf_sync_all();
         run = *s_last != 0;
         if (run) __threadfence();
       }
@@ -265,30 +283,45 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
         const int mt = mg * MT + tt;  // weight tile of this accumulator
         const int n = mt * PBM + r;
         for (int cc = 0; cc < NT / 32; cc++) {
-          float y[32];
+          const int t0 = jt * NT + cc * 32 + g * P_HALF;  // first token of this thread's half chunk
+          float xo[P_HALF];  // RESID: the residual row, loaded with the pieces (one round trip)
+          if constexpr (EPI == PEPI_RESID) {
+#pragma unroll
+            for (int i = 0; i < P_HALF; i++) xo[i] = a.x[(size_t)(t0 + i) * a.ldx + n];
+          }
+          float y[P_HALF];
           if (nseg > 1) {
 #pragma unroll
-            for (int i = 0; i < 32; i++) y[i] = 0.f;
-            for (int sl = 0; sl < nseg; sl++) {
-              const float* src =
-                  a.partial + (((size_t)u * a.maxseg + sl) * MT + tt) * NT * PBM + (size_t)(cc * 32) * PBM + r;
+            for (int i = 0; i < P_HALF; i++) y[i] = 0.f;
+            for (int s0 = 0; s0 < nseg; s0 += P_MAXPIECE) {  // pieces summed in K order
+              float pv[P_MAXPIECE][P_HALF];
 #pragma unroll
-              for (int i = 0; i < 32; i++) y[i] += __ldcg(src + (size_t)i * PBM);
+              for (int q = 0; q < P_MAXPIECE; q++) {
+                if (s0 + q < nseg) {
+                  const float* src = a.partial + (((size_t)u * a.maxseg + s0 + q) * MT + tt) * NT * PBM +
+                                     (size_t)(cc * 32 + g * P_HALF) * PBM + r;
+#pragma unroll
+                  for (int i = 0; i < P_HALF; i++) pv[q][i] = __ldcg(src + (size_t)i * PBM);
+                }
+              }
+#pragma unroll
+              for (int q = 0; q < P_MAXPIECE; q++) {
+                if (s0 + q < nseg) {
+#pragma unroll
+                  for (int i = 0; i < P_HALF; i++) y[i] += pv[q][i];
+                }
+              }
             }
           } else {
-            tmem_ld_32x32b_x32(tbase0 + tt * NT + cc * 32, y);
+            tmem_ld_32x32b_x16(tbase0 + tt * NT + cc * 32 + g * P_HALF, y);
           }
-          const int t0 = jt * NT + cc * 32;  // first token of the chunk
           if (EPI != PEPI_RESID && a.ss_in != nullptr) {
 #pragma unroll
-            for (int i = 0; i < 32; i++) y[i] *= s_scale[cc * 32 + i];
+            for (int i = 0; i < P_HALF; i++) y[i] *= s_scale[cc * 32 + g * P_HALF + i];
           }
           if constexpr (EPI == PEPI_RESID) {
-            float xo[32];  // all 32 residual loads in flight before the first store
 #pragma unroll
-            for (int i = 0; i < 32; i++) xo[i] = a.x[(size_t)(t0 + i) * a.ldx + n];
-#pragma unroll
-            for (int i = 0; i < 32; i++) {
+            for (int i = 0; i < P_HALF; i++) {
               const float xn = xo[i] + y[i];
               a.x[(size_t)(t0 + i) * a.ldx + n] = xn;
               y[i] = xn;
@@ -296,26 +329,26 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
             if (a.act_next != nullptr) {
               const float w = a.w_next[n];
 #pragma unroll
-              for (int i = 0; i < 32; i++) {
+              for (int i = 0; i < P_HALF; i++) {
                 const float h = y[i] * w;
                 const uint16_t hi = f2bf_bits(h);
                 a.act_next[(size_t)(t0 + i) * a.ld_next + n] = hi;
                 a.act_next[(size_t)(a.C + t0 + i) * a.ld_next + n] = f2bf_bits(h - bf2f(hi));
               }
 #pragma unroll
-              for (int i = 0; i < 32; i++) {
+              for (int i = 0; i < P_HALF; i++) {
                 const float sq = warp_sum(y[i] * y[i]);
-                if (lane == 0) s_red[(warp & 3) * 32 + i] = sq;
+                if (lane == 0) s_red[(warp & 3) * P_HALF + i] = sq;
               }
-              pf_sync();
-              if (et < 32)
-                a.ss_out[(size_t)mt * a.C + t0 + et] =
-                    (s_red[et] + s_red[32 + et]) + (s_red[64 + et] + s_red[96 + et]);
+              pf_sync_g(g);
+              if (eg < P_HALF)
+                a.ss_out[(size_t)mt * a.C + t0 + eg] =
+                    (s_red[eg] + s_red[P_HALF + eg]) + (s_red[2 * P_HALF + eg] + s_red[3 * P_HALF + eg]);
             }
           } else if constexpr (EPI == PEPI_QKV) {
 #pragma unroll
-            for (int i = 0; i < 32; i++) ys[r * P_YS_LD + i] = y[i];
-            pf_sync();
+            for (int i = 0; i < P_HALF; i++) ys[r * P_YS_LD + i] = y[i];
+            pf_sync_g(g);
             const int head = mt;
             const int idx = r & 63;
             const bool lo_half = r < 64;
@@ -323,7 +356,7 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
             if (head < a.NH + a.NKV) {
               const float invf = a.inv[idx];
 #pragma unroll 8
-              for (int i = 0; i < 32; i++) {
+              for (int i = 0; i < P_HALF; i++) {
                 const int t = t0 + i;
                 float sn, cs;
                 sincosf((float)t * invf, &sn, &cs);
@@ -340,9 +373,9 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
               }
             } else {
               const int vh = head - a.NH - a.NKV;
-              uint32_t packed[16];  // this dimension's 32 tokens for V^T (zero past the prompt)
+              uint32_t packed[P_HALF / 2];  // this dimension's 16 tokens for V^T (zero past the prompt)
 #pragma unroll
-              for (int i = 0; i < 32; i += 2) {
+              for (int i = 0; i < P_HALF; i += 2) {
                 const int t = t0 + i;
                 const uint16_t v0 = t < a.P ? f2bf_bits(y[i]) : 0, v1 = t + 1 < a.P ? f2bf_bits(y[i + 1]) : 0;
                 packed[i / 2] = (uint32_t)v0 | ((uint32_t)v1 << 16);
@@ -351,26 +384,29 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
               }
               uint4* vrow = reinterpret_cast<uint4*>(a.vt + ((size_t)vh * 128 + r) * a.C + t0);
 #pragma unroll
-              for (int k4 = 0; k4 < 4; k4++)
+              for (int k4 = 0; k4 < P_HALF / 8; k4++)
                 vrow[k4] = make_uint4(packed[4 * k4], packed[4 * k4 + 1], packed[4 * k4 + 2], packed[4 * k4 + 3]);
             }
           } else if constexpr (EPI == PEPI_SWIGLU) {
+            // rows r < 64 hold the gate and rows r + 64 the up projection of feature r: both rows
+            // land in the exchange buffer, then the thread of row r handles tokens 0..7 and the
+            // thread of row r + 64 tokens 8..15 of the half chunk
 #pragma unroll
-            for (int i = 0; i < 32; i++) ys[r * P_YS_LD + i] = y[i];
-            pf_sync();
-            if (r < 64) {
-              const int fcol = mt * 64 + r;
-#pragma unroll 8
-              for (int i = 0; i < 32; i++) {
-                const float g = y[i], uu = ys[(r + 64) * P_YS_LD + i];
-                const float act = g / (1.0f + expf(-g)) * uu;
-                const uint16_t hi = f2bf_bits(act);
-                a.act_out[(size_t)(t0 + i) * a.ld_act + fcol] = hi;
-                a.act_out[(size_t)(a.C + t0 + i) * a.ld_act + fcol] = f2bf_bits(act - bf2f(hi));
-              }
+            for (int i = 0; i < P_HALF; i++) ys[r * P_YS_LD + i] = y[i];
+            pf_sync_g(g);
+            const int fr = r & 63, i0 = r < 64 ? 0 : P_HALF / 2;
+            const int fcol = mt * 64 + fr;
+#pragma unroll
+            for (int k = 0; k < P_HALF / 2; k++) {
+              const int i = i0 + k;
+              const float gv = ys[fr * P_YS_LD + i], uv = ys[(fr + 64) * P_YS_LD + i];
+              const float act = gv / (1.0f + expf(-gv)) * uv;
+              const uint16_t hi = f2bf_bits(act);
+              a.act_out[(size_t)(t0 + i) * a.ld_act + fcol] = hi;
+              a.act_out[(size_t)(a.C + t0 + i) * a.ld_act + fcol] = f2bf_bits(act - bf2f(hi));
             }
           }
-          pf_sync();  // ys / s_scale / s_red reused by the next chunk
+          pf_sync_g(g);  // ys / s_red reused by the next chunk
         }
        }
         if (nseg > 1) {
@@ -382,10 +418,15 @@ __global__ void __launch_bounds__(192, 1) pfgemm_kernel(const __grid_constant__ 
       }
       f = fend;
     }
+    tc_fence_before();
+    pf_arrive(epi_done);
   }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  if (warp == 1) {
+    // the epilogue warps' last TMEM reads are ordered before the dealloc by epi_done
+    mbar_wait(epi_done, 0u, ST_EPI_WAIT, &g_status_prefill);
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
 }
 
 // ------------------------------------------------- causal attention on tcgen05
@@ -637,7 +678,7 @@ static int launch_pf(const void* W, int L, int layer, int N, int K, const void* 
   static std::atomic<unsigned long long> attr_set{0};
   RNGD_TRY(set_smem_limit_once((const void*)pfgemm_kernel<EPI, NT, MT>, (int)PCfg<NT, MT>::SMEM, &attr_set,
                                "cudaFuncSetAttribute(pfgemm)"));
-  return launch_pdl(pfgemm_kernel<EPI, NT, MT>, dim3(grid), dim3(192), PCfg<NT, MT>::SMEM, s, "pfgemm_kernel", tw,
+  return launch_pdl(pfgemm_kernel<EPI, NT, MT>, dim3(grid), dim3(64 + P_EPI), PCfg<NT, MT>::SMEM, s, "pfgemm_kernel", tw,
                     tx, a);
 }
 
