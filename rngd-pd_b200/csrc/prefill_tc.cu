@@ -13,7 +13,10 @@
 // issued as two MMAs into the same TMEM accumulator (D = W*hi + W*lo), which keeps
 // fp32-level accuracy.  Scheduling is persistent stream-K over (weight tile,
 // token tile, K block), as for decode (decode_tc.cu): one CTA per SM, equal work,
-// deterministic in-order reduction of tiles cut between CTAs.
+// deterministic in-order reduction of tiles cut between CTAs.  A unit cut between CTAs is
+// summed by its first owner (its own piece stays in TMEM): the other owners store their
+// pieces and publish each with one release flag = (shape tag, unit epoch + 1), the first
+// owner acquires the flags (bounded wait), adds the pieces in K order and advances the epoch.
 //
 // Operand layout: act [2C][K] bf16, rows 0..C-1 = hi of token t, rows C..2C-1 =
 // lo.  RMSNorm is folded exactly as in decode: the producer of x writes x * w and
@@ -56,8 +59,9 @@ enum PEpi : int { PEPI_QKV = 0, PEPI_RESID = 1, PEPI_SWIGLU = 2 };
 struct PArgs {
   int N, K, nkb, ntok, total, maxseg, layer;
   int C, P;
-  float* partial;  // [units][maxseg][NT][128]
-  int* counters;   // [units]
+  float* partial;  // [units][maxseg][MT][NT][128] pieces of split units (slot 0's never stored)
+  int* counters;   // [units] split epochs, then [units][maxseg] piece flags; zeroed once
+  int nunits, tag;  // units of this launch; 1..15, distinct for GEMM shapes sharing the scratch
   const float* ss_in;  // [ss_tiles][C]
   int ss_tiles;
   float eps, inv_h;
@@ -100,7 +104,6 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint64_t* epi_done = acc_empty + 2;   // the epilogue threads are past their last TMEM read
   uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + Cfg::BAR_BYTES);
-  int* s_last = (int*)(tmem_slot + 1);
   float* s_scale = (float*)((uint8_t*)full + Cfg::BAR_BYTES + 64);   // [NT] RMS scale of the unit's tokens
   float* ys_all = s_scale + NT;                                      // [2][128][P_YS_LD]
   float* s_red_all = ys_all + 2 * PBM * P_YS_LD;                     // [2][4][16]
@@ -232,6 +235,9 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
       const long fend = ustart + a.nkb < f1 ? ustart + a.nkb : f1;
       const int mg = (int)(u % ngrp), jt = (int)(u / ngrp);
       const int buf = seg & 1;
+      // epoch of the unit's split, read before the accumulator wait (only the unit's first owner
+      // advances it, after every piece of this launch was published under the value read here)
+      const int epoch = a.maxseg > 1 ? __ldcg(a.counters + u) : 0;
       // RMS scales of this unit's NT tokens, read while the accumulator is still being built:
       // token jt*NT + i's sum over the ss tiles in tile order, loads batched 16 at a time
       if (EPI != PEPI_RESID && a.ss_in != nullptr) {
@@ -258,8 +264,11 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
       const int nseg = last - first + 1;
       const uint32_t tbase0 = tmem + lane_base + (uint32_t)(buf * MT * NT);
       bool run = true;
-      if (nseg > 1) {
-        const int slot = cta - first;
+      const int slot = cta - first;
+      const uint32_t flag = ((uint32_t)a.tag << 28) | ((uint32_t)(epoch + 1) & 0x0FFFFFFFu);
+      int* pflags = a.counters + a.nunits + (size_t)u * a.maxseg;
+      if (nseg > 1 && slot > 0) {
+        // a later piece of the unit: store it, publish it with one release, no wait
         for (int tt = 0; tt < MT; tt++) {
           float* pdst = a.partial + (((size_t)u * a.maxseg + slot) * MT + tt) * NT * PBM;
           for (int cc = 0; cc < NT / 32; cc++) {
@@ -271,12 +280,30 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
         }
         tc_fence_before();
         pf_arrive(&acc_empty[buf]);
-        __threadfence();
+        pf_sync_all();  // every thread's piece stores precede the release below
+        if (et == 0) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(pflags + slot), "r"(flag) : "memory");
+        run = false;
+      } else if (nseg > 1) {
+        // the unit's first piece is this CTA's own (in TMEM): wait (bounded) for the others'
+        // flags; the barrier then orders every thread's piece loads after the acquires
+        if (et == 0) {
+          uint64_t t0 = 0;
+          for (int sl = 1; sl < nseg; sl++) {
+            while (true) {
+              uint32_t v;
+              asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(pflags + sl) : "memory");
+              if (v == flag) break;
+              const uint64_t now = globaltimer();
+              if (t0 == 0) {
+                t0 = now;
+              } else if (now - t0 > kWaitTimeoutNs) {
+                atomicCAS(&g_status_prefill, 0, ST_PIECE_WAIT);
+                break;
+              }
+            }
+          }
+        }
         pf_sync_all();
-        if (et == 0) *s_last = (atomicAdd(&a.counters[u], 1) == nseg - 1);
-        pf_sync_all();
-        run = *s_last != 0;
-        if (run) __threadfence();
       }
       if (run) {
        for (int tt = 0; tt < MT; tt++) {
@@ -290,10 +317,9 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
             for (int i = 0; i < P_HALF; i++) xo[i] = a.x[(size_t)(t0 + i) * a.ldx + n];
           }
           float y[P_HALF];
+          tmem_ld_32x32b_x16(tbase0 + tt * NT + cc * 32 + g * P_HALF, y);  // piece 0: this CTA's own
           if (nseg > 1) {
-#pragma unroll
-            for (int i = 0; i < P_HALF; i++) y[i] = 0.f;
-            for (int s0 = 0; s0 < nseg; s0 += P_MAXPIECE) {  // pieces summed in K order
+            for (int s0 = 1; s0 < nseg; s0 += P_MAXPIECE) {  // later pieces added in K order
               float pv[P_MAXPIECE][P_HALF];
 #pragma unroll
               for (int q = 0; q < P_MAXPIECE; q++) {
@@ -312,8 +338,6 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
                 }
               }
             }
-          } else {
-            tmem_ld_32x32b_x16(tbase0 + tt * NT + cc * 32 + g * P_HALF, y);
           }
           if (EPI != PEPI_RESID && a.ss_in != nullptr) {
 #pragma unroll
@@ -409,12 +433,9 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
           pf_sync_g(g);  // ys / s_red reused by the next chunk
         }
        }
-        if (nseg > 1) {
-          if (et == 0) a.counters[u] = 0;
-        } else {
-          tc_fence_before();
-          pf_arrive(&acc_empty[buf]);
-        }
+        tc_fence_before();
+        pf_arrive(&acc_empty[buf]);
+        if (nseg > 1 && et == 0) a.counters[u] = epoch + 1;  // read by the next launch only
       }
       f = fend;
     }
@@ -673,8 +694,10 @@ static int launch_pf(const void* W, int L, int layer, int N, int K, const void* 
   a.total = (int)(units * a.nkb);
   const int grid = pf_grid(a.total);
   a.maxseg = pf_maxseg(units, a.nkb, grid);
+  a.nunits = (int)units;
   a.layer = layer;
   RNGD_REQUIRE(a.maxseg == 1 || (a.partial && a.counters), "prefill GEMM: split tiles need partial/counters");
+  RNGD_REQUIRE(a.tag >= 1 && a.tag <= 15, "prefill GEMM: shape tag %d outside 1..15", a.tag);
   static std::atomic<unsigned long long> attr_set{0};
   RNGD_TRY(set_smem_limit_once((const void*)pfgemm_kernel<EPI, NT, MT>, (int)PCfg<NT, MT>::SMEM, &attr_set,
                                "cudaFuncSetAttribute(pfgemm)"));
@@ -705,7 +728,7 @@ static void pf_shape_ws(int N, int K, int C, size_t* pf, size_t* ct) {
   const long units = (long)(N / (MT * PBM)) * (C / NT), nkb = K / PBK;
   const int ms = pf_maxseg(units, nkb, pf_grid(units * nkb));
   *pf = ms > 1 ? (size_t)units * ms * MT * NT * PBM : 0;
-  *ct = ms > 1 ? (size_t)units : 0;
+  *ct = ms > 1 ? (size_t)units * (1 + ms) : 0;  // epochs, then flags
 }
 
 int launch_operand(const float* x, int ldx, int rows, int H, const float* w, void* act, int ld_act, float* ss,
@@ -803,14 +826,18 @@ extern "C" int rngd_prefill_layers(const rngd_model_t* m, const rngd_prefill_io_
     a.kv = (uint16_t*)io->kv + (size_t)(l - layer0) * layer_elems;
     a.vt = (uint16_t*)io->act2;
     a.NH = m->NH; a.NKV = m->NKV; a.S = io->S;
+    a.tag = 1;
     RNGD_TRY(launch_pf_any<PEPI_QKV>(m->wqkv, m->L, l, NQKV, H, io->act, ld, a, s));
     RNGD_TRY(launch_pf_attn(m, io, a.kv, s));
     a.x = io->x; a.ldx = H;
     a.w_next = m->n2 + (size_t)l * H; a.act_next = (uint16_t*)io->act; a.ld_next = ld; a.ss_out = io->ss;
+    a.tag = 2;
     RNGD_TRY(launch_pf_any<PEPI_RESID>(m->wo, m->L, l, H, QN, io->act_o, QN, a, s));
     a.act_out = (uint16_t*)io->act2; a.ld_act = Mi;
+    a.tag = 3;
     RNGD_TRY(launch_pf_any<PEPI_SWIGLU>(m->wgu, m->L, l, 2 * Mi, H, io->act, ld, a, s));
     a.w_next = l + 1 < m->L ? m->n1 + (size_t)(l + 1) * H : m->norm;
+    a.tag = 4;
     RNGD_TRY(launch_pf_any<PEPI_RESID>(m->wd, m->L, l, H, Mi, io->act2, Mi, a, s));
   }
   return RNGD_OK;
@@ -837,6 +864,7 @@ extern "C" int rngd_tc_gemm_tokens(const void* W, int N, int K, const float* X, 
   a.counters = counters;
   a.x = Y;
   a.ldx = N;
+  a.tag = 5;
   return launch_pf_any<PEPI_RESID>(W, 1, 0, N, K, act, K, a, s);
 }
 
