@@ -595,13 +595,15 @@ def run_micro(args):
         return run_micro_step_small(args)
     if args.micro == "handoff":
         return run_micro_handoff(args)
-    if args.micro == "prefill":
+    if args.micro in ("prefill", "prefill_small"):
+        # prefill_small: the same pass on a 2-layer model of the same shape (~3 GB, for captures)
         from rngd_pd.engines.decode_batch import BatchDecodeEngine
         from rngd_pd.engines.model import ModelConfig
         torch.cuda.set_device(0)
-        cfg = ModelConfig.llama31_8b()
-        eng = BatchDecodeEngine(cfg, synth.SyntheticState(cfg, seed=0), B=B, S=S, group=8)
-        print(json.dumps({"micro": "prefill", **prefill_measure(eng, reps=args.steps, warmup=args.warmup)}),
+        cfg = ModelConfig.llama31_8b() if args.micro == "prefill" else ModelConfig.from_dims(L=2)
+        eng = BatchDecodeEngine(cfg, synth.SyntheticState(cfg, seed=0), B=B, S=S,
+                                group=8 if args.micro == "prefill" else 2)
+        print(json.dumps({"micro": args.micro, **prefill_measure(eng, reps=args.steps, warmup=args.warmup)}),
               flush=True)
         return
     if args.micro.startswith("pf_"):
@@ -794,7 +796,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn", "pf_gate_up", "pf_qkv", "pf_o",
-                                        "pf_down", "handoff", "prefill", "step_small"],
+                                        "pf_down", "handoff", "prefill", "prefill_small", "step_small"],
                     help="time one decode GEMM shape alone (small footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
