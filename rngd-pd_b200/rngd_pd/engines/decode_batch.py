@@ -94,11 +94,15 @@ class BatchDecodeEngine:
         self._partial = torch.zeros(max(partial_floats, 1), **f32)
         self._counters = torch.zeros(max(counters, 1), dtype=torch.int32, device=d)
         self._best = torch.zeros(MAXB, dtype=torch.int64, device=d)
-        self._toks = torch.zeros(B, dtype=torch.int32, device=d)
-        self._pos = torch.zeros(B, dtype=torch.int32, device=d)
+        # tokens and positions side by side, so one host->device copy carries both
+        self._tp = torch.zeros((2, B), dtype=torch.int32, device=d)
+        self._toks, self._pos = self._tp[0], self._tp[1]
         self._next = torch.zeros(B, dtype=torch.int32, device=d)
         self._in_host = torch.zeros((2, B), dtype=torch.int32).pin_memory()
+        self._in_np = self._in_host.numpy()   # the pinned buffer, written in place
         self._out_host = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self._checked = set()                 # cache bindings (data pointers) already validated
+        self._group_numel = self.NG * B * c.n_kv * S * c.head_dim
         self.stream = torch.cuda.Stream(device=d)
         self.use_graph = os.environ.get("RNGD_CUDA_GRAPH", "1") != "0"
         self._graphs = {}
@@ -268,19 +272,23 @@ class BatchDecodeEngine:
 
     def _run(self, toks, positions, Kd, Vd):
         """Upload this step's tokens/positions and run the (captured) step on self.stream."""
-        self._check_cache(Kd, Vd)
+        groups = list(Kd) + list(Vd)
+        key = tuple(t.data_ptr() for t in groups)
+        # a binding (its data pointers) gets the full check once; later steps re-check size and
+        # dtype only, which still catches a smaller tensor allocated at a freed address
+        if key not in self._checked or any(t.numel() != self._group_numel or t.dtype != BF for t in groups):
+            self._check_cache(Kd, Vd)
+            self._checked.add(key)
         self._copied.synchronize()            # the previous step's upload has left the pinned buffer
-        self._in_host[0] = torch.tensor(toks, dtype=torch.int32)
-        self._in_host[1] = torch.tensor(positions, dtype=torch.int32)
+        self._in_np[0] = toks
+        self._in_np[1] = positions
         s = self.stream
         s.wait_stream(torch.cuda.current_stream(self.dev))
         def upload():
-            self._toks.copy_(self._in_host[0], non_blocking=True)
-            self._pos.copy_(self._in_host[1], non_blocking=True)
+            self._tp.copy_(self._in_host, non_blocking=True)
             self._copied.record(s)
 
         with torch.cuda.stream(s):
-            key = tuple(t.data_ptr() for t in list(Kd) + list(Vd))
             g = self._graphs.get(key) if self.use_graph else None
             upload()
             if self.use_graph and g is None:
@@ -327,11 +335,10 @@ class BatchDecodeEngine:
         """Upload tokens/positions for step_device() (validated like step())."""
         toks, positions = self._validate(toks, positions)
         self._copied.synchronize()
-        self._in_host[0] = torch.tensor(toks, dtype=torch.int32)
-        self._in_host[1] = torch.tensor(positions, dtype=torch.int32)
+        self._in_np[0] = toks
+        self._in_np[1] = positions
         with torch.cuda.stream(self.stream):
-            self._toks.copy_(self._in_host[0], non_blocking=True)
-            self._pos.copy_(self._in_host[1], non_blocking=True)
+            self._tp.copy_(self._in_host, non_blocking=True)
             self._copied.record(self.stream)
 
     @_lib.on_device
