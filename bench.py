@@ -483,6 +483,44 @@ def prefill_measure(eng, reps=5, warmup=2):
             "flops_per_pass": flops, "note": "GEMMs issue hi and lo activation halves: tensor work is ~2x the useful"}
 
 
+def prefill_chunk_measure(eng, reps=3, warmup=1):
+    """Chunked prefill (ChunkPrefillEngine, engines/prefill_chunk.py): one 256-token prompt
+    (seed 4) in chunks of 16 positions against a one-lane cache, on the decode engine's card and
+    weights.  Every chunk is one decode step of 16 streams sharing the lane, so it streams the
+    whole 15 GB of weights: HBM-bound, reported as weight GB/s of the median pass."""
+    import torch
+    from rngd_pd import synth
+    from rngd_pd.engines.prefill_chunk import ChunkPrefillEngine
+    C, P = 16, 256
+    ck = ChunkPrefillEngine(eng.cfg, None, S=S, C=C, group=eng.NG, share=eng)
+    toks = synth.tokens(P, seed=4)
+    for _ in range(warmup):
+        ck.prefill_device(toks)
+    ms = []
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ck._e.stream)
+        ck.prefill_device(toks)
+        e1.record(ck._e.stream)
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    t = statistics.median(ms)
+    chunks = P // C
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    gbs = WEIGHT_BYTES * chunks / (t / 1e3) / 1e9
+    del ck
+    return {"workload": "chunked prefill: one prompt of 256 tokens in chunks of 16 (one decode step of 16 "
+                        "streams sharing a cache lane per chunk), Llama-3.1-8B shape",
+            "ms": t, "chunks": chunks, "ms_per_chunk": t / chunks, "weight_gbs": gbs, "peak_gbs": hbm,
+            "frac": gbs / hbm, "note": "includes the host->device upload of each chunk's 16 tokens"}
+
+
 def handoff_pairs(rank, world, dev, reps, warmup):
     """Config 3 across processes: GPU 2i prefills (seeded caches) and pushes into GPU 2i+1's
     decode cache, mapped through CUDA IPC; 1/4/16 requests per batch.  Returns, on every rank,
@@ -719,6 +757,7 @@ def run_ours(args):
 
     roof = gemm_roofline(eng) if rank == 0 else None
     prefill = prefill_measure(eng) if rank == 0 else None
+    prefill_chunk = prefill_chunk_measure(eng) if rank == 0 else None
 
     # ------------------------------------------------- KV handoff (config 3)
     from rngd_pd.engines.model import ModelConfig as _MC
@@ -784,6 +823,7 @@ def run_ours(args):
         "gpu_launches": eng.launches_per_step * K,
         "handoff": handoff,
         "prefill": prefill,
+        "prefill_chunk": prefill_chunk,
     }
     print(json.dumps(line), flush=True)
 

@@ -93,6 +93,10 @@ typedef struct rngd_decode_io {
   int32_t* counters;    /* split-tile epochs, rngd_decode_workspace() int32 entries, zeroed once */
   uint64_t* best;       /* [16] argmax keys */
   int32_t* next;        /* device [B] greedy next tokens */
+  const int32_t* lanes; /* optional device [B]: the cache lane of each stream (< Bcap); NULL = stream b
+                           uses lane b.  Streams may share a lane at distinct positions: a chunk of
+                           one sequence's prompt (engines/prefill_chunk.py:109-142), where stream c
+                           holds position base + c and attends to the lane's positions <= its own. */
 } rngd_decode_io_t;
 
 /* Sizes of the decode scratch buffers for a model (shape-only; independent of B). */

@@ -282,3 +282,31 @@ def prefill(model: SynthModel, tokens, S, kv_bf16=True):
         K[i, :, :, :P] = kT
         V[i, :, :P, :] = vT
     return K, V, lm_logits(x[P - 1:P], model.norm(), model.lm_head(), d.eps)[0]
+
+
+def prefill_chunked(model: SynthModel, tokens, S, C, kv_bf16=True):
+    """Chunked prefill of one prompt, C positions per pass, against a cache that starts empty;
+    returns (K [L,NKV,HD,S], V [L,NKV,S,HD], logits_last).
+
+    Follows engines/prefill_chunk.py:108-142: the prompt is padded with its last token to a
+    whole number of chunks (the pad positions' K/V are written too), every layer of a chunk
+    runs cpu_layer_chunk at base = the chunk's first position, and the next token comes from
+    the last prompt position's hidden state through the final norm and lm_head.
+    """
+    d = model.d
+    inv = inv_freq(d)
+    P = len(tokens)
+    pad = (-P) % C
+    toks = list(tokens) + [tokens[-1]] * pad
+    K = np.zeros((d.L, d.NKV, d.HD, S), np.float32)
+    V = np.zeros((d.L, d.NKV, S, d.HD), np.float32)
+    emb = model.embed()
+    hid = None
+    for base in range(0, len(toks), C):
+        x = emb[toks[base:base + C]].astype(np.float32)
+        for i in range(d.L):
+            x, K[i], V[i] = cpu_layer_chunk(x, model.layer(i), K[i], V[i], inv, base, C, S, d.eps, d,
+                                            kv_bf16=kv_bf16)
+        hid = x
+    h = hid[(P - 1) % C:(P - 1) % C + 1]
+    return K, V, lm_logits(h, model.norm(), model.lm_head(), d.eps)[0]

@@ -250,7 +250,8 @@ constexpr int kAttnThreads = 256;  // two halves of 128 threads, one per pair of
 template <bool FUSED>
 __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq, const uint16_t* __restrict__ kc,
                                            const uint16_t* __restrict__ vc, const int32_t* __restrict__ pos,
-                                           int NH, int NKV, int S, float* __restrict__ part,
+                                           const int32_t* __restrict__ lanes, int NH, int NKV, int S,
+                                           float* __restrict__ part,
                                            unsigned long long* __restrict__ recw, int* __restrict__ epochs,
                                            uint16_t* __restrict__ act, int ld_act) {
   extern __shared__ __align__(16) uint8_t attn_smem[];
@@ -267,7 +268,8 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
   const int nchunk = gridDim.x;
   const int PS = kHD + 2;  // partial record: o[HD], m, l
   const int s0 = c * kChunk;
-  const size_t head_base = ((size_t)b * NKV + kvh) * (size_t)S * kHD;
+  const int lane_b = lanes != nullptr ? lanes[b] : b;  // the cache lane this stream reads
+  const size_t head_base = ((size_t)lane_b * NKV + kvh) * (size_t)S * kHD;
   const uint8_t* kg = (const uint8_t*)(kc + head_base + (size_t)s0 * kHD);
   const uint8_t* vg = (const uint8_t*)(vc + head_base + (size_t)s0 * kHD);
   int P, n, old = 0;  // positions < P are attended; rows [0, old) of the chunk staged early
@@ -276,7 +278,12 @@ __device__ __forceinline__ void attn_chunk(const float* __restrict__ q, int ldq,
     P = min(pb + 1, S);
     n = min(kChunk, P - s0);
     if (n <= 0) return;  // no positions in this chunk: chunk 0 reads only chunks that hold some
-    old = max(0, min(n, pb - s0));
+    // rows this step may write: from pos[b] on; with a lane map, from the smallest position of
+    // any stream (streams sharing a lane append to it in this same step)
+    int fresh = pb;
+    if (lanes != nullptr)
+      for (int bb = 0; bb < (int)gridDim.z; bb++) fresh = min(fresh, pos[bb]);
+    old = max(0, min(n, fresh - s0));
     for (int i = t; i < old * 16; i += kAttnThreads) {
       const int j = i >> 4, c16 = (i & 15) * 16;
       cp_async16(sK + j * kRowBytes + c16, kg + (size_t)j * 256 + c16);
@@ -564,17 +571,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const float*
                                                            const uint16_t* __restrict__ vc,
                                                            const int32_t* __restrict__ pos, int NH,
                                                            int NKV, int S, float* __restrict__ part) {
-  attn_chunk<false>(q, ldq, kc, vc, pos, NH, NKV, S, part, nullptr, nullptr, nullptr, 0);
+  attn_chunk<false>(q, ldq, kc, vc, pos, nullptr, NH, NKV, S, part, nullptr, nullptr, nullptr, 0);
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 3) attn_fused_kernel(const float* __restrict__ q, int ldq,
                                                          const uint16_t* __restrict__ kc,
                                                          const uint16_t* __restrict__ vc,
-                                                         const int32_t* __restrict__ pos, int NH, int NKV,
+                                                         const int32_t* __restrict__ pos,
+                                                         const int32_t* __restrict__ lanes, int NH, int NKV,
                                                          int S, unsigned long long* __restrict__ recw,
                                                          int* __restrict__ epochs, uint16_t* __restrict__ act,
                                                          int ld_act) {
-  attn_chunk<true>(q, ldq, kc, vc, pos, NH, NKV, S, nullptr, recw, epochs, act, ld_act);
+  attn_chunk<true>(q, ldq, kc, vc, pos, lanes, NH, NKV, S, nullptr, recw, epochs, act, ld_act);
 }
 
 // Combines the chunk partials of one (stream, head) in chunk order.
@@ -638,8 +646,9 @@ size_t attn_fused_scratch_units(int Bcap, int NKV, int S) {
 }
 
 // The decode step's attention: one fused grid (chunks, combine, hi/lo operand of the O GEMM).
-int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B,
-                           int NH, int NKV, int HD, int S, float* part, void* act, int ld_act, cudaStream_t s) {
+int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos,
+                           const int32_t* lanes, int B, int NH, int NKV, int HD, int S, float* part, void* act,
+                           int ld_act, cudaStream_t s) {
   RNGD_REQUIRE(q && kc && vc && pos && part && act, "attn_decode: null pointer");
   RNGD_REQUIRE(HD == kHD && NH == kG * NKV, "attn_decode: built for HD=128 and 4 query heads per kv head");
   RNGD_REQUIRE(S % kChunk == 0 && S > 0 && S <= 8192, "attn_decode: S=%d must be a multiple of 128", S);
@@ -651,7 +660,7 @@ int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* 
   int* epochs = (int*)part;
   unsigned long long* recw = (unsigned long long*)(part + attn_epoch_units(NKV));
   return launch_pdl(attn_fused_kernel, dim3(nchunk, NKV, B), dim3(kAttnThreads), kAttnSmem, s, "attn_fused_kernel", q, ldq,
-                    (const uint16_t*)kc, (const uint16_t*)vc, pos, NH, NKV, S, recw, epochs, (uint16_t*)act,
+                    (const uint16_t*)kc, (const uint16_t*)vc, pos, lanes, NH, NKV, S, recw, epochs, (uint16_t*)act,
                     ld_act);
 }
 

@@ -83,6 +83,7 @@ struct GemmArgs {
   int ldq;
   uint16_t* kc;
   uint16_t* vc;
+  const int32_t* lanes;  // [B] cache lane of each stream, nullptr = stream b -> lane b
   int NH, NKV, S;
   // RESID: x += y; act_next = hi/lo(x * w_next); ss_out = per-tile sums of squares of x
   float* x;
@@ -106,9 +107,10 @@ struct GemmArgs {
   unsigned long long* trace;
 };
 
-// smem: stages | barriers (2*STAGES + 5) + tmem slot/flags (64 B) | scale (64 B) | pos (64 B) | ys | s_red
+// smem: stages | barriers (2*STAGES + 5) + tmem slot/flags (64 B) | scale (64 B) | pos (64 B) | lane (64 B)
+//       | ys | s_red
 constexpr size_t kBarBytes = (2 * STAGES + 5) * 8;
-constexpr size_t kSmemBytes = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + kBarBytes + 64 + 64 + 64 +
+constexpr size_t kSmemBytes = 1024 /*align*/ + STAGES * (A_BYTES + B_BYTES) + kBarBytes + 64 + 64 + 64 + 64 +
                               BM * YS_LD * 4 + 4 * MAXB * 8;
 
 __device__ __forceinline__ uint32_t orderable(float f) {
@@ -149,7 +151,8 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
   uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + kBarBytes);
   float* s_scale = (float*)((uint8_t*)full + kBarBytes + 64);  // [16]
   int* s_pos = (int*)((uint8_t*)full + kBarBytes + 128);       // [16]
-  float* ys = (float*)((uint8_t*)full + kBarBytes + 192);
+  int* s_lane = (int*)((uint8_t*)full + kBarBytes + 192);      // [16] cache lane of each stream
+  float* ys = (float*)((uint8_t*)full + kBarBytes + 256);
   unsigned long long* s_red = (unsigned long long*)(ys + BM * YS_LD);  // [4][16]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -282,7 +285,10 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
     // while the weights stream rather than on the GEMM's tail
     float rcos[SPG], rsin[SPG];
     if constexpr (EPI == EPI_QKV) {
-      if (ep < MAXB) s_pos[ep] = ep < a.B ? a.pos[ep] : -1;
+      if (ep < MAXB) {
+        s_pos[ep] = ep < a.B ? a.pos[ep] : -1;
+        s_lane[ep] = ep < a.B ? (a.lanes != nullptr ? a.lanes[ep] : ep) : 0;
+      }
       const float invf = a.inv[r & 63];
 #pragma unroll
       for (int i = 0; i < SPG; i++) {
@@ -490,7 +496,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
                 if (head < a.NH) {
                   a.q[(size_t)b * a.ldq + n] = o[i];
                 } else if (p >= 0 && p < a.S) {
-                  a.kc[(((size_t)b * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o[i]);
+                  a.kc[(((size_t)s_lane[b] * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o[i]);
                 }
               }
             }
@@ -499,7 +505,7 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
             for (int i = 0; i < SPG; i++) {
               const int b = sb + i, p = s_pos[b];
               if (b < a.B && p >= 0 && p < a.S)
-                a.vc[(((size_t)b * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[i]);
+                a.vc[(((size_t)s_lane[b] * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[i]);
             }
           }
         } else if constexpr (EPI == EPI_SWIGLU) {
@@ -789,7 +795,8 @@ int launch_operand(const float* x, int ldx, int B, int H, const float* w, void* 
   return launch_operand_ex(x, ldx, B, H, w, act, ld_act, MAXB, ss, MAXB, best, s);
 }
 
-int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos, int B,
+int launch_attn_decode_act(const float* q, int ldq, const void* kc, const void* vc, const int32_t* pos,
+                           const int32_t* lanes, int B,
                            int NH, int NKV, int HD, int S, float* part, void* act, int ld_act, cudaStream_t s);
 int launch_embed(const void* emb, const int32_t* toks, int H, int V, float* x, int B, cudaStream_t s);
 
@@ -810,7 +817,8 @@ static int check_tc_io(const rngd_model_t* m, const rngd_decode_io_t* io) {
   RNGD_REQUIRE(m->HD == 128 && m->NH == 4 * m->NKV, "decode: kernels are built for HD=128, NH=4*NKV");
   RNGD_REQUIRE(m->H % 128 == 0 && (2 * m->M) % 128 == 0 && m->M % 64 == 0,
                "decode: H and 2*M must be multiples of 128");
-  RNGD_REQUIRE(io->B >= 1 && io->B <= 16 && io->B <= io->Bcap, "decode: B=%d outside 1..min(16, Bcap)", io->B);
+  RNGD_REQUIRE(io->B >= 1 && io->B <= 16 && (io->lanes != nullptr || io->B <= io->Bcap) && io->Bcap >= 1,
+               "decode: B=%d outside 1..16 (and <= Bcap=%d without a lane map)", io->B, io->Bcap);
   RNGD_REQUIRE(io->S % 128 == 0 && io->S > 0 && io->S <= 8192, "decode: S=%d must be a multiple of 128", io->S);
   RNGD_REQUIRE(io->kcache && io->vcache && io->toks && io->pos && io->x && io->q && io->act && io->act_o &&
                    io->act2 && io->ss && io->logits && io->attn_part && io->partial && io->counters && io->best &&
@@ -923,11 +931,11 @@ extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t*
     a.eps = m->eps;
     a.inv_h = 1.0f / (float)H;
     // attention block: io->act holds x * n1[l] (written by the prologue or the previous layer)
-    a.pos = io->pos; a.inv = m->inv_freq; a.q = io->q; a.ldq = QN; a.kc = kc; a.vc = vc;
+    a.pos = io->pos; a.inv = m->inv_freq; a.q = io->q; a.ldq = QN; a.kc = kc; a.vc = vc; a.lanes = io->lanes;
     a.NH = m->NH; a.NKV = m->NKV; a.S = io->S;
     a.counters = io->counters + off[0]; a.tag = 1;
     RNGD_TRY(launch_skgemm<EPI_QKV>(m->wqkv, m->L, l, NQKV, H, io->act, ld_act, a, s));
-    RNGD_TRY(launch_attn_decode_act(io->q, QN, kc, vc, io->pos, B, m->NH, m->NKV, m->HD, io->S, io->attn_part,
+    RNGD_TRY(launch_attn_decode_act(io->q, QN, kc, vc, io->pos, io->lanes, B, m->NH, m->NKV, m->HD, io->S, io->attn_part,
                                     io->act_o, QN, s));
     // O projection + residual; writes x * n2[l] for the MLP
     a.x = io->x; a.ldx = H;

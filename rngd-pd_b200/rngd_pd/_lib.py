@@ -51,7 +51,7 @@ class DecodeIO(ctypes.Structure):
     _fields_ = [("B", _i32), ("Bcap", _i32), ("S", _i32), ("kv_layers", _i32), ("kcache", _vp), ("vcache", _vp),
                 ("toks", _vp), ("pos", _vp), ("x", _vp), ("q", _vp), ("act", _vp), ("act_o", _vp),
                 ("act2", _vp), ("ss", _vp), ("logits", _vp), ("attn_part", _vp), ("partial", _vp),
-                ("counters", _vp), ("best", _vp), ("next", _vp)]
+                ("counters", _vp), ("best", _vp), ("next", _vp), ("lanes", _vp)]
 
 
 class PrefillIO(ctypes.Structure):

@@ -66,3 +66,19 @@ def test_prefill_c_equals_numpy():
     np.testing.assert_allclose(lg, lgr, rtol=1e-4, atol=1e-4)
     assert nxt == int(np.argmax(lgr))
     cm.close()
+
+
+def test_chunked_prefill_driver_matches_whole_prompt_prefill():
+    """The restated chunked engine loop (engines/prefill_chunk.py:108-142) gives the same cache
+    and logits as the whole-prompt prefill for one chunk and for several."""
+    import numpy as np
+    from oracle import ref_np as R
+    d = R.Dims(H=256, M=512, NH=4, NKV=1, HD=128, L=2, V=300)
+    m = R.SynthModel(d, seed=0)
+    toks = [(7 * i + 3) % d.V for i in range(24)]
+    K1, V1, l1 = R.prefill(m, toks, 32, kv_bf16=True)
+    for C in (24, 8):
+        K2, V2, l2 = R.prefill_chunked(m, toks, 32, C, kv_bf16=True)
+        np.testing.assert_allclose(K2, K1, rtol=1e-2, atol=2e-3)
+        np.testing.assert_allclose(V2, V1, rtol=1e-2, atol=2e-3)
+        np.testing.assert_allclose(l2, l1, rtol=1e-4, atol=1e-4)
