@@ -1,0 +1,294 @@
+"""Iteration-level (continuous) batching over the B200 decode engines
+(the reference's _ContinuousScheduler, src/rngd_pd/serving/cluster.py:832-1134, and its
+one-card producer, serving/cluster.py:646-818).
+
+Before every decode step the loop admits whatever is waiting into the free lanes and
+retires whatever finished, so a batch can mix a stream on its third token with one on its
+hundredth.  A stream's cache comes from `produce(item) -> (K, V, first, pos, aux_ms)`, the
+only thing that differs between a one-card server (prefill on the same card) and a
+disaggregated one; admission writes it into one lane of the resident cache
+(BatchDecodeEngine.write_slot_kv) and leaves the other lanes alone.  With a TieredDecode
+engine the loop reports the live lanes before each step (set_live), so the step runs at the
+narrowest width that covers them.
+
+While streams are running, a new prompt's prefill can be staged: `produce_owner.begin_produce`
+hands back a stage whose `advance(n)` runs n layer groups, and the loop runs a few groups
+per iteration between decode steps, so an arriving prompt does not stall every stream in
+flight for a whole prefill.  With nothing running, waiting prompts are admitted at once.
+
+Items are dicts: "tokens" (the prompt) and "max_new" (tokens to return, the prefill's next
+token included), optionally "on_token" (called with each token as it is produced; it must
+not block).  submit(item) blocks and returns the item's result dict, or raises the error
+that ended it; an error in a step ends the streams of that step only and the loop goes on.
+"""
+import collections
+import os
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+
+
+def _emit(item, token):
+    cb = item.get("on_token")
+    if cb is not None:
+        cb(token)
+
+
+class ContinuousScheduler:
+    def __init__(self, B, engine, produce, admit_min=1, produce_owner=None, produce_on_device=True,
+                 stage_groups=None, stage_admission=None):
+        self.B, self.eng, self.produce = B, engine, produce
+        self.admit_min = max(1, int(admit_min))
+        self.produce_owner = produce_owner
+        # a producer that reads host memory only (a disaggregated load) runs in the background
+        # from arrival on; the loop admits streams whose cache is ready.  One that uses the
+        # card runs inside the loop, in order with the decode steps.
+        self._loader = None if produce_on_device else ThreadPoolExecutor(
+            max_workers=int(os.environ.get("PD_KV_LOADERS", "2")))
+        self.stage_groups = int(stage_groups if stage_groups is not None
+                                else os.environ.get("PD_STAGE_GROUPS", "4"))
+        self.stage_admission = (stage_admission if stage_admission is not None
+                                else os.environ.get("RNGD_ADMIT", "stage") != "block")
+        self.slots = [None] * B
+        self.pending = collections.deque()
+        self.cv = threading.Condition()
+        self._staging = None             # (lane, item, stage) of a prefill in progress
+        self._closed = False
+        # counters: steps, lane-steps that carried a stream, and the empty lane-steps split into
+        # starved (nothing was waiting) and held (something waited, admit_min kept it out)
+        self.steps = self.lane_steps = 0
+        self.starved_lane_steps = self.held_lane_steps = 0
+        self.admits, self.admit_ms, self.admit_stall_ms = 0, 0.0, 0.0
+        self.stage_steps = 0
+        self._thread = threading.Thread(target=self._loop, daemon=True)
+        self._thread.start()
+
+    # ---------------------------------------------------------------- callers
+    def submit(self, item):
+        """Queue one request and wait for it; returns its result dict."""
+        item["ev"] = threading.Event()
+        item["out"] = item["err"] = None
+        if self._loader is not None:
+            item["_fut"] = self._loader.submit(self.produce, item)
+            item["_fut"].add_done_callback(lambda _f: self._wake())
+        with self.cv:
+            if self._closed:
+                raise RuntimeError("scheduler is closed")
+            self.pending.append(item)
+            self.cv.notify()
+        item["ev"].wait()
+        if item["err"] is not None:
+            raise item["err"]
+        return item["out"]
+
+    def close(self):
+        """Stop the loop after the current iteration; queued requests fail."""
+        with self.cv:
+            self._closed = True
+            self.cv.notify()
+        self._thread.join(timeout=60)
+        err = RuntimeError("scheduler closed")
+        for item in list(self.pending):
+            if not item["ev"].is_set():
+                item["err"] = err
+                item["ev"].set()
+        self.pending.clear()
+        if self._loader is not None:
+            self._loader.shutdown(wait=False)
+
+    def occupancy(self):
+        return self.lane_steps / max(self.steps * self.B, 1)
+
+    # ---------------------------------------------------------------- loop
+    def _wake(self):
+        with self.cv:
+            self.cv.notify()
+
+    def _live(self):
+        return [i for i, s in enumerate(self.slots) if s is not None]
+
+    def _ready(self):
+        """Pending items the loop may take now (called with cv held); a background load that
+        failed fails its own request only."""
+        if self._loader is None:
+            return len(self.pending)
+        ready, waiting = [], []
+        for item in self.pending:
+            fut = item["_fut"]
+            if not fut.done():
+                waiting.append(item)
+            elif fut.exception() is not None:
+                item["err"] = fut.exception()
+                item["ev"].set()
+            else:
+                item["_produced"] = fut.result()
+                ready.append(item)
+        self.pending = collections.deque(ready + waiting)
+        return len(ready)
+
+    def _seat(self, lane, item, produced):
+        K, V, first, pos, aux_ms = produced
+        self.slots[lane] = {"item": item, "cur": int(first), "pos": int(pos), "pos0": int(pos),
+                            "outs": [int(first)], "aux_ms": aux_ms, "step_ms": [],
+                            "t0": time.perf_counter(), "s0": self.steps, "l0": self.lane_steps,
+                            "v0": self.starved_lane_steps, "h0": self.held_lane_steps}
+        _emit(item, int(first))
+
+    def _admit(self, taking, Kd, Vd):
+        """Produce, write and seat one stream at a time (its first token goes out while the
+        rest of the admission is still running)."""
+        ms = 0.0
+        for lane, item in taking:
+            produced = item.pop("_produced", None) or self.produce(item)
+            t0 = time.perf_counter()
+            Kd, Vd = self.eng.write_slot_kv(Kd, Vd, lane, produced[0], produced[1])
+            ms += (time.perf_counter() - t0) * 1e3
+            self._seat(lane, item, produced)
+        self.admits += 1
+        self.admit_ms += ms
+        self.admit_stall_ms += ms
+        return Kd, Vd
+
+    def _finish(self, lane):
+        s, self.slots[lane] = self.slots[lane], None
+        st = sorted(s["step_ms"])
+        n = max(self.steps - s["s0"], 1)
+        s["item"]["out"] = {
+            "tokens": s["outs"], "pos": s["pos0"], "prefill_ms": round(s["aux_ms"], 1),
+            "tpot_ms": round(st[len(st) // 2], 3) if st else 0.0,
+            "decode_ms": round((time.perf_counter() - s["t0"]) * 1e3, 1),
+            "batch": len(self._live()) + 1, "batch_width": self.B, "sched": "continuous",
+            "admit_ms": round(self.admit_ms / max(self.admits, 1), 2),
+            "occupancy": round((self.lane_steps - s["l0"]) / n, 2),
+            "starved_lanes": round((self.starved_lane_steps - s["v0"]) / n, 2),
+            "held_lanes": round((self.held_lane_steps - s["h0"]) / n, 2),
+            "occupancy_all": round(self.lane_steps / max(self.steps, 1), 2),
+            "admit_stall_ms": round(self.admit_stall_ms, 1)}
+        s["item"]["ev"].set()
+
+    def _fail_all(self, e, taking):
+        for lane in self._live():
+            s, self.slots[lane] = self.slots[lane], None
+            s["item"]["err"] = e
+            s["item"]["ev"].set()
+        for _lane, item in taking:
+            if not item["ev"].is_set():
+                item["err"] = item.get("err") or e
+                item["ev"].set()
+        if self._staging is not None:
+            item = self._staging[1]
+            self._staging = None
+            if not item["ev"].is_set():
+                item["err"] = e
+                item["ev"].set()
+
+    def _loop(self):
+        Kd = Vd = None
+        while True:
+            with self.cv:
+                while True:
+                    if self._closed:
+                        return
+                    ready = self._ready()
+                    if ready or self._live() or self._staging is not None:
+                        break
+                    self.cv.wait(timeout=0.05 if self.pending else None)
+                free = [i for i, s in enumerate(self.slots) if s is None]
+                n = 0 if self._staging is not None else min(len(free), ready)
+                if self._live() and n < min(self.admit_min, len(free)):
+                    n = 0                        # not worth an admission yet
+                taking = [(free[k], self.pending.popleft()) for k in range(n)]
+                waiting = len(self.pending)
+                empty = len(free) - n
+                self.starved_lane_steps += max(0, empty - waiting)
+                self.held_lane_steps += min(empty, waiting)
+            try:
+                if Kd is None:
+                    Kd, Vd = self.eng.blank_kv()
+                tell = getattr(self.eng, "set_live", None)    # TieredDecode
+                if tell is not None:
+                    tell(self._live())
+                if self._staging is not None:
+                    lane, item, stage = self._staging
+                    self.stage_steps += 1
+                    if stage.advance(self.stage_groups):
+                        produced = stage.result()
+                        self._staging = None
+                        t0 = time.perf_counter()
+                        Kd, Vd = self.eng.write_slot_kv(Kd, Vd, lane, produced[0], produced[1])
+                        self.admit_stall_ms += (time.perf_counter() - t0) * 1e3
+                        self._seat(lane, item, produced)
+                elif (taking and self._live() and self.stage_admission
+                      and hasattr(self.produce_owner, "begin_produce") and "_produced" not in taking[0][1]):
+                    # protect the running streams: one prompt a few layer groups per iteration
+                    lane, item = taking[0]
+                    self._staging = (lane, item, self.produce_owner.begin_produce(item))
+                    with self.cv:
+                        for _lane, rest in reversed(taking[1:]):
+                            self.pending.appendleft(rest)
+                    taking = []
+                elif taking:
+                    Kd, Vd = self._admit(taking, Kd, Vd)
+                live = self._live()
+                if not live:
+                    continue
+                if tell is not None:
+                    tell(live)
+                cur = [self.slots[i]["cur"] if self.slots[i] else 0 for i in range(self.B)]
+                pos = [self.slots[i]["pos"] if self.slots[i] else 0 for i in range(self.B)]
+                t1 = time.perf_counter()
+                nxt, Kd, Vd = self.eng.step(cur, pos, Kd, Vd)
+                dt = (time.perf_counter() - t1) * 1e3
+                done = []
+                for i in live:
+                    s = self.slots[i]
+                    if len(s["outs"]) >= s["item"]["max_new"]:   # max_new = 1: the prefill's token
+                        done.append(i)
+                        continue
+                    s["step_ms"].append(dt)
+                    s["outs"].append(int(nxt[i]))
+                    _emit(s["item"], int(nxt[i]))
+                    s["cur"] = int(nxt[i])
+                    s["pos"] += 1
+                    if len(s["outs"]) >= s["item"]["max_new"]:
+                        done.append(i)
+                self.lane_steps += len(live)
+                self.steps += 1
+                for i in done:
+                    self._finish(i)
+            except Exception as e:   # a bad step fails its own streams; the loop goes on
+                self._fail_all(e, taking)
+                Kd = Vd = None
+
+
+class OneCardProducer:
+    """Prefill on the decode card and hand the scheduler the device cache directly (the
+    reference's SoloWorker producers, serving/cluster.py:747-776)."""
+
+    def __init__(self, prefill_engine):
+        self.pre = prefill_engine
+
+    def produce(self, item):
+        t0 = time.perf_counter()
+        K, V, nxt = self.pre.prefill_device(item["tokens"])
+        return K, V, nxt, len(item["tokens"]), (time.perf_counter() - t0) * 1e3
+
+    def begin_produce(self, item):
+        stage = self.pre.begin_device_prefill(item["tokens"])
+        t0 = time.perf_counter()
+        P = len(item["tokens"])
+
+        class _Stage:
+            def advance(self, n=1):
+                return stage.advance(n)
+
+            def result(self):
+                K, V, nxt = stage.result()
+                return K, V, nxt, P, (time.perf_counter() - t0) * 1e3
+
+        return _Stage()
+
+
+_ContinuousScheduler = ContinuousScheduler   # the reference's private name
+
+__all__ = ["ContinuousScheduler", "OneCardProducer"]
