@@ -623,12 +623,15 @@ def run_micro_step_small(args):
                       "status": _lib.device_status()}), flush=True)
 
 
-def run_micro_serve(args):
-    """Continuous batching on one card (serving/scheduler.py over BatchDecodeEngine B=16 and a
-    FullPrefillEngine sharing its weights): a seeded Poisson trace in the shape of BASELINE
-    config 5 (prompts U[128, 448] tokens, 64 output tokens each) submitted by one client thread
-    per request at its arrival time.  Box tok/s = output tokens / (last completion - first
-    arrival); TTFT = arrival -> first token; TPOT = a request's median decode step."""
+def run_micro_serve(args, pd=False):
+    """Continuous batching (serving/scheduler.py over BatchDecodeEngine B=16): a seeded Poisson
+    trace in the shape of BASELINE config 5 (prompts U[128, 448] tokens, 64 output tokens each)
+    submitted by one client thread per request at its arrival time.  One card (pd=False): a
+    FullPrefillEngine on the decode engine's weights, prompts admitted between steps.  PD on two
+    GPUs of one process (pd=True): prefill on GPU 0 pushes each prompt's cache over NVLink into
+    the decode lane leased on GPU 1 while GPU 1 keeps stepping.  Box tok/s = output tokens /
+    (last completion - first arrival); TTFT = arrival -> first token; TPOT = a request's median
+    decode step."""
     import threading
     import numpy as np
     import torch
@@ -637,24 +640,37 @@ def run_micro_serve(args):
     from rngd_pd.engines.model import ModelConfig
     from rngd_pd.engines.prefill_full import FullPrefillEngine
     from rngd_pd import _lib
-    from rngd_pd.serving.scheduler import ContinuousScheduler, OneCardProducer
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    from rngd_pd.serving.scheduler import ContinuousScheduler, NvlinkProducer, OneCardProducer
     cfg = ModelConfig.llama31_8b()
-    eng = BatchDecodeEngine(cfg, synth.SyntheticState(cfg, seed=0), B=B, S=S, group=8)
-    pre = FullPrefillEngine(cfg, eng.w, C=256, group=2, S=S)
+    if pd:
+        if torch.cuda.device_count() < 2:
+            print(json.dumps({"micro": "serve_pd", "unavailable": "needs two GPUs"}), flush=True)
+            return
+        eng = BatchDecodeEngine(cfg, synth.SyntheticState(cfg, seed=0), B=B, S=S, group=8, chip=1)
+        pre = FullPrefillEngine(cfg, synth.SyntheticState(cfg, seed=0), C=256, group=2, S=S, chip=0)
+    else:
+        torch.cuda.set_device(0)
+        eng = BatchDecodeEngine(cfg, synth.SyntheticState(cfg, seed=0), B=B, S=S, group=8)
+        pre = FullPrefillEngine(cfg, eng.w, C=256, group=2, S=S)
     pre.add_bucket(512)
     rate, n_req, out_tok = float(os.environ.get("SERVE_RATE", "40")), int(os.environ.get("SERVE_N", "96")), 64
     rng = np.random.default_rng(5)
     arrivals = np.cumsum(rng.exponential(1.0 / rate, n_req))
     prompts = [rng.integers(0, cfg.vocab, int(rng.integers(128, 449))).tolist() for _ in range(n_req)]
-    prod = OneCardProducer(pre)
+    if pd:
+        kv = eng.blank_kv()
+        prod = NvlinkProducer(pre, eng, kv)
+        sched = ContinuousScheduler(B, eng, None, produce_owner=prod, idle_pos=S - 1, kv=kv)
+        stage = False
+    else:
+        prod = OneCardProducer(pre)
     # admission: waiting prompts prefilled back to back between decode steps (RNGD_ADMIT=block;
     # measured here against staging 4 or 16 layer groups per iteration, the reference's default
     # for a card whose prefill group costs as much as a decode step: a B200 prefill costs a few
     # decode steps, and blocking gave the best TTFT and box throughput); SERVE_ADMIT=stage for the other
-    stage = os.environ.get("SERVE_ADMIT", "block") == "stage"
-    sched = ContinuousScheduler(B, eng, prod.produce, produce_owner=prod, stage_admission=stage)
+    if not pd:
+        stage = os.environ.get("SERVE_ADMIT", "block") == "stage"
+        sched = ContinuousScheduler(B, eng, prod.produce, produce_owner=prod, stage_admission=stage)
     # warm-up outside the trace: every prefill bucket and the captured step
     for P in (200, 400):
         sched.submit({"tokens": [1] * P, "max_new": 4})
@@ -680,12 +696,16 @@ def run_micro_serve(args):
     for t in threads:
         t.join()
     sched.close()
+    if pd:
+        prod.close()
     ok = [i for i in range(n_req) if done_at[i] is not None]
     span = max(done_at[i] for i in ok) - (t_start + arrivals[0])
     pct = lambda v, q: float(np.percentile([x for x in v if x is not None], q))
-    print(json.dumps({"micro": "serve", "workload": "one card: continuous batching B=16, S=512, seeded Poisson "
-                      "trace, prompts U[128,448], 64 output tokens, Llama-3.1-8B shape",
-                      "admission": "stage" if stage else "block",
+    print(json.dumps({"micro": "serve_pd" if pd else "serve",
+                      "workload": ("PD on two GPUs (prefill GPU 0 -> NVLink -> decode lanes on GPU 1)" if pd else
+                                   "one card") + ": continuous batching B=16, S=512, seeded Poisson trace, prompts "
+                                   "U[128,448], 64 output tokens, Llama-3.1-8B shape",
+                      "admission": "nvlink lane fill" if pd else ("stage" if stage else "block"),
                       "rate_req_s": rate, "requests": n_req, "completed": len(ok), "errors": errors[:3],
                       "box_tok_s": len(ok) * out_tok / span, "span_s": span,
                       "ttft_ms_p50": pct(ttft, 50), "ttft_ms_p90": pct(ttft, 90),
@@ -702,8 +722,8 @@ def run_micro(args):
         return run_micro_attn(args)
     if args.micro == "step_small":
         return run_micro_step_small(args)
-    if args.micro == "serve":
-        return run_micro_serve(args)
+    if args.micro in ("serve", "serve_pd"):
+        return run_micro_serve(args, pd=args.micro == "serve_pd")
     if args.micro == "handoff":
         return run_micro_handoff(args)
     if args.micro in ("prefill", "prefill_small"):
@@ -917,7 +937,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn", "pf_gate_up", "pf_qkv", "pf_o",
-                                        "pf_down", "handoff", "prefill", "prefill_small", "step_small", "serve"],
+                                        "pf_down", "handoff", "prefill", "prefill_small", "step_small", "serve",
+                                        "serve_pd"],
                     help="time one decode GEMM shape alone (small footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -16,6 +16,13 @@ hands back a stage whose `advance(n)` runs n layer groups, and the loop runs a f
 per iteration between decode steps, so an arriving prompt does not stall every stream in
 flight for a whole prefill.  With nothing running, waiting prompts are admitted at once.
 
+A producer that writes the lane itself (`produce_owner.start_lane(item, lane) -> Future`, e.g.
+a prefill on another GPU pushing into the reserved lane over NVLink) gets a free lane when a
+request is taken; the lane stays out of the batch while it fills, the other lanes keep
+stepping, and the stream is seated when the future completes.  Lanes without a stream step at
+position `idle_pos`: pass S - 1 when lanes fill asynchronously, so the appends of idle lanes
+stay clear of the rows a push is writing (a prompt never reaches the last row).
+
 Items are dicts: "tokens" (the prompt) and "max_new" (tokens to return, the prefill's next
 token included), optionally "on_token" (called with each token as it is produced; it must
 not block).  submit(item) blocks and returns the item's result dict, or raises the error
@@ -36,8 +43,12 @@ def _emit(item, token):
 
 class ContinuousScheduler:
     def __init__(self, B, engine, produce, admit_min=1, produce_owner=None, produce_on_device=True,
-                 stage_groups=None, stage_admission=None):
+                 stage_groups=None, stage_admission=None, idle_pos=0, kv=None):
         self.B, self.eng, self.produce = B, engine, produce
+        self._kv0 = kv                   # a resident cache to use (e.g. one a transport writes into)
+        self.idle_pos = int(idle_pos)
+        self._start_lane = getattr(produce_owner, "start_lane", None)
+        self.filling = {}                # lane -> (item, future) while its cache is produced elsewhere
         self.admit_min = max(1, int(admit_min))
         self.produce_owner = produce_owner
         # a producer that reads host memory only (a disaggregated load) runs in the background
@@ -107,6 +118,19 @@ class ContinuousScheduler:
     def _live(self):
         return [i for i, s in enumerate(self.slots) if s is not None]
 
+    def _free(self):
+        return [i for i, s in enumerate(self.slots) if s is None and i not in self.filling]
+
+    def _collect_filled(self):
+        """Seat the streams whose lanes finished filling; a failed fill fails its request only."""
+        for lane in [ln for ln, (_it, fut) in self.filling.items() if fut.done()]:
+            item, fut = self.filling.pop(lane)
+            if fut.exception() is not None:
+                item["err"] = fut.exception()
+                item["ev"].set()
+            else:
+                self._seat(lane, item, fut.result())
+
     def _ready(self):
         """Pending items the loop may take now (called with cv held); a background load that
         failed fails its own request only."""
@@ -167,6 +191,7 @@ class ContinuousScheduler:
         s["item"]["ev"].set()
 
     def _fail_all(self, e, taking):
+        # lanes still filling keep filling: their requests are seated (or failed) later
         for lane in self._live():
             s, self.slots[lane] = self.slots[lane], None
             s["item"]["err"] = e
@@ -183,17 +208,19 @@ class ContinuousScheduler:
                 item["ev"].set()
 
     def _loop(self):
-        Kd = Vd = None
+        Kd, Vd = self._kv0 if self._kv0 is not None else (None, None)
         while True:
             with self.cv:
                 while True:
                     if self._closed:
                         return
                     ready = self._ready()
-                    if ready or self._live() or self._staging is not None:
+                    if self.filling and (ready or any(f.done() for _i, f in self.filling.values())):
                         break
-                    self.cv.wait(timeout=0.05 if self.pending else None)
-                free = [i for i, s in enumerate(self.slots) if s is None]
+                    if (ready and self._free()) or self._live() or self._staging is not None:
+                        break
+                    self.cv.wait(timeout=0.05 if (self.pending or self.filling) else None)
+                free = self._free()
                 n = 0 if self._staging is not None else min(len(free), ready)
                 if self._live() and n < min(self.admit_min, len(free)):
                     n = 0                        # not worth an admission yet
@@ -206,6 +233,14 @@ class ContinuousScheduler:
                 if Kd is None:
                     Kd, Vd = self.eng.blank_kv()
                 tell = getattr(self.eng, "set_live", None)    # TieredDecode
+                if self._start_lane is not None:
+                    # lanes filled elsewhere: start each taken request's fill, seat finished ones
+                    for lane, item in taking:
+                        fut = self._start_lane(item, lane)
+                        fut.add_done_callback(lambda _f: self._wake())
+                        self.filling[lane] = (item, fut)
+                    taking = []
+                    self._collect_filled()
                 if tell is not None:
                     tell(self._live())
                 if self._staging is not None:
@@ -235,7 +270,7 @@ class ContinuousScheduler:
                 if tell is not None:
                     tell(live)
                 cur = [self.slots[i]["cur"] if self.slots[i] else 0 for i in range(self.B)]
-                pos = [self.slots[i]["pos"] if self.slots[i] else 0 for i in range(self.B)]
+                pos = [self.slots[i]["pos"] if self.slots[i] else self.idle_pos for i in range(self.B)]
                 t1 = time.perf_counter()
                 nxt, Kd, Vd = self.eng.step(cur, pos, Kd, Vd)
                 dt = (time.perf_counter() - t1) * 1e3
@@ -258,7 +293,7 @@ class ContinuousScheduler:
                     self._finish(i)
             except Exception as e:   # a bad step fails its own streams; the loop goes on
                 self._fail_all(e, taking)
-                Kd = Vd = None
+                Kd, Vd = self._kv0 if self._kv0 is not None else (None, None)
 
 
 class OneCardProducer:
@@ -289,6 +324,48 @@ class OneCardProducer:
         return _Stage()
 
 
+class NvlinkProducer:
+    """Disaggregated producer inside one process: the prompt is prefilled on one GPU and its
+    cache pushed over NVLink straight into the decode lane the scheduler leased (the reference
+    moves it host-staged through /dev/shm: serving/cluster.py:1329-1334).  Prefills run one at
+    a time on a worker thread, so they overlap the decode steps on the other GPU; the fill ends
+    when the host sees every layer's flag of the lane.  Use with the scheduler's
+    `kv=(Kd, Vd)` (the cache bound here) and `idle_pos=S-1`."""
+
+    def __init__(self, prefill_engine, decode_engine, kv, timeout=10.0):
+        import itertools
+        from rngd_pd.nvlink import NvlinkTransport
+        self.pre, self.timeout = prefill_engine, timeout
+        self.rx = NvlinkTransport(decode_engine.dev)
+        self.rx.bind_cache(*decode_engine.full_kv(*kv))
+        self.tx = NvlinkTransport(prefill_engine.dev)
+        self._peer = self.tx.set_remote_handshake(self.rx.handshake_metadata())
+        self._ids = itertools.count()
+        self._pool = ThreadPoolExecutor(max_workers=1)
+
+    def start_lane(self, item, lane):
+        req = f"pd-{next(self._ids)}"
+        ticket = self.rx.reserve(req, lane, sender_device=self.pre.dev.index)
+        self.tx.add_lease(self._peer, ticket)
+        tokens = item["tokens"]
+
+        def fill():
+            t0 = time.perf_counter()
+            try:
+                kv, nxt = self.pre.prefill_kv_device(tokens)
+                self.tx.push_device(req, kv, stream=self.pre.stream, tokens=len(tokens))
+                self.rx.wait(req, timeout=self.timeout)
+            finally:
+                self.rx.release(req)
+            return None, None, nxt, len(tokens), (time.perf_counter() - t0) * 1e3
+        return self._pool.submit(fill)
+
+    def close(self):
+        self._pool.shutdown(wait=True)
+        self.tx.close()
+        self.rx.close()
+
+
 _ContinuousScheduler = ContinuousScheduler   # the reference's private name
 
-__all__ = ["ContinuousScheduler", "OneCardProducer"]
+__all__ = ["ContinuousScheduler", "OneCardProducer", "NvlinkProducer"]

@@ -153,3 +153,52 @@ def test_prefill_on_gpu0_decode_on_gpu1_equals_one_card():
     assert torch.equal(got, dec1.logits_bv().cpu())
     tx.close()
     rx.close()
+
+
+def test_continuous_batching_with_prefill_on_another_gpu_equals_one_card():
+    """ContinuousScheduler + NvlinkProducer: prompts prefilled on GPU 0 are pushed into the
+    decode lanes leased on GPU 1 while GPU 1 keeps stepping; every request's tokens equal the
+    tokens of prefill and decode both on GPU 1 (the decode step is batch-invariant)."""
+    import threading
+    from oracle import ref_np as R
+    from rngd_pd.engines.decode_batch import BatchDecodeEngine
+    from rngd_pd.engines.model import ModelConfig
+    from rngd_pd.engines.prefill_full import FullPrefillEngine
+    from rngd_pd.serving.scheduler import ContinuousScheduler, NvlinkProducer
+    from rngd_pd.synth import SyntheticState
+    d = R.Dims(H=512, M=1024, NH=8, NKV=2, HD=128, L=2, V=1000)
+    cfg = ModelConfig.from_dims(H=d.H, M=d.M, NH=d.NH, NKV=d.NKV, HD=d.HD, L=d.L, V=d.V, eps=d.eps, theta=d.theta)
+    Sd = 256
+    pf0 = FullPrefillEngine(cfg, SyntheticState(cfg, seed=0), C=128, group=1, S=Sd, chip=0)
+    dec1 = BatchDecodeEngine(cfg, SyntheticState(cfg, seed=0), B=4, S=Sd, group=1, chip=1)
+    pf1 = FullPrefillEngine(cfg, dec1.w, C=128, group=1, S=Sd)
+    reqs = [([(11 * i + 3 * j) % d.V for j in range(4 + 11 * i)], 3 + i % 4) for i in range(9)]
+
+    def alone(tokens, n):
+        K, V, first = pf1.prefill_device(tokens)
+        Kd, Vd = dec1.blank_kv()
+        Kd, Vd = dec1.write_slot_kv(Kd, Vd, 0, K, V)
+        out, cur, pos = [first], first, len(tokens)
+        while len(out) < n:
+            nxt, Kd, Vd = dec1.step([cur, 0, 0, 0], [pos, 0, 0, 0], Kd, Vd)
+            out.append(nxt[0])
+            cur, pos = nxt[0], pos + 1
+        return out
+    want = [alone(t, n) for t, n in reqs]
+    kv = dec1.blank_kv()
+    prod = NvlinkProducer(pf0, dec1, kv)
+    sched = ContinuousScheduler(4, dec1, None, produce_owner=prod, idle_pos=Sd - 1, kv=kv)
+    got = [None] * len(reqs)
+
+    def client(i):
+        got[i] = sched.submit({"tokens": reqs[i][0], "max_new": reqs[i][1]})["tokens"]
+    threads = [threading.Thread(target=client, args=(i,)) for i in range(len(reqs))]
+    try:
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(timeout=120)
+    finally:
+        sched.close()
+        prod.close()
+    assert got == want

@@ -40,7 +40,8 @@ class FakeDecode:
             for g in range(GROUPS):
                 Kd[g][:, b, pos[b] % S] += toks[b] + 1
                 Vd[g][:, b, pos[b] % S] += 2 * toks[b] + 1
-            out.append(int(sum(float(Kd[g][:, b].sum() + Vd[g][:, b].sum()) for g in range(GROUPS))) % VOCAB)
+            out.append(int(sum(float(Kd[g][:, b, :S - 1].sum() + Vd[g][:, b, :S - 1].sum())
+                               for g in range(GROUPS))) % VOCAB)
         return out, Kd, Vd
 
 
@@ -171,3 +172,48 @@ def test_admit_min_holds_lanes_while_streams_run():
     for r, res in zip(reqs, results):
         assert res["tokens"] == _alone(r["tokens"], r["max_new"])
     assert sched.held_lane_steps + sched.starved_lane_steps > 0
+
+
+class LaneFiller:
+    """A producer that fills the lane itself from another thread, like a prefill on another GPU
+    pushing into the leased lane: rows [0, S - 1) only, while the other lanes keep stepping."""
+
+    def __init__(self, kv, fail_every=None):
+        from concurrent.futures import ThreadPoolExecutor
+        self.Kd, self.Vd = kv
+        self.pool = ThreadPoolExecutor(max_workers=2)
+        self.fail_every, self.n = fail_every, 0
+
+    def start_lane(self, item, lane):
+        self.n += 1
+        fail = self.fail_every is not None and self.n % self.fail_every == 0
+
+        def fill():
+            time.sleep(0.002)
+            if fail:
+                raise RuntimeError("injected fill failure")
+            K, V, first = _prefill(item["tokens"])
+            for g in range(GROUPS):
+                self.Kd[g][:, lane, :S - 1] = K[g][:, :S - 1]
+                self.Vd[g][:, lane, :S - 1] = V[g][:, :S - 1]
+            return None, None, first, len(item["tokens"]), 0.0
+        return self.pool.submit(fill)
+
+
+def test_lanes_filled_elsewhere_overlap_the_steps():
+    reqs = _requests(30, seed=3)
+    eng = FakeDecode(6)
+    kv = eng.blank_kv()
+    filler = LaneFiller(kv, fail_every=7)
+    sched = ContinuousScheduler(6, eng, None, produce_owner=filler, idle_pos=S - 1, kv=kv)
+    try:
+        results, _ = _serve(sched, reqs)
+    finally:
+        sched.close()
+    failed = 0
+    for r, res in zip(reqs, results):
+        if isinstance(res, RuntimeError):
+            failed += 1                                  # its own fill failed, nobody else's
+            continue
+        assert res["tokens"] == _alone(r["tokens"], r["max_new"])
+    assert failed == len(reqs) // 7
