@@ -14,10 +14,13 @@
 // are one pass.
 //
 // Completion fence: every CTA fences after its stores and counts itself into its
-// request's counter; the CTA that completes a request's count issues fence.sc.sys
-// and publishes flags[l] = seq for each moved layer with a system-scope release
-// store (the "threadfence reduction" pattern), so a reader that observes the flag
-// with acquire semantics sees all the request's bytes.  The reader's wait is a bounded device loop that reports a
+// request's counter; the CTA that completes a request's count issues one fence.sc.sys
+// and then publishes flags[l] = seq for each moved layer with relaxed system-scope
+// stores (a fence followed by strong writes is a release of each of them; the
+// "threadfence reduction" pattern), so a reader that observes a flag with acquire
+// semantics sees all the request's bytes.  One fence, not a release store per layer:
+// every system-scope release waits for the previous one, and 32 of them in a row cost
+// ~50 us per launch.  The reader's wait is a bounded device loop that reports a
 // status; it never traps or spins forever.
 #include "tc.cuh"
 
@@ -46,9 +49,9 @@ struct XferBatch {
 // and a store, with kXferVec independent loads in flight per thread.
 //
 // Completion: each CTA fences at gpu scope (the counters live on this GPU) and counts itself
-// into its request's counter; the CTA that completes a request fences at system scope and
-// publishes that request's layer flags with a system-scope release, so a reader acquiring a
-// flag sees every byte of the request.
+// into its request's counter; the CTA that completes a request fences once at system scope
+// and then writes that request's layer flags with relaxed system-scope stores, so a reader
+// acquiring a flag sees every byte of the request.
 __global__ void __launch_bounds__(kXferThreads) kv_handoff_kernel(const __grid_constant__ XferBatch b,
                                                                   long src_stride_vec, uint4* __restrict__ dst_k,
                                                                   uint4* __restrict__ dst_v, unsigned head_vec,
@@ -85,7 +88,7 @@ __global__ void __launch_bounds__(kXferThreads) kv_handoff_kernel(const __grid_c
       __threadfence_system();
       long long* f = flags + (long)b.lane[r] * L;
       for (int l = layer0; l < layer1; l++)
-        asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(f + l), "l"(b.seq[r]) : "memory");
+        asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(f + l), "l"(b.seq[r]) : "memory");
       done[r] = 0u;  // ready for the next handoff on this stream
     }
   }
