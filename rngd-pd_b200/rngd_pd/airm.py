@@ -3,6 +3,8 @@
   ShmTransport     the connector's /dev/shm path as an rm-core KVTransport (entry point
                    `airm.kv_transports` name `shm`): host-dram -> host-dram on one machine,
                    bf16/fp16 wire, plan / submit / wait / take (airm.py:137-221).
+  TcpTransport     the cross-node relay path (name `tcp`, airm.py:224-271): host-dram ->
+                   host-dram on any two machines through a TcpKVServer, CRC-checked.
   NvlinkTransport  the new GPU -> GPU path (name `nvlink`): device-hbm -> device-hbm tiers,
                    payload moved by peer-to-peer stores into the decode cache (rngd_pd.nvlink).
 
@@ -154,6 +156,53 @@ class ShmTransport(_KeyedKV, _kv.ShmTransport):
             self._delivered.clear()
         for key in keys:
             self._unlink(key)
+
+
+class TcpTransport(_KeyedKV, _kv.TcpTransport):
+    """KV between two host-memory tiers on any two machines over TCP (airm.py:224-271).
+
+    remote=(host, port) is the relay both sides use (default $AIRM_KV_TCP_ADDR); serve_port=
+    also runs one in this process.  A host-staging path: KV leaves the card, crosses host memory
+    and the network, and is uploaded on the other side.  The relay hands a blob out once, so
+    wait() keeps the bytes it fetched (CRC-checked) for take()."""
+
+    name = "tcp"
+    SCOPE = "only host-dram -> host-dram"
+
+    def __init__(self, remote=None, serve_port=None):
+        _kv.TcpTransport.__init__(self, remote=remote, serve_port=serve_port)
+        self._held = {}
+        self._init_kv()
+
+    def supports(self, src, dst):
+        return src.kind == "host-dram" and dst.kind == "host-dram" and src.name != dst.name
+
+    def _detail(self):
+        return {"server": "%s:%d" % self.remote if self.remote else None}
+
+    def _fetch(self, key, timeout):
+        buf = self.pull(key, timeout=timeout)
+        with self._lock:
+            self._held[key] = buf
+        return buf
+
+    def _consume(self, key):
+        with self._lock:
+            return self._held.pop(key)
+
+    def close(self):
+        with self._lock:
+            self._pending.clear()
+            self._delivered.clear()
+            self._held.clear()
+        _kv.TcpTransport.close(self)
+
+    def conformance_case(self):
+        """Two host tiers and, when no relay is named, one on a free loopback port in this process."""
+        if self.remote is None:
+            _kv.TcpTransport.__init__(self, serve_port=0)
+        return (MemoryTier("tcp-prefill", "host-dram", 1 << 30), MemoryTier("tcp-decode", "host-dram", 1 << 30),
+                KVLayout(num_layers=2, num_kv_heads=2, head_dim=8, dtype="bf16"))
 
 
 class NvlinkTransport(_nv.NvlinkTransport):

@@ -7,7 +7,9 @@ Dual construction exactly as the reference:
 
 The transport is injected, or named ($AIRM_KV_TRANSPORT / kv_transport=) through
 select_transport, or in-process.  Host arrays travel as the reference's wire bytes
-(push/pull, bf16 or fp16).  Device tensors handed to save_kv_layer go through a
+(push/pull, bf16 or fp16); torch tensors on a byte transport (shm, tcp) are staged as the
+same bytes from their own 16-bit values, and registered torch buffers are filled from them
+the same way (a bf16 tensor on the bf16 wire moves as raw bits both ways).  Device tensors handed to save_kv_layer go through a
 transport's device path when it has one (`nvlink`: peer-to-peer stores straight into
 the decode side's leased cache lane), and wait_for_layer_load then waits for that
 layer's completion flag instead of pulling bytes.
@@ -17,7 +19,8 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from rngd_pd.connector.transport import InProcTransport, Transport, deser, select_transport, ser
+from rngd_pd.connector.transport import (InProcTransport, Transport, deser, deser_into, select_transport, ser,
+                                         ser_tensor)
 
 from vllm.distributed.kv_transfer.kv_connector.v1.base import (KVConnectorBase_V1, KVConnectorMetadata,
                                                                KVConnectorRole)
@@ -124,6 +127,9 @@ class RngdKVConnector(KVConnectorBase_V1):
         if _is_device(k) and hasattr(self.t, "push_layer"):
             li = int(layer_name.split(".")[-1])
             self.t.push_layer(self.req_id, li, k.contiguous(), v.contiguous())
+        elif hasattr(k, "detach"):
+            self.t.push(f"{self.req_id}/{layer_name}/k", ser_tensor(k))
+            self.t.push(f"{self.req_id}/{layer_name}/v", ser_tensor(v))
         else:
             self.t.push(f"{self.req_id}/{layer_name}/k", ser(self._host(k)))
             self.t.push(f"{self.req_id}/{layer_name}/v", ser(self._host(v)))
@@ -142,24 +148,27 @@ class RngdKVConnector(KVConnectorBase_V1):
         """Block until this layer's KV is present (rngd_kv.py:139-166).  Device transports:
         wait on the layer's completion flag (the bytes are already in the bound cache lane) and
         return the lane's (k, v) views.  Host transports: pull, decode and write into the
-        registered buffers.  Timeout: $PD_KV_PULL_TIMEOUT (default 5 s) -> TimeoutError."""
+        registered buffers (torch buffers are filled in place by deser_into and returned).
+        Timeout: $PD_KV_PULL_TIMEOUT (default 5 s) -> TimeoutError."""
         t = float(os.environ.get("PD_KV_PULL_TIMEOUT", "5"))
         li = int(layer_name.split(".")[-1])
         if hasattr(self.t, "lane_views") and getattr(self.t, "_cache", None) is not None:
             self.t.wait(self.req_id, layer0=li, layer1=li + 1, timeout=t)
             K, V = self.t.lane_views(self.req_id)
             return K[li], V[li]
-        k = deser(self.t.pull(f"{self.req_id}/{layer_name}/k", timeout=t))
-        v = deser(self.t.pull(f"{self.req_id}/{layer_name}/v", timeout=t))
-        if self._kv_caches is not None:
-            if isinstance(self._kv_caches, dict):
-                dst = self._kv_caches.get(layer_name)
-                if dst is not None:
-                    dst[0][:] = k
-                    dst[1][:] = v
-            else:
-                self._kv_caches[0][li][:] = k
-                self._kv_caches[1][li][:] = v
+        kb = self.t.pull(f"{self.req_id}/{layer_name}/k", timeout=t)
+        vb = self.t.pull(f"{self.req_id}/{layer_name}/v", timeout=t)
+        dst = None
+        if isinstance(self._kv_caches, dict):
+            dst = self._kv_caches.get(layer_name)
+        elif self._kv_caches is not None:
+            dst = (self._kv_caches[0][li], self._kv_caches[1][li])
+        if dst is not None and hasattr(dst[0], "detach"):
+            return deser_into(kb, dst[0]), deser_into(vb, dst[1])
+        k, v = deser(kb), deser(vb)
+        if dst is not None:
+            dst[0][:] = k
+            dst[1][:] = v
         return k, v
 
     def get_finished(self, finished_req_ids):

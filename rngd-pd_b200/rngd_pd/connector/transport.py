@@ -6,12 +6,15 @@ One interface, swappable backends, chosen by name:
     + the NIXL-parity handshake hooks handshake_metadata() / set_remote_handshake()
     ├─ InProcTransport   in-process dict (tests, single process)
     ├─ ShmTransport      /dev/shm files, atomic publish (cross-process, same host)
+    ├─ TcpTransport      a TcpKVServer relay (rngd_pd.connector.tcpkv): cross-node, host-staged
     └─ NvlinkTransport   GPU -> GPU peer-to-peer stores over NVLink (rngd_pd.nvlink),
                          registered as `nvlink`; moves device KV with push_device()
 
 `ser` / `deser` are byte-compatible with the reference's wire (fp16 default, `bf16` =
 fp32 bits >> 16), so pods on the reference's code and on this build interoperate over
-the same shm directory.  `select_transport(name)` resolves a name through rm-core's
+the same shm directory or TCP relay.  `ser_tensor` / `deser_into` give the same bytes
+straight from and into torch tensors: a bf16 tensor on the bf16 wire crosses the bus as its
+raw bits, with no fp32 pass on the host.  `select_transport(name)` resolves a name through rm-core's
 `airm.kv_transports` entry points when rm-core is installed, else through this
 package's own table; an unknown name raises KeyError, never a fallback.
 """
@@ -43,6 +46,55 @@ def deser(buf):
     if isinstance(o, dict) and "bf16" in o:
         return (o["bf16"].astype(np.uint32) << 16).view(np.float32).reshape(o["shape"])
     return o.astype(np.float32)
+
+
+def _host_view(t):
+    """A contiguous torch tensor -> a numpy view of it in host memory (device tensors are copied
+    into a pinned buffer first)."""
+    import torch
+    if t.is_cuda:
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t)
+        return h.numpy()
+    return t.numpy()
+
+
+def ser_tensor(t, wire=None):
+    """A torch tensor (any device) -> the bytes ser(t.float().numpy(), wire) gives.  On the bf16
+    wire a bf16 tensor is staged as its raw bits (2 bytes per element cross the bus); on the fp16
+    wire the device converts (round to nearest even, as numpy's astype does from the exact fp32
+    value); other cases go through ser()."""
+    import torch
+    w = wire or WIRE
+    t = t.detach()
+    if w == "bf16" and t.dtype == torch.bfloat16:
+        bits = _host_view(t.contiguous().view(torch.int16)).view(np.uint16)
+        return pickle.dumps({"bf16": bits, "shape": tuple(int(d) for d in t.shape)}, protocol=4)
+    if w != "bf16" and t.dtype in (torch.bfloat16, torch.float16, torch.float32):
+        return pickle.dumps(_host_view(t.contiguous().to(torch.float16)), protocol=4)
+    return ser(t.float().cpu().numpy(), wire=w)
+
+
+def deser_into(buf, dst):
+    """Wire bytes -> dst (a torch tensor, any device) in place; returns dst.  bf16 wire bytes into
+    a bf16 tensor are copied as raw bits; everything else goes through deser()'s float32 values.
+    ValueError if the element counts differ."""
+    import torch
+    o = pickle.loads(buf)
+    if isinstance(o, dict) and "bf16" in o:
+        bits = np.ascontiguousarray(o["bf16"]).reshape(-1)
+        if bits.size != dst.numel():
+            raise ValueError(f"wire holds {bits.size} elements, destination {tuple(dst.shape)}")
+        if dst.dtype == torch.bfloat16:
+            dst.view(torch.int16).copy_(torch.from_numpy(bits.view(np.int16)).view(dst.shape))
+            return dst
+        vals = (bits.astype(np.uint32) << 16).view(np.float32)
+    else:
+        vals = np.ascontiguousarray(o, dtype=np.float32).reshape(-1)
+        if vals.size != dst.numel():
+            raise ValueError(f"wire holds {vals.size} elements, destination {tuple(dst.shape)}")
+    dst.copy_(torch.from_numpy(vals).view(dst.shape))
+    return dst
 
 
 class Transport(ABC):
@@ -121,6 +173,71 @@ class ShmTransport(Transport):
             return f.read()
 
 
+class TcpTransport(Transport):
+    """Cross-node KV through one TcpKVServer relay (connector/transport.py:104-154).
+
+    remote=(host, port) names the relay, default $AIRM_KV_TCP_ADDR ("host:port"); serve_port=
+    also runs a relay in this process (0 = any free port), which is then the default remote.
+    Prefill and decode name the same relay, beside the decode worker or on a third node.  The
+    client pools persistent connections and every blob carries a CRC-32 checked by the relay and
+    the taker, so a pull returns the pushed bytes or raises.  select_transport("tcp") gives one
+    instance per process (`shared`).  AIRM_KV_TCP_LOG=1 prints one line per blob (key, bytes,
+    sha256 prefix, ms) for byte-exact audits."""
+    shared = True
+
+    def __init__(self, remote=None, serve_port=None):
+        from rngd_pd.connector.tcpkv import TcpKVClient, TcpKVServer, parse_addr
+        self.server = None
+        if serve_port is not None:
+            self.server = TcpKVServer(serve_port)
+            self.server.start()
+            serve_port = self.server.wait_ready()
+        if remote is None:
+            env = os.environ.get("AIRM_KV_TCP_ADDR")
+            if env:
+                remote = parse_addr(env)
+            elif serve_port is not None:
+                remote = ("127.0.0.1", serve_port)
+        self.remote = (remote[0], int(remote[1])) if remote else None
+        self._client = TcpKVClient(*self.remote) if self.remote else None
+
+    def _relay(self):
+        if self._client is None:
+            raise ValueError("tcp transport needs remote=(host, port) or AIRM_KV_TCP_ADDR=host:port")
+        return self._client
+
+    def push(self, key, buf):
+        t0 = time.perf_counter()
+        self._relay().push(key, buf)
+        self._audit("push", key, buf, t0)
+
+    def pull(self, key, timeout=5.0):
+        t0 = time.perf_counter()
+        buf = self._relay().take(key, timeout=timeout)     # the relay waits for the key: no polling
+        self._audit("pull", key, buf, t0)
+        return buf
+
+    @staticmethod
+    def _audit(op, key, buf, t0):
+        if os.environ.get("AIRM_KV_TCP_LOG", "0") in ("0", ""):
+            return
+        import hashlib
+        import sys
+        line = (f"[kv-tcp] {op} {key} {memoryview(buf).nbytes} {hashlib.sha256(buf).hexdigest()[:16]} "
+                f"{(time.perf_counter() - t0) * 1e3:.2f}ms\n")
+        sys.stdout.write(line)      # one write per line: several threads may log
+        sys.stdout.flush()
+
+    def handshake_metadata(self):
+        return {"tcp": "%s:%d" % self.remote} if self.remote else {}
+
+    def close(self):
+        if self._client is not None:
+            self._client.close()
+        if self.server is not None:
+            self.server.stop()
+
+
 class FencedTransport(Transport):
     """Connector Transport over an rm-core tier-to-tier KVTransport (connector/transport.py:238-289):
     push() plans and submits one transfer per key; pull() waits on that transfer's completion
@@ -176,10 +293,10 @@ class FencedTransport(Transport):
 
 
 # This package's own adapters, used when rm-core's registry is not installed or does not
-# know the name.  The reference's tcp / nixl / nixl-ucx transports are host-staging paths
-# outside this build; they resolve only through rm-core's registry when installed.
-_OWN = {"shm": "rngd_pd.airm:ShmTransport", "nvlink": "rngd_pd.airm:NvlinkTransport",
-        "inproc": "rngd_pd.connector.transport:InProcTransport"}
+# know the name.  The reference's nixl / nixl-ucx transports (RDMA through NIXL, absent here)
+# resolve only through rm-core's registry when installed.
+_OWN = {"shm": "rngd_pd.airm:ShmTransport", "tcp": "rngd_pd.airm:TcpTransport",
+        "nvlink": "rngd_pd.airm:NvlinkTransport", "inproc": "rngd_pd.connector.transport:InProcTransport"}
 _CLASSES = {}
 _FENCED = {}
 _SHARED = {}
@@ -239,12 +356,14 @@ def select_transport(name=None, **kw) -> Transport:
 
 
 def make_transport(backend="shm", **kw) -> Transport:
-    """Factory (connector/transport.py:353-361): backend in {inproc, shm, nvlink}."""
+    """Factory (connector/transport.py:353-361): backend in {inproc, shm, tcp, nvlink}."""
     b = backend.lower()
     if b == "inproc":
         return InProcTransport()
     if b == "shm":
         return ShmTransport(**kw)
+    if b == "tcp":
+        return TcpTransport(**kw)
     if b == "nvlink":
         from rngd_pd.nvlink import NvlinkTransport
         return NvlinkTransport(**kw)
