@@ -625,8 +625,9 @@ def run_micro_step_small(args):
 
 def run_micro_serve(args, pd=False):
     """Continuous batching (serving/scheduler.py over BatchDecodeEngine B=16): a seeded Poisson
-    trace in the shape of BASELINE config 5 (prompts U[128, 448] tokens, 64 output tokens each)
-    submitted by one client thread per request at its arrival time.  One card (pd=False): a
+    trace in the shape of the end-to-end PD configuration (prompts U[128, 448] tokens, 64 output
+    tokens each) sent through the in-process Gateway by one client thread per request at its
+    arrival time; the line carries the gateway Window's airm summary too.  One card (pd=False): a
     FullPrefillEngine on the decode engine's weights, prompts admitted between steps.  PD on two
     GPUs of one process (pd=True): prefill on GPU 0 pushes each prompt's cache over NVLink into
     the decode lane leased on GPU 1 while GPU 1 keeps stepping.  Box tok/s = output tokens /
@@ -640,6 +641,7 @@ def run_micro_serve(args, pd=False):
     from rngd_pd.engines.model import ModelConfig
     from rngd_pd.engines.prefill_full import FullPrefillEngine
     from rngd_pd import _lib
+    from rngd_pd.serving.gateway import Gateway
     from rngd_pd.serving.scheduler import ContinuousScheduler, NvlinkProducer, OneCardProducer
     cfg = ModelConfig.llama31_8b()
     if pd:
@@ -674,6 +676,7 @@ def run_micro_serve(args, pd=False):
     # warm-up outside the trace: every prefill bucket and the captured step
     for P in (200, 400):
         sched.submit({"tokens": [1] * P, "max_new": 4})
+    gw = Gateway({"llama-3.1-8b": sched}, S=S)      # requests enter as the reference's gateway takes them
     ttft, tpot, done_at, errors = [None] * n_req, [None] * n_req, [None] * n_req, []
     t_start = time.perf_counter() + 0.2
 
@@ -681,12 +684,11 @@ def run_micro_serve(args, pd=False):
         t_arr = t_start + arrivals[i]
         time.sleep(max(0.0, t_arr - time.perf_counter()))
         first = []
-        item = {"tokens": prompts[i][:S - out_tok], "max_new": out_tok,
-                "on_token": lambda t: first.append(time.perf_counter()) if not first else None}
+        body = {"model": "llama-3.1-8b", "tokens": prompts[i], "max_tokens": out_tok}
         try:
-            out = sched.submit(item)
+            resp = gw.complete(body, on_token=lambda t: first.append(time.perf_counter()) if not first else None)
             ttft[i] = (first[0] - t_arr) * 1e3
-            tpot[i] = out["tpot_ms"]
+            tpot[i] = resp["pd"]["tpot_ms"]
             done_at[i] = time.perf_counter()
         except Exception as e:   # noqa: BLE001 - reported
             errors.append(repr(e))
@@ -711,7 +713,8 @@ def run_micro_serve(args, pd=False):
                       "ttft_ms_p50": pct(ttft, 50), "ttft_ms_p90": pct(ttft, 90),
                       "tpot_ms_p50": pct(tpot, 50), "tpot_ms_p90": pct(tpot, 90),
                       "occupancy": sched.occupancy(), "steps": sched.steps, "admissions": sched.admits,
-                      "staged_steps": sched.stage_steps, "status": _lib.device_status()}), flush=True)
+                      "staged_steps": sched.stage_steps, "airm": gw.window.summary(),
+                      "status": _lib.device_status()}), flush=True)
 
 
 def run_micro(args):

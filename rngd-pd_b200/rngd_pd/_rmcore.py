@@ -84,9 +84,13 @@ class TransferResult:
     error: str = None
 
 
-# name -> (unit, direction, help), the subset of rm-core's METRICS the transports emit
+# name -> (unit, direction, help), the subset of rm-core's METRICS this package emits: the
+# transports' per-transfer figures and the serving summary (rngd_pd.airm.summarize)
 METRICS = {"kv_transfer_ms": ("ms", "lower", "KV handoff time per transfer"),
-           "kv_transfer_gbps": ("GB/s", "higher", "KV handoff payload bandwidth")}
+           "kv_transfer_gbps": ("GB/s", "higher", "KV handoff payload bandwidth"),
+           "ttft_p90_ms": ("ms", "lower", "time to first token, 90th percentile"),
+           "tpot_p90_ms": ("ms", "lower", "time per output token after the first, 90th percentile"),
+           "tok_s": ("tok/s", "higher", "generated tokens per second over the window")}
 
 
 @dataclass

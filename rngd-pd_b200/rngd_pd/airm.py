@@ -9,9 +9,12 @@
                    payload moved by peer-to-peer stores into the decode cache (rngd_pd.nvlink).
 
 rm-core's protocol types come from `rm_core` when it is installed, else from
-rngd_pd._rmcore (a restatement of the same names).  The workload runner and the Prometheus
-metrics of the reference module are outside this build; both transports record rm-core's
-`kv_transfer_ms` (and nvlink also `kv_transfer_gbps`) measurements.
+rngd_pd._rmcore (a restatement of the same names).  The transports record rm-core's
+`kv_transfer_ms` (nvlink also `kv_transfer_gbps`) measurements.  The serving metrics of the
+reference module (airm.py:393-507) are here too: `summarize` turns per-request records into
+rm-core-named figures (ttft_p90_ms, tpot_p90_ms, tok_s, kv_transfer_ms), `Window` keeps the
+last requests a gateway served, and `serve_metrics` exposes them as airm_* gauges over HTTP.
+The workload runner (airm.py:223-391, process launch) is outside this build.
 """
 import collections
 import os
@@ -23,10 +26,11 @@ import numpy as np
 
 try:  # pragma: no cover - depends on the host
     from rm_core import (ContractError, KVLayout, Measurement, MemoryTier, TransferHandle, TransferPlan,
-                         TransferResult, TransportError)
+                         TransferResult, TransportError, prometheus_name)
+    from rm_core.metrics import METRICS
 except ImportError:
-    from rngd_pd._rmcore import (ContractError, KVLayout, Measurement, MemoryTier, TransferHandle, TransferPlan,
-                                 TransferResult, TransportError)
+    from rngd_pd._rmcore import (METRICS, ContractError, KVLayout, Measurement, MemoryTier, TransferHandle,
+                                 TransferPlan, TransferResult, TransportError, prometheus_name)
 
 from rngd_pd import nvlink as _nv
 from rngd_pd.connector import transport as _kv
@@ -287,3 +291,131 @@ def summarize_transfers(measurements):
         if vals:
             out[name] = float(np.median(vals))
     return out
+
+
+# ------------------------------------------------------------------ serving metrics
+def _pct(vals, q):
+    vals = [float(v) for v in vals if v is not None]
+    return round(float(np.percentile(vals, q)), 1) if vals else None
+
+
+def summarize(records, wall_s=None):
+    """rm-core-named summary of per-request records (airm.py:400-422).
+
+    A record holds ttft_ms, tpot_ms, out_tokens and, when the KV crossed between cards,
+    kv_save_ms / kv_load_ms.  Records with an "error" are left out.  tok_s divides the
+    generated tokens by wall_s, else by the span from the first start (t0) to the last end
+    (t1); kv_transfer_ms is the median per-request handoff (save + load).  Figures without
+    data are omitted."""
+    recs = [r for r in records if r and "error" not in r]
+    if not recs:
+        return {}
+    if wall_s is None and all("t0" in r and "t1" in r for r in recs):
+        wall_s = max(r["t1"] for r in recs) - min(r["t0"] for r in recs)
+    xfer = [(r.get("kv_save_ms") or 0.0) + (r.get("kv_load_ms") or 0.0) for r in recs
+            if r.get("kv_save_ms") is not None or r.get("kv_load_ms") is not None]
+    tokens = sum(r.get("out_tokens") or 0 for r in recs)
+    out = {"ttft_p90_ms": _pct([r.get("ttft_ms") for r in recs], 90),
+           "tpot_p90_ms": _pct([r.get("tpot_ms") for r in recs], 90),
+           "tok_s": round(tokens / wall_s, 1) if wall_s else None,
+           "kv_transfer_ms": _pct(xfer, 50)}
+    return {k: v for k, v in out.items() if v is not None}
+
+
+def measurements(summary, **tags):
+    """Validated rm-core Measurements of a summarize() result (airm.py:425-432); the
+    kv_transport tag stays on kv_transfer_ms only."""
+    base = dict({"component": COMPONENT}, **tags)
+    out = []
+    for name, value in summary.items():
+        t = dict(base)
+        if name != "kv_transfer_ms":
+            t.pop("kv_transport", None)
+        out.append(Measurement(name, float(value), t).validate())
+    return out
+
+
+def prometheus_text(ms):
+    """Prometheus exposition of measurements as gauges (airm.py:435-445)."""
+    lines, typed = [], set()
+    for m in ms:
+        series = prometheus_name(m.name)
+        if series not in typed:
+            lines.append(f"# HELP {series} {METRICS[m.name][2]} ({m.unit})")
+            lines.append(f"# TYPE {series} gauge")
+            typed.add(series)
+        labels = ",".join(f'{k}="{v}"' for k, v in sorted(m.tags.items()))
+        lines.append(f"{series}{{{labels}}} {m.value:g}")
+    return "\n".join(lines) + "\n"
+
+
+class Window:
+    """The last `size` requests a gateway served, as airm_* gauges (airm.py:448-485).
+
+    TPOT is what a client sees, (wall - TTFT) / (tokens - 1), not the decode loop's median
+    step: the wait for a lane and admission stalls count, so the gauge rises when the decode
+    side saturates."""
+
+    def __init__(self, size=512):
+        self.recs = collections.deque(maxlen=size)
+        self.lock = threading.Lock()
+
+    def record(self, t0, t1, resp):
+        pd = resp.get("pd", {}) if isinstance(resp, dict) else {}
+        n = (resp.get("usage") or {}).get("completion_tokens", 0) if isinstance(resp, dict) else 0
+        ttft = pd.get("ttft_ms")
+        wall = (t1 - t0) * 1e3
+        if isinstance(ttft, (int, float)) and n and n > 1:
+            tpot = max(0.0, wall - ttft) / (n - 1)
+        else:
+            tpot = pd.get("tpot_ms")
+        rec = {"t0": t0, "t1": t1, "ttft_ms": ttft, "tpot_ms": tpot, "out_tokens": n}
+        if pd.get("mode") == "disaggregated-kv-transfer":
+            rec.update(kv_save_ms=pd.get("kv_save_ms"), kv_load_ms=pd.get("kv_load_ms"))
+        with self.lock:
+            self.recs.append(rec)
+
+    def observe(self, fn):
+        """Wrap a route so every completed request is recorded."""
+        def wrapped(body):
+            t0 = time.perf_counter()
+            resp = fn(body)
+            self.record(t0, time.perf_counter(), resp)
+            return resp
+        return wrapped
+
+    def summary(self):
+        with self.lock:
+            recs = list(self.recs)
+        return summarize(recs)
+
+    def text(self, kv_transport=None):
+        kv = kv_transport or os.environ.get("AIRM_KV_TRANSPORT") or "shm"
+        return prometheus_text(measurements(self.summary(), kv_transport=kv))
+
+
+def serve_metrics(window, port, host="0.0.0.0"):
+    """airm_* gauges of `window` on http://host:port/metrics from a daemon thread
+    (airm.py:488-507); returns the server (server_address has the bound port)."""
+    from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
+
+    class _Metrics(BaseHTTPRequestHandler):
+        def log_message(self, *a):
+            pass
+
+        def do_GET(self):
+            if self.path.rstrip("/") != "/metrics":
+                self.send_response(404)
+                self.end_headers()
+                return
+            body = window.text().encode()
+            self.send_response(200)
+            self.send_header("Content-Type", "text/plain; version=0.0.4")
+            self.send_header("Content-Length", str(len(body)))
+            self.end_headers()
+            self.wfile.write(body)
+
+    srv = ThreadingHTTPServer((host, port), _Metrics)
+    srv.daemon_threads = True
+    threading.Thread(target=srv.serve_forever, daemon=True).start()
+    return srv

@@ -353,11 +353,18 @@ class NvlinkProducer:
             t0 = time.perf_counter()
             try:
                 kv, nxt = self.pre.prefill_kv_device(tokens)
-                self.tx.push_device(req, kv, stream=self.pre.stream, tokens=len(tokens))
+                t1 = time.perf_counter()
+                moved = self.tx.push_device(req, kv, stream=self.pre.stream, tokens=len(tokens))
+                t2 = time.perf_counter()
                 self.rx.wait(req, timeout=self.timeout)
+                t3 = time.perf_counter()
             finally:
                 self.rx.release(req)
-            return None, None, nxt, len(tokens), (time.perf_counter() - t0) * 1e3
+            # the request's transfer record (the reference's pd fields): prefill, the push's
+            # launch, and the wait until every layer flag of the lane was seen
+            item["_xfer"] = {"prefill_ms": round((t1 - t0) * 1e3, 2), "kv_save_ms": round((t2 - t1) * 1e3, 3),
+                             "kv_load_ms": round((t3 - t2) * 1e3, 3), "kv_mb": round(moved / 1e6, 2)}
+            return None, None, nxt, len(tokens), (t3 - t0) * 1e3
         return self._pool.submit(fill)
 
     def close(self):
