@@ -298,7 +298,9 @@ class BatchDecodeEngine:
                 # run leaves no trace.
                 self._launch(Kd, Vd, s)
                 g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=s):
+                # thread_local: a CUDA call made meanwhile by another thread (a producer copying
+                # flags or allocating on another GPU) is legal and does not void this capture
+                with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
                     self._launch(Kd, Vd, s)
                 self._graphs[key] = g
                 # the step ends by advancing toks/pos on the device (for step_device):

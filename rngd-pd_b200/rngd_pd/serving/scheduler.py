@@ -21,7 +21,9 @@ a prefill on another GPU pushing into the reserved lane over NVLink) gets a free
 request is taken; the lane stays out of the batch while it fills, the other lanes keep
 stepping, and the stream is seated when the future completes.  Lanes without a stream step at
 position `idle_pos`: pass S - 1 when lanes fill asynchronously, so the appends of idle lanes
-stay clear of the rows a push is writing (a prompt never reaches the last row).
+stay clear of the rows a push is writing (a prompt never reaches the last row).  Given such a
+fixed cache (`kv=`), the constructor runs one all-idle step on it, so the step's CUDA graph is
+captured before any producer thread starts.
 
 Items are dicts: "tokens" (the prompt) and "max_new" (tokens to return, the prefill's next
 token included), optionally "on_token" (called with each token as it is produced; it must
@@ -71,6 +73,10 @@ class ContinuousScheduler:
         self.starved_lane_steps = self.held_lane_steps = 0
         self.admits, self.admit_ms, self.admit_stall_ms = 0, 0.0, 0.0
         self.stage_steps = 0
+        if kv is not None:
+            # a fixed cache: run (and so capture) its first decode step now, before any producer
+            # thread exists, with every lane idle at idle_pos (rows no stream reads)
+            engine.step([0] * B, [self.idle_pos] * B, *kv)
         self._thread = threading.Thread(target=self._loop, daemon=True)
         self._thread.start()
 
