@@ -623,6 +623,75 @@ def run_micro_step_small(args):
                       "status": _lib.device_status()}), flush=True)
 
 
+def run_micro_serve_box(args):
+    """The end-to-end PD box in one process over every visible GPU (serving/pd.py build_pd):
+    P prefill GPUs push each prompt's cache over NVLink into the lanes of D decode GPUs, each a
+    continuous-batching scheduler (B=16, S=512) behind one gateway.  SERVE_SPLIT picks the split
+    ("2P:6D"; default half and half, i.e. 1P:1D pairs), SERVE_N the requests (default 512),
+    SERVE_RATE the Poisson arrival rate (default 40 req/s per decode GPU).  Prompts U[128, 448]
+    tokens, 64 output tokens, seeded.  Box tok/s = output tokens / (last completion - first
+    arrival); TTFT = arrival -> first token; TPOT = a request's median decode step."""
+    import threading
+    import numpy as np
+    import torch
+    from rngd_pd import _lib, synth
+    from rngd_pd.engines.model import ModelConfig
+    from rngd_pd.serving.pd import build_pd, parse_split
+    n = torch.cuda.device_count()
+    split = parse_split(os.environ["SERVE_SPLIT"]) if os.environ.get("SERVE_SPLIT") else (n // 2, n - n // 2)
+    if n < 2 or split[0] + split[1] > n:
+        print(json.dumps({"micro": "serve_box", "unavailable": f"split {split} needs more than the {n} GPUs visible"}),
+              flush=True)
+        return
+    cfg = ModelConfig.llama31_8b()
+    box = build_pd(cfg, synth.SyntheticState(cfg, seed=0), split=split, B=B, S=S)
+    out_tok = 64
+    rate = float(os.environ.get("SERVE_RATE", str(40.0 * split[1])))
+    n_req = int(os.environ.get("SERVE_N", "512"))
+    rng = np.random.default_rng(5)
+    arrivals = np.cumsum(rng.exponential(1.0 / rate, n_req))
+    prompts = [rng.integers(0, cfg.vocab, int(rng.integers(128, 449))).tolist() for _ in range(n_req)]
+    for P in (200, 400):                    # warm-up outside the trace: both buckets on every pairing
+        for _ in range(max(split)):
+            box.gateway.complete({"tokens": [1] * P, "max_tokens": 4})
+    box.gateway.window.recs.clear()
+    ttft, tpot, done_at, errors = [None] * n_req, [None] * n_req, [None] * n_req, []
+    t_start = time.perf_counter() + 0.2
+
+    def client(i):
+        t_arr = t_start + arrivals[i]
+        time.sleep(max(0.0, t_arr - time.perf_counter()))
+        first = []
+        try:
+            resp = box.gateway.complete({"tokens": prompts[i], "max_tokens": out_tok},
+                                        on_token=lambda t: first.append(time.perf_counter()) if not first else None)
+            ttft[i] = (first[0] - t_arr) * 1e3
+            tpot[i] = resp["pd"]["tpot_ms"]
+            done_at[i] = time.perf_counter()
+        except Exception as e:   # noqa: BLE001 - reported
+            errors.append(repr(e))
+    threads = [threading.Thread(target=client, args=(i,)) for i in range(n_req)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    occ = box.occupancy()
+    box.close()
+    ok = [i for i in range(n_req) if done_at[i] is not None]
+    span = max(done_at[i] for i in ok) - (t_start + arrivals[0]) if ok else float("nan")
+    pct = lambda v, q: float(np.percentile([x for x in v if x is not None], q)) if ok else None
+    print(json.dumps({"micro": "serve_box", "split": f"{split[0]}P:{split[1]}D", "gpus": n,
+                      "workload": "PD box in one process: prefill GPUs -> NVLink -> decode lanes, continuous "
+                                  "batching B=16, S=512, seeded Poisson trace, prompts U[128,448], 64 output "
+                                  "tokens, Llama-3.1-8B shape",
+                      "rate_req_s": rate, "requests": n_req, "completed": len(ok), "errors": errors[:3],
+                      "box_tok_s": len(ok) * out_tok / span if ok else 0.0, "span_s": span,
+                      "ttft_ms_p50": pct(ttft, 50), "ttft_ms_p90": pct(ttft, 90),
+                      "tpot_ms_p50": pct(tpot, 50), "tpot_ms_p90": pct(tpot, 90),
+                      "decode_occupancy": occ, "airm": box.gateway.window.summary(),
+                      "status": _lib.device_status()}), flush=True)
+
+
 def run_micro_serve(args, pd=False):
     """Continuous batching (serving/scheduler.py over BatchDecodeEngine B=16): a seeded Poisson
     trace in the shape of the end-to-end PD configuration (prompts U[128, 448] tokens, 64 output
@@ -727,6 +796,8 @@ def run_micro(args):
         return run_micro_step_small(args)
     if args.micro in ("serve", "serve_pd"):
         return run_micro_serve(args, pd=args.micro == "serve_pd")
+    if args.micro == "serve_box":
+        return run_micro_serve_box(args)
     if args.micro == "handoff":
         return run_micro_handoff(args)
     if args.micro in ("prefill", "prefill_small"):
@@ -941,7 +1012,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["gate_up", "qkv", "o", "down", "lm", "attn", "pf_gate_up", "pf_qkv", "pf_o",
                                         "pf_down", "handoff", "prefill", "prefill_small", "step_small", "serve",
-                                        "serve_pd"],
+                                        "serve_pd", "serve_box"],
                     help="time one decode GEMM shape alone (small footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:

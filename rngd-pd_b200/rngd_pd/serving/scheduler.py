@@ -330,55 +330,109 @@ class OneCardProducer:
         return _Stage()
 
 
+class PrefillPool:
+    """Prefill engines (one per GPU) shared by several producers, e.g. 2 prefill GPUs feeding 6
+    decode GPUs (the reference's gateway round-robins prefill pods: serving/cluster.py:1490-1501).
+    A prompt takes the engine with the fewest prompts holding or waiting for it (ties go
+    round-robin) and holds it from its prefill to the launch of its push, so an engine's
+    output is never overwritten before the push that reads it is queued behind it."""
+
+    def __init__(self, engines):
+        import itertools
+        self.engines = list(engines)
+        if not self.engines:
+            raise ValueError("prefill pool needs at least one engine")
+        self._busy = [0] * len(self.engines)
+        self._locks = [threading.Lock() for _ in self.engines]
+        self._mu = threading.Lock()
+        self._rr = itertools.count()
+
+    def take(self):
+        """Context manager: the chosen engine, held exclusively inside the block."""
+        import contextlib
+        n = len(self.engines)
+        with self._mu:
+            first = next(self._rr) % n
+            i = min(range(n), key=lambda j: (self._busy[j], (j - first) % n))
+            self._busy[i] += 1
+
+        @contextlib.contextmanager
+        def held():
+            try:
+                with self._locks[i]:
+                    yield self.engines[i]
+            finally:
+                with self._mu:
+                    self._busy[i] -= 1
+        return held()
+
+
 class NvlinkProducer:
     """Disaggregated producer inside one process: the prompt is prefilled on one GPU and its
     cache pushed over NVLink straight into the decode lane the scheduler leased (the reference
-    moves it host-staged through /dev/shm: serving/cluster.py:1329-1334).  Prefills run one at
-    a time on a worker thread, so they overlap the decode steps on the other GPU; the fill ends
-    when the host sees every layer's flag of the lane.  Use with the scheduler's
-    `kv=(Kd, Vd)` (the cache bound here) and `idle_pos=S-1`."""
+    moves it host-staged through /dev/shm: serving/cluster.py:1329-1334).  Prefills run on
+    worker threads (one per prefill engine), so they overlap the decode steps on the other GPU;
+    the fill ends when the host sees every layer's flag of the lane.  `prefill_engine` is one
+    engine or a PrefillPool shared with other producers.  Use with the scheduler's
+    `kv=(Kd, Vd)` (the cache bound here) and `idle_pos=S-1`.  `transport` builds the
+    transports (NvlinkTransport; a test passes a fake)."""
 
-    def __init__(self, prefill_engine, decode_engine, kv, timeout=10.0):
+    def __init__(self, prefill_engine, decode_engine, kv, timeout=10.0, transport=None):
         import itertools
-        from rngd_pd.nvlink import NvlinkTransport
-        self.pre, self.timeout = prefill_engine, timeout
-        self.rx = NvlinkTransport(decode_engine.dev)
+        if transport is None:
+            from rngd_pd.nvlink import NvlinkTransport as transport
+        self.pool = prefill_engine if isinstance(prefill_engine, PrefillPool) else PrefillPool([prefill_engine])
+        self.pre, self.timeout = self.pool.engines[0], timeout
+        self.rx = transport(decode_engine.dev)
         self.rx.bind_cache(*decode_engine.full_kv(*kv))
-        self.tx = NvlinkTransport(prefill_engine.dev)
-        self._peer = self.tx.set_remote_handshake(self.rx.handshake_metadata())
+        self._tx = {}                    # prefill GPU -> (its sending transport, the receiver's key)
+        for e in self.pool.engines:
+            d = e.dev.index
+            if d not in self._tx:
+                tx = transport(e.dev)
+                self._tx[d] = (tx, tx.set_remote_handshake(self.rx.handshake_metadata()))
         self._ids = itertools.count()
-        self._pool = ThreadPoolExecutor(max_workers=1)
+        self._pool = ThreadPoolExecutor(max_workers=len(self.pool.engines))
 
     def start_lane(self, item, lane):
         req = f"pd-{next(self._ids)}"
-        ticket = self.rx.reserve(req, lane, sender_device=self.pre.dev.index)
-        self.tx.add_lease(self._peer, ticket)
         tokens = item["tokens"]
 
         def fill():
             t0 = time.perf_counter()
+            leased = False
             try:
-                kv, nxt = self.pre.prefill_kv_device(tokens)
-                t1 = time.perf_counter()
-                moved = self.tx.push_device(req, kv, stream=self.pre.stream, tokens=len(tokens))
-                t2 = time.perf_counter()
+                with self.pool.take() as pre:
+                    tq = time.perf_counter()
+                    d = pre.dev.index
+                    tx, peer = self._tx[d]
+                    tx.add_lease(peer, self.rx.reserve(req, lane, sender_device=d))
+                    leased = True
+                    kv, nxt = pre.prefill_kv_device(tokens)
+                    t1 = time.perf_counter()
+                    moved = tx.push_device(req, kv, stream=pre.stream, tokens=len(tokens))
+                    t2 = time.perf_counter()
                 self.rx.wait(req, timeout=self.timeout)
                 t3 = time.perf_counter()
             finally:
-                self.rx.release(req)
+                if leased:
+                    self.rx.release(req)
             # the request's transfer record (the reference's pd fields): prefill, the push's
-            # launch, and the wait until every layer flag of the lane was seen
-            item["_xfer"] = {"prefill_ms": round((t1 - t0) * 1e3, 2), "kv_save_ms": round((t2 - t1) * 1e3, 3),
-                             "kv_load_ms": round((t3 - t2) * 1e3, 3), "kv_mb": round(moved / 1e6, 2)}
+            # launch, and the wait until every layer flag of the lane was seen; queue_ms is the
+            # wait for a prefill engine
+            item["_xfer"] = {"prefill_ms": round((t1 - tq) * 1e3, 2), "kv_save_ms": round((t2 - t1) * 1e3, 3),
+                             "kv_load_ms": round((t3 - t2) * 1e3, 3), "kv_mb": round(moved / 1e6, 2),
+                             "queue_ms": round((tq - t0) * 1e3, 2)}
             return None, None, nxt, len(tokens), (t3 - t0) * 1e3
         return self._pool.submit(fill)
 
     def close(self):
         self._pool.shutdown(wait=True)
-        self.tx.close()
+        for tx, _peer in self._tx.values():
+            tx.close()
         self.rx.close()
 
 
 _ContinuousScheduler = ContinuousScheduler   # the reference's private name
 
-__all__ = ["ContinuousScheduler", "OneCardProducer", "NvlinkProducer"]
+__all__ = ["ContinuousScheduler", "OneCardProducer", "NvlinkProducer", "PrefillPool"]
