@@ -5,6 +5,8 @@
                    bf16/fp16 wire, plan / submit / wait / take (airm.py:137-221).
   TcpTransport     the cross-node relay path (name `tcp`, airm.py:224-271): host-dram ->
                    host-dram on any two machines through a TcpKVServer, CRC-checked.
+  NixlUcxTransport cross-node through NIXL's UCX backend (name `nixl-ucx`, airm.py:274-318):
+                   one-sided READ between registered host arenas, descriptors via the relay.
   NvlinkTransport  the new GPU -> GPU path (name `nvlink`): device-hbm -> device-hbm tiers,
                    payload moved by peer-to-peer stores into the decode cache (rngd_pd.nvlink).
 
@@ -207,6 +209,44 @@ class TcpTransport(_KeyedKV, _kv.TcpTransport):
             _kv.TcpTransport.__init__(self, serve_port=0)
         return (MemoryTier("tcp-prefill", "host-dram", 1 << 30), MemoryTier("tcp-decode", "host-dram", 1 << 30),
                 KVLayout(num_layers=2, num_kv_heads=2, head_dim=8, dtype="bf16"))
+
+
+class NixlUcxTransport(_KeyedKV, _kv.NixlUcxTransport):
+    """KV between two host-memory tiers on any two machines through NIXL's UCX backend
+    (airm.py:274-318).  remote=(host, port) is the relay for the descriptors (default
+    $AIRM_KV_TCP_ADDR), serve_port= also runs one here, agent= a NIXL agent (tests pass a fake),
+    pool_bytes= the arena per side.  wait() READs the blob (CRC-checked) and keeps it for take()."""
+
+    name = "nixl-ucx"
+    SCOPE = "only host-dram -> host-dram"
+
+    def __init__(self, remote=None, serve_port=None, agent=None, pool_bytes=None):
+        _kv.NixlUcxTransport.__init__(self, remote=remote, serve_port=serve_port, agent=agent, pool_bytes=pool_bytes)
+        self._held = {}
+        self._init_kv()
+
+    def supports(self, src, dst):
+        return src.kind == "host-dram" and dst.kind == "host-dram" and src.name != dst.name
+
+    def _detail(self):
+        return {"server": "%s:%d" % self.remote if self.remote else None, "agent": self.store.name}
+
+    def _fetch(self, key, timeout):
+        buf = self.pull(key, timeout=timeout)
+        with self._lock:
+            self._held[key] = buf
+        return buf
+
+    def _consume(self, key):
+        with self._lock:
+            return self._held.pop(key)
+
+    def close(self):
+        with self._lock:
+            self._pending.clear()
+            self._delivered.clear()
+            self._held.clear()
+        _kv.NixlUcxTransport.close(self)
 
 
 class NvlinkTransport(_nv.NvlinkTransport):

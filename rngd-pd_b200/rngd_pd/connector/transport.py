@@ -7,6 +7,8 @@ One interface, swappable backends, chosen by name:
     ├─ InProcTransport   in-process dict (tests, single process)
     ├─ ShmTransport      /dev/shm files, atomic publish (cross-process, same host)
     ├─ TcpTransport      a TcpKVServer relay (rngd_pd.connector.tcpkv): cross-node, host-staged
+    ├─ NixlUcxTransport  NIXL UCX one-sided READ between registered host arenas, descriptors
+    │                    through the relay (rngd_pd.connector.ucxkv): cross-node, host-staged
     └─ NvlinkTransport   GPU -> GPU peer-to-peer stores over NVLink (rngd_pd.nvlink),
                          registered as `nvlink`; moves device KV with push_device()
 
@@ -173,6 +175,34 @@ class ShmTransport(Transport):
             return f.read()
 
 
+def _relay_endpoint(remote, serve_port):
+    """(own relay or None, (host, port) or None, TcpKVClient or None) for a transport that talks
+    to a TcpKVServer: remote, else $AIRM_KV_TCP_ADDR, else the relay started on serve_port."""
+    from rngd_pd.connector.tcpkv import TcpKVClient, TcpKVServer, parse_addr
+    server = None
+    if serve_port is not None:
+        server = TcpKVServer(serve_port)
+        server.start()
+        serve_port = server.wait_ready()
+    if remote is None:
+        env = os.environ.get("AIRM_KV_TCP_ADDR")
+        if env:
+            remote = parse_addr(env)
+        elif serve_port is not None:
+            remote = ("127.0.0.1", serve_port)
+    remote = (remote[0], int(remote[1])) if remote else None
+    return server, remote, (TcpKVClient(*remote) if remote else None)
+
+
+def _audit_line(tag, op, key, buf, t0):
+    import hashlib
+    import sys
+    line = (f"[{tag}] {op} {key} {memoryview(buf).nbytes} {hashlib.sha256(buf).hexdigest()[:16]} "
+            f"{(time.perf_counter() - t0) * 1e3:.2f}ms\n")
+    sys.stdout.write(line)      # one write per line: several threads may log
+    sys.stdout.flush()
+
+
 class TcpTransport(Transport):
     """Cross-node KV through one TcpKVServer relay (connector/transport.py:104-154).
 
@@ -186,20 +216,7 @@ class TcpTransport(Transport):
     shared = True
 
     def __init__(self, remote=None, serve_port=None):
-        from rngd_pd.connector.tcpkv import TcpKVClient, TcpKVServer, parse_addr
-        self.server = None
-        if serve_port is not None:
-            self.server = TcpKVServer(serve_port)
-            self.server.start()
-            serve_port = self.server.wait_ready()
-        if remote is None:
-            env = os.environ.get("AIRM_KV_TCP_ADDR")
-            if env:
-                remote = parse_addr(env)
-            elif serve_port is not None:
-                remote = ("127.0.0.1", serve_port)
-        self.remote = (remote[0], int(remote[1])) if remote else None
-        self._client = TcpKVClient(*self.remote) if self.remote else None
+        self.server, self.remote, self._client = _relay_endpoint(remote, serve_port)
 
     def _relay(self):
         if self._client is None:
@@ -219,19 +236,65 @@ class TcpTransport(Transport):
 
     @staticmethod
     def _audit(op, key, buf, t0):
-        if os.environ.get("AIRM_KV_TCP_LOG", "0") in ("0", ""):
-            return
-        import hashlib
-        import sys
-        line = (f"[kv-tcp] {op} {key} {memoryview(buf).nbytes} {hashlib.sha256(buf).hexdigest()[:16]} "
-                f"{(time.perf_counter() - t0) * 1e3:.2f}ms\n")
-        sys.stdout.write(line)      # one write per line: several threads may log
-        sys.stdout.flush()
+        if os.environ.get("AIRM_KV_TCP_LOG", "0") not in ("0", ""):
+            _audit_line("kv-tcp", op, key, buf, t0)
 
     def handshake_metadata(self):
         return {"tcp": "%s:%d" % self.remote} if self.remote else {}
 
     def close(self):
+        if self._client is not None:
+            self._client.close()
+        if self.server is not None:
+            self.server.stop()
+
+
+class NixlUcxTransport(Transport):
+    """Cross-node KV through NIXL's UCX backend (connector/transport.py:157-211; the store is
+    rngd_pd.connector.ucxkv): push() stages the blob in this process's NIXL-registered arena
+    and publishes a descriptor in the TcpKVServer at remote=(host, port) or $AIRM_KV_TCP_ADDR
+    (descriptors only); pull() takes the descriptor and READs the bytes from the pushing
+    process over UCX, so the pusher must stay up until the reader has read.  UCX_TLS picks the
+    wire (tcp, or rc/ud verbs with an RDMA NIC).  CRC-32 per blob end to end; AIRM_KV_UCX_LOG=1
+    prints size and SHA-256 per blob.  One shared instance per process (select_transport), so
+    the agent, its registered arenas and the UCX endpoints outlive a request.  No NIXL raises."""
+    shared = True
+
+    def __init__(self, remote=None, serve_port=None, agent=None, pool_bytes=None):
+        from rngd_pd.connector.ucxkv import UcxKVStore
+        self.server, self.remote, self._client = _relay_endpoint(remote, serve_port)
+        self.store = UcxKVStore(self._client, agent=agent, pool_bytes=pool_bytes)
+
+    def _ready(self):
+        if self._client is None:
+            raise ValueError("nixl-ucx transport needs remote=(host, port) or AIRM_KV_TCP_ADDR=host:port "
+                             "(a TcpKVServer for the descriptors)")
+        return self.store
+
+    def push(self, key, buf):
+        t0 = time.perf_counter()
+        self._ready().push(key, buf)
+        self._audit("push", key, buf, t0)
+
+    def pull(self, key, timeout=5.0):
+        t0 = time.perf_counter()
+        buf = self._ready().pull(key, timeout=timeout)
+        self._audit("pull", key, buf, t0)
+        return buf
+
+    @staticmethod
+    def _audit(op, key, buf, t0):
+        if os.environ.get("AIRM_KV_UCX_LOG", "0") not in ("0", ""):
+            _audit_line("kv-ucx", op, key, buf, t0)
+
+    def handshake_metadata(self):
+        out = dict(self.store.describe())
+        if self.remote:
+            out["tcp"] = "%s:%d" % self.remote
+        return out
+
+    def close(self):
+        self.store.close()
         if self._client is not None:
             self._client.close()
         if self.server is not None:
@@ -293,10 +356,11 @@ class FencedTransport(Transport):
 
 
 # This package's own adapters, used when rm-core's registry is not installed or does not
-# know the name.  The reference's nixl / nixl-ucx transports (RDMA through NIXL, absent here)
-# resolve only through rm-core's registry when installed.
+# know the name.  The reference's rm-core `nixl` transport (rngd_pd.kv_nixl, an RDMA plugin
+# absent here) resolves only through rm-core's registry when installed.
 _OWN = {"shm": "rngd_pd.airm:ShmTransport", "tcp": "rngd_pd.airm:TcpTransport",
-        "nvlink": "rngd_pd.airm:NvlinkTransport", "inproc": "rngd_pd.connector.transport:InProcTransport"}
+        "nixl-ucx": "rngd_pd.airm:NixlUcxTransport", "nvlink": "rngd_pd.airm:NvlinkTransport",
+        "inproc": "rngd_pd.connector.transport:InProcTransport"}
 _CLASSES = {}
 _FENCED = {}
 _SHARED = {}
@@ -356,7 +420,7 @@ def select_transport(name=None, **kw) -> Transport:
 
 
 def make_transport(backend="shm", **kw) -> Transport:
-    """Factory (connector/transport.py:353-361): backend in {inproc, shm, tcp, nvlink}."""
+    """Factory (connector/transport.py:353-361): backend in {inproc, shm, tcp, nixl-ucx, nvlink}."""
     b = backend.lower()
     if b == "inproc":
         return InProcTransport()
@@ -364,6 +428,8 @@ def make_transport(backend="shm", **kw) -> Transport:
         return ShmTransport(**kw)
     if b == "tcp":
         return TcpTransport(**kw)
+    if b == "nixl-ucx":
+        return NixlUcxTransport(**kw)
     if b == "nvlink":
         from rngd_pd.nvlink import NvlinkTransport
         return NvlinkTransport(**kw)
