@@ -18,7 +18,7 @@ stats.  The fixture holds both byte streams of each connection and the two blobs
 replay the client streams against this build's relay and compare the replies, and compare the
 bytes this build's client sends for the same calls.
 
-    python tests/golden/make_tcp_transcript.py [--reference /root/reference]
+    python tests/golden/make_tcp_transcript.py --reference <reference checkout>   (or $RNGD_REFERENCE)
 """
 import argparse
 import os
@@ -67,8 +67,11 @@ class Recorder:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("RNGD_REFERENCE"),
+                    help="the reference project checkout (default $RNGD_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("pass --reference <reference checkout> or set RNGD_REFERENCE")
     sys.path.insert(0, os.path.join(a.reference, "src"))
     from rngd_pd.connector import tcpkv
     from rngd_pd.connector.transport import ser

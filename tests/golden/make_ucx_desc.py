@@ -5,7 +5,7 @@ this repository) and writes tests/golden/ucx_desc.npz: for each case the argumen
 name, metadata, address, n, crc) and the descriptor bytes.  tests/test_kv_ucx.py checks that
 this build packs the same bytes and reads the reference's.
 
-    python tests/golden/make_ucx_desc.py [--reference /root/reference]
+    python tests/golden/make_ucx_desc.py --reference <reference checkout>   (or $RNGD_REFERENCE)
 """
 import argparse
 import json
@@ -22,8 +22,11 @@ CASES = [("airm-kv-prefill-0", b'{"agent": "prefill", "ucx": [1, 2, 3]}', 0x7F12
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("RNGD_REFERENCE"),
+                    help="the reference project checkout (default $RNGD_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("pass --reference <reference checkout> or set RNGD_REFERENCE")
     sys.path.insert(0, os.path.join(a.reference, "src"))
     from rngd_pd.connector import ucxkv
     assert os.path.abspath(ucxkv.__file__).startswith(os.path.abspath(a.reference)), ucxkv.__file__
