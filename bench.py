@@ -14,8 +14,9 @@ needed between steps.
            (CUDA-graph replays that feed each argmax back as the next token)
   e2e      the same through the public API BatchDecodeEngine.step(): host
            token/position lists in (pinned H2D), next tokens out (D2H), per step
-  N > 1    one independent replica per GPU (decode does not shard),
-           value = all ranks' tokens / max-over-ranks device time
+  N > 1    one independent replica per GPU (decode does not shard: every GPU holds
+           the whole model and its own streams), value = all ranks' tokens /
+           max-over-ranks device time
 
 --impl reference times the CPU fp32 path (the test oracle's C restatement of
 the reference's cpu_layer, on all host cores) on the same workload; rank 0
