@@ -1,307 +1,401 @@
-"""Cross-node KV relay over TCP (API and wire protocol of src/rngd_pd/connector/tcpkv.py).
+"""Cross-node KV relay over TCP (the public names and wire protocol of the reference's
+src/rngd_pd/connector/tcpkv.py: TcpKVServer, TcpKVClient, parse_addr, the relay CLI).
 
-Where NVLink does not reach (prefill and decode on different nodes) the KV cache is staged
-through host memory and a relay: the prefill side pushes each layer's wire bytes to a
-TcpKVServer, the decode side takes them, and neither has to reach the other directly.  The
-relay holds a blob in host memory until one take hands it out (or its time-to-live passes).
+Where NVLink does not reach (prefill and decode on different nodes), each layer's wire bytes
+are pushed to a relay, and the decode side takes them from it; neither side has to reach the
+other directly.  The relay keeps a blob in host memory until one take hands it out or its
+time to live passes.
 
-    python -m rngd_pd.connector.tcpkv --port 5577     # a relay process, standard library only
+    python -m rngd_pd.connector.tcpkv --port 5577     # a relay; standard library only
 
-Wire (little-endian; one connection carries any number of requests).  It is byte-for-byte the
-reference's, so prefill and decode pods of either build share one relay:
+Wire (little-endian).  One connection carries any number of requests, one after another:
 
     push   b"P" klen:i32 key  n:i64 crc:u32 data   -> b"OK" | b"ER" (crc mismatch, blob dropped)
     take   b"W" klen:i32 key  wait_ms:i32          -> n:i64 crc:u32 data   (n = -1: absent after wait_ms)
     stats  b"S"                                    -> n:i64 json
 
-crc is zlib.crc32 of the data, computed by the pusher and checked by the relay on arrival and
-by the taker on delivery (0 = unchecked; AIRM_KV_TCP_CRC=0 stops computing it), so a take
-returns the pushed bytes or raises.
+crc is zlib.crc32 of the data.  The pusher computes it, the relay checks it on arrival and the
+taker on delivery (0 = unchecked; AIRM_KV_TCP_CRC=0 stops computing it).  The protocol and the
+stats JSON (its keys and their order) are shared with the reference's relay, so pods of either
+build use one relay.
+
+How this module is built: the relay keeps one mailbox per key (the blob, an event, the number
+of takers waiting), so a push wakes only the takes of its own key, and a sweeper thread drops
+blobs past their time to live.  Each connection has a thread of its own with blocking reads into
+one preallocated buffer per blob; socket reads and zlib's CRC release the GIL, so several
+connections move and check their blobs at once.  Requests are dispatched by their op byte
+through a table, and an unknown op drops only its own connection.  The client keeps a
+small bounded set of persistent connections, each with its own lock; a call takes whichever
+connection is idle, opens another while fewer than `max_connections` exist, and otherwise
+waits for one.  A request goes out as one scatter-gather send of header and payload, without
+joining them in memory.
 """
 import argparse
 import json
 import os
-import queue
 import socket
-import socketserver
 import struct
 import threading
 import time
 import zlib
 
 DEFAULT_PORT = 5577
-_BLOB = struct.Struct("<qI")      # n, crc
+_SIZE_CRC = struct.Struct("<qI")
 _I32 = struct.Struct("<i")
 _I64 = struct.Struct("<q")
+_SOCK_BUF = 4 << 20
+_STAT_KEYS = ("pushed", "taken", "expired", "crc_errors", "bytes_in", "bytes_out")
 
 
 def crc_enabled():
-    return os.environ.get("AIRM_KV_TCP_CRC", "1") not in ("0", "false", "no")
+    return os.environ.get("AIRM_KV_TCP_CRC", "1").strip().lower() not in ("0", "false", "no")
 
 
-def recv_exact(sock, n):
-    """Exactly n bytes from sock into one bytearray, or ConnectionError if the peer closes."""
+def _tune(sock):
+    """No Nagle delay, and socket buffers large enough that a 1 MiB layer moves in few reads."""
+    sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
+    for opt in (socket.SO_RCVBUF, socket.SO_SNDBUF):
+        try:
+            sock.setsockopt(socket.SOL_SOCKET, opt, _SOCK_BUF)
+        except OSError:
+            pass
+
+
+# --------------------------------------------------------------------------------- relay
+class _Mailbox:
+    """One key's slot in the relay: the blob once pushed, an event its takers wait on, and how
+    many takers are waiting."""
+    __slots__ = ("entry", "filled", "takers")
+
+    def __init__(self):
+        self.entry = None                   # (data, crc, stored at)
+        self.filled = threading.Event()
+        self.takers = 0
+
+
+class TcpKVServer(threading.Thread):
+    """The relay: start(), wait_ready() -> bound port (port 0 picks a free one), stop().
+
+    A blob nobody takes within ttl_s seconds ($AIRM_KV_TCP_TTL_S, default 900) is dropped, so a
+    request that died between prefill and decode does not hold its cache.  `stats` counts
+    pushed / taken / expired blobs, CRC errors and the bytes in and out."""
+
+    SWEEP_S = 0.25
+
+    def __init__(self, port, host="0.0.0.0", ttl_s=None):
+        super().__init__(daemon=True, name=f"tcpkv-relay:{port}")
+        self.host, self.port = host, int(port)
+        self.ttl_s = float(ttl_s if ttl_s is not None else os.environ.get("AIRM_KV_TCP_TTL_S", "900"))
+        self.stats = dict.fromkeys(_STAT_KEYS, 0)
+        self._boxes = {}                    # key -> _Mailbox
+        self._mu = threading.Lock()         # the mailbox table and the counters
+        self._listener = None
+        self._failure = None
+        self._up = threading.Event()
+        self._down = threading.Event()
+        self._ops = {b"P": self._op_push, b"W": self._op_take, b"S": self._op_stats}
+
+    # -- lifecycle ------------------------------------------------------------------------------
+    def run(self):
+        try:
+            self._listener = socket.create_server((self.host, self.port), backlog=64)
+        except OSError as e:
+            self._failure = e
+            self._up.set()
+            return
+        self.port = self._listener.getsockname()[1]
+        self._up.set()
+        threading.Thread(target=self._sweep, daemon=True, name="tcpkv-sweep").start()
+        while not self._down.is_set():
+            try:
+                conn, _ = self._listener.accept()
+            except OSError:
+                break                       # stop() shut the listener down
+            _tune(conn)
+            threading.Thread(target=self._serve, args=(conn,), daemon=True, name="tcpkv-conn").start()
+
+    def wait_ready(self, timeout=5.0):
+        if not self._up.wait(timeout) or self._failure is not None:
+            raise RuntimeError(f"TcpKVServer could not listen on {self.host}:{self.port}: {self._failure}")
+        return self.port
+
+    def stop(self):
+        """Stop accepting; connections already open end when their clients close them."""
+        self._down.set()
+        if self._listener is not None:
+            try:
+                self._listener.shutdown(socket.SHUT_RDWR)
+            except OSError:
+                pass
+            self._listener.close()
+
+    def snapshot(self):
+        """The stats reply's fields: counters, keys held and the bytes they hold."""
+        with self._mu:
+            held = [b.entry[0] for b in self._boxes.values() if b.entry is not None]
+            return dict(self.stats, keys=len(held), bytes_held=sum(len(d) for d in held))
+
+    # -- the store ------------------------------------------------------------------------------
+    def _sweep(self):
+        while not self._down.wait(self.SWEEP_S):
+            cutoff = time.monotonic() - self.ttl_s
+            with self._mu:
+                for key, box in list(self._boxes.items()):
+                    if box.entry is not None and box.entry[2] <= cutoff:
+                        box.entry = None
+                        box.filled.clear()
+                        self.stats["expired"] += 1
+                        if not box.takers:
+                            del self._boxes[key]
+
+    def _store(self, key, data, crc):
+        with self._mu:
+            box = self._boxes.get(key)
+            if box is None:
+                box = self._boxes[key] = _Mailbox()
+            box.entry = (data, crc, time.monotonic())
+            self.stats["pushed"] += 1
+            self.stats["bytes_in"] += len(data)
+            box.filled.set()
+
+    def _claim(self, key, wait_s):
+        """The blob under `key`, removed; waits up to wait_s for a push.  None if none came."""
+        deadline = time.monotonic() + wait_s
+        with self._mu:
+            box = self._boxes.get(key)
+            if box is None:
+                box = self._boxes[key] = _Mailbox()
+            box.takers += 1
+        entry = None
+        try:
+            while True:
+                with self._mu:
+                    if box.entry is not None:
+                        entry, box.entry = box.entry, None
+                        box.filled.clear()
+                        self.stats["taken"] += 1
+                        self.stats["bytes_out"] += len(entry[0])
+                        return entry
+                left = deadline - time.monotonic()
+                if left <= 0 or not box.filled.wait(left):
+                    return None
+        finally:
+            with self._mu:
+                box.takers -= 1
+                if not box.takers and box.entry is None and self._boxes.get(key) is box:
+                    del self._boxes[key]
+
+    # -- one connection -------------------------------------------------------------------------
+    def _op_push(self, conn):
+        key = _recv_into_new(conn, _I32.unpack(_recv_into_new(conn, 4))[0]).decode()
+        n, crc = _SIZE_CRC.unpack(_recv_into_new(conn, _SIZE_CRC.size))
+        if n < 0:
+            return False
+        data = _recv_into_new(conn, n)
+        if crc and zlib.crc32(data) != crc:
+            with self._mu:
+                self.stats["crc_errors"] += 1
+            conn.sendall(b"ER")
+        else:
+            self._store(key, data, crc)
+            conn.sendall(b"OK")
+        return True
+
+    def _op_take(self, conn):
+        key = _recv_into_new(conn, _I32.unpack(_recv_into_new(conn, 4))[0]).decode()
+        (wait_ms,) = _I32.unpack(_recv_into_new(conn, 4))
+        entry = self._claim(key, max(0, wait_ms) / 1e3)
+        if entry is None:
+            conn.sendall(_SIZE_CRC.pack(-1, 0))
+        else:
+            _send_parts(conn, (_SIZE_CRC.pack(len(entry[0]), entry[1]), entry[0]))
+        return True
+
+    def _op_stats(self, conn):
+        body = json.dumps(self.snapshot()).encode()
+        _send_parts(conn, (_I64.pack(len(body)), body))
+        return True
+
+    def _serve(self, conn):
+        try:
+            while True:
+                op = conn.recv(1)
+                handler = self._ops.get(op)
+                if handler is None or not handler(conn):
+                    return                  # closed, or a request this relay does not know
+        except (ConnectionError, OSError, ValueError, struct.error):
+            return
+        finally:
+            conn.close()
+
+
+# --------------------------------------------------------------------------------- client
+def _send_parts(sock, parts):
+    """Send every byte of `parts` (buffers) with scatter-gather sends."""
+    views = [memoryview(p).cast("B") for p in parts if memoryview(p).nbytes]
+    while views:
+        sent = sock.sendmsg(views)
+        while views and sent >= views[0].nbytes:
+            sent -= views[0].nbytes
+            views.pop(0)
+        if sent:
+            views[0] = views[0][sent:]
+
+
+def _recv_into_new(sock, n):
+    """Exactly n bytes from sock as a bytearray; ConnectionError if the peer closes first."""
     buf = bytearray(n)
-    view = memoryview(buf)
-    got = 0
+    view, got = memoryview(buf), 0
     while got < n:
-        k = sock.recv_into(view[got:], n - got)
-        if k == 0:
-            raise ConnectionError(f"peer closed after {got} of {n} bytes")
+        k = sock.recv_into(view[got:])
+        if not k:
+            raise ConnectionError(f"relay closed the connection after {got} of {n} bytes")
         got += k
     return buf
 
 
-def _nbytes(data):
-    return memoryview(data).nbytes
+class _Link:
+    """One persistent connection to the relay and the lock that serialises its requests."""
 
-
-class _Handler(socketserver.BaseRequestHandler):
-    """One client connection: requests in order until the client closes or sends garbage."""
-
-    def setup(self):
-        self.request.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
-
-    def handle(self):
-        relay, s = self.server.relay, self.request
-        try:
-            while True:
-                op = s.recv(1)
-                if not op:
-                    return
-                if op == b"S":
-                    s.sendall(relay._stats_reply())
-                    continue
-                if op not in (b"P", b"W"):
-                    return                                  # unknown request: drop the connection
-                (klen,) = _I32.unpack(recv_exact(s, 4))
-                if klen < 0:
-                    return
-                key = recv_exact(s, klen).decode()
-                if op == b"P":
-                    n, crc = _BLOB.unpack(recv_exact(s, _BLOB.size))
-                    if n < 0:
-                        return
-                    s.sendall(b"OK" if relay._put(key, recv_exact(s, n), crc) else b"ER")
-                else:
-                    (wait_ms,) = _I32.unpack(recv_exact(s, 4))
-                    entry = relay._take(key, max(0, wait_ms) / 1e3)
-                    if entry is None:
-                        s.sendall(_BLOB.pack(-1, 0))
-                    else:
-                        s.sendall(_BLOB.pack(len(entry[0]), entry[1]))
-                        s.sendall(entry[0])
-        except (ConnectionError, OSError):
-            return
-
-
-class _ThreadedServer(socketserver.ThreadingMixIn, socketserver.TCPServer):
-    daemon_threads = True
-    allow_reuse_address = True
-    request_queue_size = 64
-
-    def __init__(self, addr, relay):
-        self.relay = relay
-        super().__init__(addr, _Handler)
-
-    def service_actions(self):          # once per poll of the accept loop
-        self.relay._expire()
-
-
-class TcpKVServer(threading.Thread):
-    """In-memory key -> bytes relay behind a TCP port (tcpkv.py:50-152): start(), wait_ready()
-    (returns the bound port; port 0 picks a free one), stop().  A blob nobody takes within
-    ttl_s seconds ($AIRM_KV_TCP_TTL_S, default 900) is dropped, so a request that died between
-    prefill and decode does not hold its cache forever.  `stats` counts pushed / taken /
-    expired blobs, crc errors and bytes in and out."""
-
-    def __init__(self, port, host="0.0.0.0", ttl_s=None):
-        super().__init__(daemon=True, name=f"tcpkv:{port}")
-        self.port, self.host = int(port), host
-        self.ttl_s = float(ttl_s if ttl_s is not None else os.environ.get("AIRM_KV_TCP_TTL_S", "900"))
-        self.store = {}                                     # key -> (data, crc, arrival time)
-        self.cv = threading.Condition()
-        self.stats = {"pushed": 0, "taken": 0, "expired": 0, "crc_errors": 0, "bytes_in": 0, "bytes_out": 0}
-        self._srv = None
-        self._error = None
-        self._ready = threading.Event()
-
-    def run(self):
-        try:
-            self._srv = _ThreadedServer((self.host, self.port), self)
-        except OSError as e:
-            self._error = e
-            self._ready.set()
-            return
-        self.port = self._srv.server_address[1]
-        self._ready.set()
-        try:
-            self._srv.serve_forever(poll_interval=0.25)
-        finally:
-            self._srv.server_close()
-
-    def wait_ready(self, timeout=5.0):
-        if not self._ready.wait(timeout) or self._error is not None:
-            raise RuntimeError(f"TcpKVServer did not start on {self.host}:{self.port}: {self._error}")
-        return self.port
-
-    def stop(self):
-        """Stop accepting and close the listening socket (open connections finish on their own)."""
-        if self._srv is not None and self.is_alive():
-            self._srv.shutdown()
-
-    # -- the store, shared by the connection threads ------------------------------------------
-    def _put(self, key, data, crc):
-        if crc and zlib.crc32(data) != crc:
-            with self.cv:
-                self.stats["crc_errors"] += 1
-            return False
-        with self.cv:
-            self.store[key] = (data, crc, time.monotonic())
-            self.stats["pushed"] += 1
-            self.stats["bytes_in"] += len(data)
-            self.cv.notify_all()
-        return True
-
-    def _take(self, key, wait_s):
-        deadline = time.monotonic() + wait_s
-        with self.cv:
-            while key not in self.store:
-                left = deadline - time.monotonic()
-                if left <= 0:
-                    break
-                self.cv.wait(left)
-            entry = self.store.pop(key, None)
-            if entry is not None:
-                self.stats["taken"] += 1
-                self.stats["bytes_out"] += len(entry[0])
-        return entry
-
-    def _expire(self):
-        now = time.monotonic()
-        with self.cv:
-            old = [k for k, (_d, _c, t) in self.store.items() if now - t > self.ttl_s]
-            for k in old:
-                del self.store[k]
-            self.stats["expired"] += len(old)
-
-    def _stats_reply(self):
-        with self.cv:
-            snap = dict(self.stats, keys=len(self.store), bytes_held=sum(len(e[0]) for e in self.store.values()))
-        body = json.dumps(snap).encode()
-        return _I64.pack(len(body)) + body
+    def __init__(self):
+        self.lock = threading.Lock()
+        self.sock = None
 
 
 class TcpKVClient:
-    """push / take / stats against one TcpKVServer over a pool of persistent connections
-    (tcpkv.py:155-230): a fresh connection per 1 MB layer would restart TCP slow start each
-    time.  Thread-safe: every call borrows a connection of its own and returns it when done;
-    a connection whose state is unknown after an error is closed, never reused."""
+    """push / take / stats against one relay, thread-safe.
 
-    def __init__(self, host, port, connect_timeout=10.0):
+    Connections persist across calls (a fresh one per 1 MB layer would restart TCP slow start
+    every time).  A call uses an idle connection, opens a new one while fewer than
+    `max_connections` are open, else waits for the next to come free.  A connection whose
+    state is unknown after an error is closed and reopened by its next user."""
+
+    def __init__(self, host, port, connect_timeout=10.0, max_connections=8):
         self.addr = (host, int(port))
-        self.connect_timeout = connect_timeout
-        self._idle = queue.LifoQueue()
+        self.connect_timeout = float(connect_timeout)
+        self.max_connections = max(1, int(max_connections))
+        self._links = []
+        self._grow = threading.Lock()
+        self._turn = 0
 
-    def _checkout(self):
-        try:
-            return self._idle.get_nowait()
-        except queue.Empty:
-            s = socket.create_connection(self.addr, timeout=self.connect_timeout)
-            s.settimeout(None)
-            s.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
-            return s
+    def _acquire(self):
+        for link in list(self._links):
+            if link.lock.acquire(blocking=False):
+                return link
+        with self._grow:
+            if len(self._links) < self.max_connections:
+                link = _Link()
+                link.lock.acquire()
+                self._links.append(link)
+                return link
+            self._turn = (self._turn + 1) % len(self._links)
+            link = self._links[self._turn]
+        link.lock.acquire()
+        return link
 
-    def _call(self, fn):
-        s = self._checkout()
+    def _exchange(self, request):
+        link = self._acquire()
         try:
-            out = fn(s)
-        except BaseException:
-            s.close()
-            raise
-        self._idle.put(s)
-        return out
+            if link.sock is None:
+                s = socket.create_connection(self.addr, timeout=self.connect_timeout)
+                s.settimeout(None)
+                _tune(s)
+                link.sock = s
+            try:
+                return request(link.sock)
+            except BaseException:
+                link.sock.close()
+                link.sock = None
+                raise
+        finally:
+            link.lock.release()
+
+    def connections(self):
+        """How many connections to the relay are open."""
+        return sum(1 for link in list(self._links) if link.sock is not None)
 
     def push(self, key, data):
-        """Store `data` (any contiguous buffer: bytes, bytearray, memoryview, numpy array) under
-        `key`; IOError if the relay rejects it (crc mismatch in transit)."""
+        """Store `data` (any contiguous buffer: bytes, bytearray, memoryview, numpy array)
+        under `key`; IOError if the relay rejects it (its CRC did not match in transit)."""
+        payload = memoryview(data).cast("B")
         kb = key.encode()
-        n = _nbytes(data)
-        crc = zlib.crc32(data) if crc_enabled() else 0
+        crc = zlib.crc32(payload) if crc_enabled() else 0
+        head = b"".join((b"P", _I32.pack(len(kb)), kb, _SIZE_CRC.pack(payload.nbytes, crc)))
 
-        def go(s):
-            s.sendall(b"P" + _I32.pack(len(kb)) + kb + _BLOB.pack(n, crc))
-            s.sendall(data)
-            ack = bytes(recv_exact(s, 2))
-            if ack != b"OK":
-                raise IOError(f"tcpkv push {key}: relay rejected the blob ({ack!r}: crc mismatch)")
-        self._call(go)
+        def request(sock):
+            _send_parts(sock, (head, payload))
+            reply = bytes(_recv_into_new(sock, 2))
+            if reply != b"OK":
+                raise IOError(f"tcpkv push {key}: the relay rejected the blob ({reply!r}: crc mismatch)")
+        self._exchange(request)
 
     def take(self, key, timeout=5.0):
-        """The blob pushed under `key` (a bytearray), waiting up to `timeout` s for it, and removed
-        from the relay; TimeoutError if it never came, IOError on a crc mismatch."""
+        """The blob pushed under `key` (a bytearray), waited for up to `timeout` s and removed
+        from the relay.  TimeoutError if it never came, IOError if its CRC does not match."""
         kb = key.encode()
-        wait_ms = max(0, int(timeout * 1e3))
+        head = b"".join((b"W", _I32.pack(len(kb)), kb, _I32.pack(max(0, int(timeout * 1e3)))))
 
-        def go(s):
-            s.sendall(b"W" + _I32.pack(len(kb)) + kb + _I32.pack(wait_ms))
-            n, crc = _BLOB.unpack(recv_exact(s, _BLOB.size))
-            if n < 0:
-                return None
-            data = recv_exact(s, n)
-            if crc and crc_enabled() and zlib.crc32(data) != crc:
-                raise IOError(f"tcpkv take {key}: crc mismatch on delivery")
-            return data
-        data = self._call(go)
+        def request(sock):
+            _send_parts(sock, (head,))
+            n, crc = _SIZE_CRC.unpack(_recv_into_new(sock, _SIZE_CRC.size))
+            return (None, 0) if n < 0 else (_recv_into_new(sock, n), crc)
+        data, crc = self._exchange(request)
         if data is None:
             raise TimeoutError(f"pull timeout: {key}")
+        if crc and crc_enabled() and zlib.crc32(data) != crc:
+            raise IOError(f"tcpkv take {key}: crc mismatch on delivery")
         return data
 
     def stats(self):
-        def go(s):
-            s.sendall(b"S")
-            (n,) = _I64.unpack(recv_exact(s, 8))
-            return json.loads(bytes(recv_exact(s, n)))
-        return self._call(go)
+        def request(sock):
+            _send_parts(sock, (b"S",))
+            (n,) = _I64.unpack(_recv_into_new(sock, _I64.size))
+            return json.loads(bytes(_recv_into_new(sock, n)))
+        return self._exchange(request)
 
     def close(self):
-        while True:
-            try:
-                self._idle.get_nowait().close()
-            except queue.Empty:
-                return
+        for link in list(self._links):
+            with link.lock:
+                if link.sock is not None:
+                    link.sock.close()
+                    link.sock = None
 
 
 def parse_addr(text, default_port=DEFAULT_PORT):
-    """'host:port' or 'host' -> (host, port)."""
+    """'host:port', 'host', '[v6 address]:port' or '[v6 address]' -> (host, port)."""
     text = text.strip()
-    if ":" not in text:
-        return text, int(default_port)
-    host, _, port = text.rpartition(":")
-    return host, int(port or default_port)
+    if text.startswith("["):
+        host, _, rest = text[1:].partition("]")
+        port = rest[1:] if rest.startswith(":") else ""
+    elif text.count(":") == 1:
+        host, port = text.split(":")
+    else:
+        host, port = text, ""
+    return host, int(port) if port else int(default_port)
 
 
 def main(argv=None):
-    ap = argparse.ArgumentParser(description="KV relay: holds pushed KV blobs until one take hands each out")
+    ap = argparse.ArgumentParser(prog="python -m rngd_pd.connector.tcpkv",
+                                 description="KV relay: keeps each pushed blob until one take hands it out")
     ap.add_argument("--host", default="0.0.0.0")
-    ap.add_argument("--port", type=int, default=int(os.environ.get("AIRM_KV_TCP_PORT", str(DEFAULT_PORT))))
-    ap.add_argument("--stats-every", type=float, default=60.0, help="print the counters every N s (0: never)")
-    a = ap.parse_args(argv)
-    srv = TcpKVServer(a.port, a.host)
-    srv.start()
-    print(f"[tcpkv] relay on {a.host}:{srv.wait_ready()}", flush=True)
-    last = None
+    ap.add_argument("--port", type=int, default=int(os.environ.get("AIRM_KV_TCP_PORT", DEFAULT_PORT)))
+    ap.add_argument("--ttl", type=float, default=None, help="seconds an untaken blob is kept (AIRM_KV_TCP_TTL_S)")
+    ap.add_argument("--stats-every", type=float, default=60.0,
+                    help="print the counters every N s when they changed (0: never)")
+    opts = ap.parse_args(argv)
+    relay = TcpKVServer(opts.port, opts.host, ttl_s=opts.ttl)
+    relay.start()
+    print(f"[tcpkv] relay on {opts.host}:{relay.wait_ready()}", flush=True)
+    shown = None
     try:
-        while srv.is_alive():
-            time.sleep(a.stats_every or 3600)
-            if a.stats_every:
-                with srv.cv:
-                    snap = dict(srv.stats, keys=len(srv.store))
-                if snap != last:
-                    print(f"[tcpkv] {json.dumps(snap)}", flush=True)
-                    last = snap
+        while relay.is_alive():
+            relay.join(opts.stats_every or None)
+            now = relay.snapshot()
+            if opts.stats_every and now != shown:
+                print(f"[tcpkv] {json.dumps(now)}", flush=True)
+                shown = now
     except KeyboardInterrupt:
-        srv.stop()
+        relay.stop()
 
 
 if __name__ == "__main__":

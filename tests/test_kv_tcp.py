@@ -80,7 +80,7 @@ class RelayTests(unittest.TestCase):
         for i in range(20):
             self.c.push(f"k{i}", b"a" * 1000)
             self.c.take(f"k{i}")
-        self.assertEqual(self.c._idle.qsize(), 1)
+        self.assertEqual(self.c.connections(), 1)
 
     def test_concurrent_clients(self):
         blobs = {f"q{i}/layer.{j}/k": os.urandom(50_000) for i in range(8) for j in range(4)}
@@ -129,7 +129,7 @@ class RelayTests(unittest.TestCase):
     def test_expired_blobs_are_dropped(self):
         self.srv.ttl_s = 0.0
         self.c.push("old", b"x")
-        time.sleep(1.2)                                       # the accept loop expires every 0.25 s
+        time.sleep(1.2)                                       # the relay sweeps every 0.25 s
         self.assertEqual(self.c.stats()["expired"], 1)
 
     def test_port_in_use_fails_loud(self):
@@ -141,6 +141,41 @@ class RelayTests(unittest.TestCase):
     def test_parse_addr(self):
         self.assertEqual(tcpkv.parse_addr("relay.ns.svc:6000"), ("relay.ns.svc", 6000))
         self.assertEqual(tcpkv.parse_addr("relay"), ("relay", 5577))
+        self.assertEqual(tcpkv.parse_addr(" [::1]:7000 "), ("::1", 7000))
+        self.assertEqual(tcpkv.parse_addr("[fe80::2]"), ("fe80::2", 5577))
+
+    def test_connections_are_bounded_and_shared(self):
+        c = tcpkv.TcpKVClient("127.0.0.1", self.port, max_connections=2)
+        errs = []
+
+        def worker(i):
+            try:
+                for j in range(10):
+                    c.push(f"b{i}.{j}", bytes([i]) * 5000)
+                    if bytes(c.take(f"b{i}.{j}")) != bytes([i]) * 5000:
+                        errs.append((i, j))
+            except Exception as e:                            # noqa: BLE001 - reported below
+                errs.append(repr(e))
+        ts = [threading.Thread(target=worker, args=(i,)) for i in range(6)]
+        [t.start() for t in ts]
+        [t.join(30) for t in ts]
+        self.assertEqual(errs, [])
+        self.assertLessEqual(c.connections(), 2)
+        c.close()
+        self.assertEqual(c.connections(), 0)
+
+    def test_take_parked_before_the_push_gets_it_directly(self):
+        results = []
+        t = threading.Thread(target=lambda: results.append(bytes(self.c.take("direct", timeout=5))))
+        t.start()
+        time.sleep(0.2)
+        other = tcpkv.TcpKVClient("127.0.0.1", self.port)
+        other.push("direct", b"handed over")
+        other.close()
+        t.join(5)
+        self.assertEqual(results, [b"handed over"])
+        st = self.c.stats()
+        self.assertEqual((st["pushed"], st["taken"], st["keys"]), (1, 1, 0))
 
 
 class WireTranscript(unittest.TestCase):
@@ -379,7 +414,7 @@ class Adapter(_Env, unittest.TestCase):
             t.plan("bad", airm.MemoryTier("gpu0", "device-hbm", 1 << 30), dst, layout, layout, (0, 4))
         plan = t.plan("q3", src, dst, layout, layout, (0, 4))
         h = t.submit(plan)
-        t._relay().take(t._pending[h.token][1], timeout=1)      # someone else took it
+        t._relay().take(t.book.open[h.token].key, timeout=1)      # someone else took it
         res = t.wait(h, timeout_s=0.1)
         self.assertFalse(res.ok)
         t.close()

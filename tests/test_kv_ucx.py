@@ -119,29 +119,43 @@ def _until(cond, t=5.0):
     return False
 
 
-class ArenaAndDescriptor(unittest.TestCase):
-    def test_alloc_free_merge(self):
-        a = ucxkv.Arena(4096)
-        assert a.address % 4096 == 0
-        x = a.alloc(100)
-        y = a.alloc(1)
-        self.assertEqual((x, y), ((0, 128), (128, 64)))
-        a.free(*x)
-        self.assertEqual(a.alloc(64), (0, 64))     # first fit reuses the hole
-        a.free(0, 64)
-        a.free(*y)
-        self.assertEqual(a.free_bytes(), 4096)
-        self.assertEqual(a._holes, [(0, 4096)])
+class PoolAndDescriptor(unittest.TestCase):
+    def test_pages_in_ring_order(self):
+        p = ucxkv.HostPool(8 * 4096)
+        assert p.address % 4096 == 0
+        a = p.take(100)                     # one page
+        b = p.take(4097)                    # two pages
+        self.assertEqual((a, b), ((0, 1), (4096, 2)))
+        p.give(*a)
+        self.assertEqual(p.take(1), (3 * 4096, 1))        # the cursor moves on, not back to page 0
+        self.assertEqual(p.take(4 * 4096), (4 * 4096, 4))  # up to the end of the pool
+        self.assertEqual(p.take(1), (0, 1))               # then round to the first free page
+        self.assertEqual(p.free_bytes(), 0)
         with self.assertRaises(ValueError):
-            a.alloc(8192)
+            p.take(9 * 4096)
 
-    def test_alloc_waits_then_times_out(self):
-        a = ucxkv.Arena(1024)
-        slot = a.alloc(1024)
-        threading.Timer(0.1, lambda: a.free(*slot)).start()
-        self.assertEqual(a.alloc(512, timeout=2.0), (0, 512))
+    def test_freed_run_is_found_when_the_cursor_has_no_room(self):
+        p = ucxkv.HostPool(4 * 4096)
+        slots = [p.take(4096) for _ in range(4)]
+        p.give(*slots[1])
+        p.give(*slots[2])
+        self.assertEqual(p.take(2 * 4096), (4096, 2))
+        self.assertEqual(p.free_bytes(), 0)
+
+    def test_take_waits_then_times_out(self):
+        p = ucxkv.HostPool(4096)
+        slot = p.take(4096)
+        threading.Timer(0.1, lambda: p.give(*slot)).start()
+        self.assertEqual(p.take(512, timeout=2.0), (0, 1))
         with self.assertRaises(TimeoutError):
-            a.alloc(1024, timeout=0.05)
+            p.take(1024, timeout=0.05)
+
+    def test_bytes_land_where_the_address_says(self):
+        p = ucxkv.HostPool(2 * 4096)
+        off, _ = p.take(10)
+        p.view(off, 10)[:] = np.arange(10, dtype=np.uint8)
+        raw = (ctypes.c_uint8 * 10).from_address(p.address + off)
+        self.assertEqual(list(raw), list(range(10)))
 
     def test_descriptors_equal_the_reference(self):
         z = np.load(GOLDEN)
@@ -176,7 +190,7 @@ class Store(unittest.TestCase):
         self.assertEqual(bytes(self.rx.pull("r/layer.0/k", timeout=2)), blob)
         self.assertTrue(_until(lambda: not self.tx.pending()))
         self.assertEqual(self.tx.stats["freed"], 1)
-        self.assertEqual(self.tx._send.free_bytes(), 1 << 20)
+        self.assertEqual(self.tx.outbox.pool.free_bytes(), 1 << 20)
         self.assertEqual(self.fab.agents["decode"].remotes, {"prefill"})
         with self.assertRaises(TimeoutError):
             self.rx.pull("r/layer.0/k", timeout=0.05)     # the descriptor was taken once
@@ -232,7 +246,7 @@ class Store(unittest.TestCase):
 
     def test_overwritten_source_fails_the_crc(self):
         self.tx.push("c", b"clean bytes")
-        self.tx._send.buf[0:5] = np.frombuffer(b"dirty", np.uint8)
+        self.tx.outbox.pool.buf[0:5] = np.frombuffer(b"dirty", np.uint8)
         with self.assertRaises(IOError):
             self.rx.pull("c")
 
