@@ -96,7 +96,9 @@ class KVLoader:
         self.ttl_s = float(os.environ.get("PD_PREFETCH_TTL_S", "900"))
         self._prefetch = {}                      # req_id -> (future, started)
         self._lock = threading.Lock()
-        self._pool = ThreadPoolExecutor(max_workers=2)
+        # one worker per prefetch the map can hold: a prefetch whose KV never arrives blocks its
+        # own worker until the connector's pull timeout, never a later request's load
+        self._pool = ThreadPoolExecutor(max_workers=max(1, self.cap), thread_name_prefix="kv-prefetch")
 
     def _buffers(self):
         kshape, vshape = (self.nl, self.NKV, self.HD, self.S), (self.nl, self.NKV, self.S, self.HD)
@@ -142,26 +144,40 @@ class KVLoader:
                 return {"prefetch": "already running"}
             now = time.perf_counter()
             for old in [k for k, (_f, t0) in self._prefetch.items() if now - t0 > self.ttl_s]:
-                del self._prefetch[old]
+                # a queued load is cancelled; one already running cannot be stopped and ends
+                # by itself (its result is dropped)
+                self._prefetch.pop(old)[0].cancel()
             if len(self._prefetch) >= self.cap:
                 return {"prefetch": "skipped (full)", "req_id": req_id}
             self._prefetch[req_id] = (self._pool.submit(self.load_now, req_id), now)
         return {"prefetch": "started", "req_id": req_id}
 
-    def load(self, req_id):
+    def load(self, req_id, stream=None):
         """(K, V, load_ms, lead_ms): the prefetched load when one was started (lead_ms = how long
-        before this call it began), else a load now (lead_ms = -1)."""
+        before this call it began), else a load now (lead_ms = -1).
+
+        Device buffers are filled on the loading thread, complete when this returns, and come
+        from that thread's stream's memory pool.  Pass the stream that will read them (the decode
+        engine's, for write_slot_kv / adopt_kv_device) as `stream`: they are then recorded on it,
+        so dropping K and V right after queuing the copy cannot hand their memory to another
+        load while the copy still reads it.  Without `stream`, keep K and V alive until that
+        stream has consumed them."""
         with self._lock:
             entry = self._prefetch.pop(req_id, None)
         if entry is None:
             K, V, ms = self.load_now(req_id)
-            return K, V, ms, -1.0
-        fut, t0 = entry
-        K, V, ms = fut.result()
-        return K, V, ms, (time.perf_counter() - t0) * 1e3
+            lead = -1.0
+        else:
+            fut, t0 = entry
+            K, V, ms = fut.result()
+            lead = (time.perf_counter() - t0) * 1e3
+        if stream is not None and self.device is not None and getattr(K, "is_cuda", False):
+            K.record_stream(stream)
+            V.record_stream(stream)
+        return K, V, ms, lead
 
     def close(self):
-        self._pool.shutdown(wait=False)
+        self._pool.shutdown(wait=False, cancel_futures=True)
 
 
 __all__ = ["PrefillSaver", "KVLoader"]

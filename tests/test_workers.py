@@ -5,6 +5,7 @@ into float32 host arrays or bf16 tensors; consumed shm files are removed; prefet
 the save and is bounded."""
 import os
 import threading
+import time
 from types import SimpleNamespace
 from unittest import mock
 
@@ -121,3 +122,69 @@ def test_a_failed_save_raises():
             raise ConnectionError("link down")
     with pytest.raises(ConnectionError, match="link down"):
         PrefillSaver(StreamEngine(), Broken()).run("rq5", [1, 2])
+
+
+def test_a_stuck_prefetch_does_not_delay_another_load(tmp_path):
+    """Two prefetches whose KV never arrives hold their own workers until the pull timeout; a
+    third request whose KV has landed still loads at once."""
+    t = kv.ShmTransport(str(tmp_path))
+    with mock.patch.dict(os.environ, {"PD_PREFETCH_CAP": "3", "PD_KV_PULL_TIMEOUT": "3"}):
+        loader = KVLoader(t, L, NKV, HD, S)
+        try:
+            assert loader.prefetch("ghost1")["prefetch"] == "started"
+            assert loader.prefetch("ghost2")["prefetch"] == "started"
+            eng = StreamEngine()
+            PrefillSaver(eng, t).run("real", [4, 5])
+            assert loader.prefetch("real")["prefetch"] == "started"
+            t0 = time.perf_counter()
+            K, V, _ms, _lead = loader.load("real")
+            assert time.perf_counter() - t0 < 1.5
+            ek, ev = _expect(eng)
+            np.testing.assert_array_equal(K, ek)
+            np.testing.assert_array_equal(V, ev)
+        finally:
+            loader.close()
+
+
+def test_reclaimed_prefetch_that_has_not_started_is_cancelled(tmp_path):
+    t = kv.ShmTransport(str(tmp_path))
+    with mock.patch.dict(os.environ, {"PD_PREFETCH_CAP": "1", "PD_KV_PULL_TIMEOUT": "0.5"}):
+        loader = KVLoader(t, L, NKV, HD, S)
+    gate = threading.Event()
+    try:
+        loader._pool.submit(gate.wait)                     # the only worker is busy
+        loader.prefetch("queued")
+        fut = loader._prefetch["queued"][0]
+        loader.ttl_s = 0.0
+        loader.prefetch("next")
+        assert fut.cancelled() and "queued" not in loader._prefetch
+    finally:
+        gate.set()
+        loader.close()
+
+
+@pytest.mark.gpu
+def test_device_save_and_load_bit_exact_on_the_gpu(tmp_path):
+    """The device half: PrefillSaver over a real FullPrefillEngine (2 layers of the Llama-3.1-8B
+    shape) transposes K on the engine's stream and stages bf16 bits; KVLoader(device='cuda')
+    fills bf16 device buffers from the wire.  Both equal prefill_device's cache bit for bit."""
+    from rngd_pd.engines.model import ModelConfig
+    from rngd_pd.engines.prefill_full import FullPrefillEngine
+    from rngd_pd.synth import SyntheticState
+    cfg = ModelConfig.from_dims(L=2)
+    eng = FullPrefillEngine(cfg, SyntheticState(cfg, seed=0), C=128, group=1, S=256)
+    toks = [(13 * i + 7) % cfg.vocab for i in range(100)]
+    Kref, Vref, nref = eng.prefill_device(toks)
+    t = kv.ShmTransport(str(tmp_path))
+    rec = PrefillSaver(eng, t).run("gpu1", toks)
+    assert rec["next"] == nref
+    loader = KVLoader(t, cfg.n_layers, cfg.n_kv, cfg.head_dim, eng.S, device="cuda")
+    try:
+        s = torch.cuda.Stream()
+        K, V, _ms, _lead = loader.load("gpu1", stream=s)
+    finally:
+        loader.close()
+    assert K.is_cuda and K.dtype == torch.bfloat16
+    assert torch.equal(K.view(torch.int16), Kref.contiguous().view(torch.int16))     # both [L, NKV, HD, S]
+    assert torch.equal(V.view(torch.int16), Vref.contiguous().view(torch.int16))
+    assert os.listdir(tmp_path) == []
