@@ -117,6 +117,11 @@ int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* io, rngd_st
  * kernels/decode_batch.py:73-109, called from engines/decode_batch.py:436-439). */
 int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, int layer1,
                        rngd_stream_t stream);
+/* io->x (fp32 [B][H]) already holds the residual stream, written by the caller: writes
+ * layer0's first operand (x * n1[layer0], hi/lo) and its sums of squares and clears the
+ * argmax keys, so rngd_decode_layers can start at layer0 from a given hidden state
+ * (replaces the x input of DecodeModel.forward, kernels/decode_batch.py:100-109). */
+int rngd_decode_begin(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, rngd_stream_t stream);
 /* Final norm + lm_head + first-max argmax into io->next; logits kept in
  * io->logits (engines/decode_batch.py:440 and greedy_tokens 162-171).
  * The layer GEMMs and the lm_head run on tcgen05 tensor cores. */
@@ -163,6 +168,10 @@ typedef struct rngd_prefill_io {
 int rngd_prefill_workspace(const rngd_model_t* m, int C, size_t* partial_floats, size_t* counters);
 /* x = embed[toks]; act = hi/lo(x * n1[0]); ss (prompt embedding, engines/prefill_full.py:356-357). */
 int rngd_prefill_embed(const rngd_model_t* m, const rngd_prefill_io_t* io, rngd_stream_t stream);
+/* io->x (fp32 [C][H]) already holds the residual stream, written by the caller: layer0's
+ * first operand and sums of squares (replaces the x input of PrefillModel.forward,
+ * kernels/prefill_full.py:79-94). */
+int rngd_prefill_begin(const rngd_model_t* m, const rngd_prefill_io_t* io, int layer0, rngd_stream_t stream);
 /* Layers [layer0, layer1) of the prefill (replaces PrefillModel.forward over one layer
  * group, kernels/prefill_full.py:56-94, called from engines/prefill_full.py:210-214). */
 int rngd_prefill_layers(const rngd_model_t* m, const rngd_prefill_io_t* io, int layer0, int layer1,

@@ -990,6 +990,20 @@ extern "C" int rngd_decode_embed(const rngd_model_t* m, const rngd_decode_io_t* 
   return launch_operand(io->x, H, io->B, H, m->n1, io->act, ld_act, io->ss, (unsigned long long*)io->best, s);
 }
 
+// io->x already holds the residual stream (fp32 [B][H], written by the caller): layer0's first
+// operand hi/lo(x * n1[layer0]) and the sums of squares, argmax keys cleared.  Starts a run of
+// layer groups from a hidden state the caller supplies (kernels/decode_batch.py:100-109:
+// DecodeModel.forward receives x rather than token ids).
+extern "C" int rngd_decode_begin(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0,
+                                 rngd_stream_t stream) {
+  RNGD_TRY(check_tc_io(m, io));
+  RNGD_REQUIRE(0 <= layer0 && layer0 < m->L, "decode_begin: layer %d outside [0, %d)", layer0, m->L);
+  const int H = m->H, QN = m->NH * m->HD;
+  const int ld_act = H > QN ? H : QN;
+  return launch_operand(io->x, H, io->B, H, m->n1 + (size_t)layer0 * H, io->act, ld_act, io->ss,
+                        (unsigned long long*)io->best, (cudaStream_t)stream);
+}
+
 // Final norm + lm_head + first-max argmax for `rows` (<= 16) rows of x, e.g. the
 // last prompt position of a prefill (engines/prefill_full.py:265-270).
 extern "C" int rngd_lmhead_rows(const rngd_model_t* m, const float* x, int ldx, int rows, void* act, float* ss,

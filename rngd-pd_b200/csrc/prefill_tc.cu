@@ -790,6 +790,18 @@ extern "C" int rngd_prefill_embed(const rngd_model_t* m, const rngd_prefill_io_t
   return launch_operand_ex(io->x, H, io->C, H, m->n1, io->act, ld, io->C, io->ss, io->C, nullptr, s);
 }
 
+// io->x already holds the residual stream (fp32 [C][H], written by the caller): layer0's first
+// operand hi/lo(x * n1[layer0]) and the sums of squares (kernels/prefill_full.py:79-94:
+// PrefillModel.forward receives x rather than token ids).
+extern "C" int rngd_prefill_begin(const rngd_model_t* m, const rngd_prefill_io_t* io, int layer0,
+                                  rngd_stream_t stream) {
+  RNGD_TRY(check_pio(m, io));
+  RNGD_REQUIRE(0 <= layer0 && layer0 < m->L, "prefill_begin: layer %d outside [0, %d)", layer0, m->L);
+  const int H = m->H, QN = m->NH * m->HD, ld = H > QN ? H : QN;
+  return launch_operand_ex(io->x, H, io->C, H, m->n1 + (size_t)layer0 * H, io->act, ld, io->C, io->ss, io->C,
+                           nullptr, (cudaStream_t)stream);
+}
+
 // Causal attention of one layer on tcgen05 (pf_attn_tc_kernel): Q hi/lo from io->q, K from
 // the layer's cache block, V^T from the act2 scratch, output into io->act_o.
 static int launch_pf_attn(const rngd_model_t* m, const rngd_prefill_io_t* io, const uint16_t* kv, cudaStream_t s) {

@@ -78,6 +78,7 @@ _MP = ctypes.POINTER(Model)
 _IOP = ctypes.POINTER(DecodeIO)
 _sig("rngd_decode_embed", _MP, _IOP, _vp)
 _sig("rngd_decode_layers", _MP, _IOP, ctypes.c_int, ctypes.c_int, _vp)
+_sig("rngd_decode_begin", _MP, _IOP, ctypes.c_int, _vp)
 _sig("rngd_decode_lmhead", _MP, _IOP, _vp)
 _sig("rngd_decode_advance", _IOP, _vp)
 _szp = ctypes.POINTER(ctypes.c_size_t)
@@ -92,6 +93,7 @@ _PIOP = ctypes.POINTER(PrefillIO)
 _sig("rngd_prefill_workspace", _MP, ctypes.c_int, _szp, _szp)
 _sig("rngd_prefill_embed", _MP, _PIOP, _vp)
 _sig("rngd_prefill_layers", _MP, _PIOP, ctypes.c_int, ctypes.c_int, _vp)
+_sig("rngd_prefill_begin", _MP, _PIOP, ctypes.c_int, _vp)
 _sig("rngd_lmhead_rows", _MP, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp)
 _sig("rngd_lmhead_workspace", _MP, _szp, _szp)
 _sig("rngd_tc_gemm_tokens", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_int,
