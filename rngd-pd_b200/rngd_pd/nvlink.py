@@ -143,6 +143,106 @@ class _Peer:
         self._opened = []
 
 
+class LaneLeases:
+    """The receiver's lease book (host-only state; the flags themselves live wherever the
+    caller keeps them).
+
+    A lane is leased to one request at a time.  Every lease takes the lane's next sequence
+    number, and the sender publishes that number into the lane's per-layer flags after the
+    layer's bytes have landed.  A layer has arrived for a lease when its flag is >= the lease's
+    number; because numbers only grow, whatever an earlier request left in the flags never
+    satisfies a later lease of the same lane.  `start_after(lane, n)` continues after the
+    numbers already present in existing flags."""
+
+    def __init__(self, lanes):
+        self.lanes = int(lanes)
+        self._lock = threading.Lock()
+        self._seq = [0] * self.lanes
+        self._held = {}              # req_id -> (lane, seq)
+        self._sender = {}            # req_id -> sender device index, when declared
+
+    def start_after(self, lane, n):
+        with self._lock:
+            self._seq[lane] = max(self._seq[lane], int(n))
+
+    def reserve(self, req_id, lane, sender_device=None):
+        if not 0 <= lane < self.lanes:
+            raise IndexError(f"lane {lane} outside 0..{self.lanes - 1}")
+        with self._lock:
+            if any(l == lane for l, _ in self._held.values()):
+                raise ValueError(f"nvlink: lane {lane} is already leased")
+            if req_id in self._held:
+                raise ValueError(f"nvlink: request {req_id!r} already holds lane {self._held[req_id][0]}")
+            self._seq[lane] += 1
+            self._held[req_id] = (lane, self._seq[lane])
+            self._sender[req_id] = sender_device
+            return {"req": req_id, "lane": lane, "seq": self._seq[lane]}
+
+    def release(self, req_id):
+        with self._lock:
+            self._held.pop(req_id, None)
+            self._sender.pop(req_id, None)
+
+    def lookup(self, req_id):
+        """(lane, seq, sender device or None) of a held lease; KeyError if none."""
+        with self._lock:
+            if req_id not in self._held:
+                raise KeyError(f"nvlink: no lease for request {req_id!r}")
+            lane, seq = self._held[req_id]
+            return lane, seq, self._sender.get(req_id)
+
+    def snapshot(self):
+        with self._lock:
+            return {r: [lane, seq] for r, (lane, seq) in self._held.items()}
+
+    def clear(self):
+        with self._lock:
+            self._held.clear()
+            self._sender.clear()
+
+    @staticmethod
+    def landed(flag_row, seq, layer0, layer1):
+        """Whether layers [layer0, layer1) of a lane's flags (a sequence of ints) reached seq."""
+        return all(int(f) >= seq for f in flag_row[layer0:layer1])
+
+
+class SenderLeases:
+    """The sender's view of leases: request -> (receiver key, lane, seq), learned from a
+    receiver's handshake metadata or from tickets forwarded with requests."""
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._known = {}
+
+    def learn(self, peer_key, leases):
+        with self._lock:
+            for r, (lane, seq) in leases.items():
+                self._known[r] = (peer_key, lane, seq)
+
+    def add(self, peer_key, ticket):
+        with self._lock:
+            self._known[ticket["req"]] = (peer_key, ticket["lane"], ticket["seq"])
+
+    def find(self, req_id):
+        with self._lock:
+            return self._known.get(req_id)
+
+    def clear(self):
+        with self._lock:
+            self._known.clear()
+
+
+def poll_until(check, timeout, what, pause=20e-6):
+    """Call check() until it is true; TimeoutError naming `what` after `timeout` seconds.
+    Returns the seconds waited."""
+    t0 = time.perf_counter()
+    while not check():
+        if time.perf_counter() - t0 > timeout:
+            raise TimeoutError(f"nvlink: {what} did not arrive within {timeout}s")
+        time.sleep(pause)
+    return time.perf_counter() - t0
+
+
 class NvlinkTransport(Transport):
     """GPU -> GPU KV transport over NVLink (`airm.kv_transports` name `nvlink`)."""
 
@@ -157,15 +257,13 @@ class NvlinkTransport(Transport):
         self._lock = threading.RLock()
         # receiver state
         self._cache = None          # (K, V, flags) tensors
-        self._leases = {}           # req_id -> (lane, seq)
-        self._sender = {}           # req_id -> device index of the sender, when declared
-        self._lane_seq = collections.defaultdict(int)
+        self.leases = LaneLeases(0)
         self._status_host = self._status_dev = None
         self._status_next = 0
         self._poll_stream = self._poll_host = None
         # sender state
         self._peers = {}            # peer key -> _Peer
-        self._remote = {}           # req_id -> (peer key, lane, seq)
+        self.remote_leases = SenderLeases()
         self._done = {}             # stream handle -> completion counter of that stream's handoffs
         self.measurements = collections.deque(maxlen=1024)
 
@@ -183,9 +281,9 @@ class NvlinkTransport(Transport):
                 torch.zeros((Bcap, L), dtype=torch.int64, device=self.device)
         with self._lock:
             self._cache = (K, V, flags)
-            self._lane_seq.clear()
+            self.leases = LaneLeases(Bcap)
             for b in range(Bcap):   # continue after whatever the flags already hold
-                self._lane_seq[b] = int(flags[b].max().item())
+                self.leases.start_after(b, int(flags[b].max().item()))
 
     def reserve(self, req_id, lane, sender_device=None):
         """Lease `lane` to `req_id` before prefill writes it; returns the ticket {req, lane, seq}.
@@ -193,28 +291,16 @@ class NvlinkTransport(Transport):
         another GPU lets wait_stream() order the decode stream with a device-side wait."""
         if self._cache is None:
             raise RuntimeError("nvlink: reserve() before bind_cache()")
-        Bcap = self._cache[0].shape[1]
-        if not 0 <= lane < Bcap:
-            raise IndexError(f"lane {lane} outside 0..{Bcap - 1}")
-        with self._lock:
-            if any(l == lane for l, _ in self._leases.values()):
-                raise ValueError(f"nvlink: lane {lane} is already leased")
-            self._lane_seq[lane] += 1
-            self._leases[req_id] = (lane, self._lane_seq[lane])
-            self._sender[req_id] = sender_device
-            return {"req": req_id, "lane": lane, "seq": self._lane_seq[lane]}
+        return self.leases.reserve(req_id, lane, sender_device)
 
     def release(self, req_id):
-        with self._lock:
-            self._leases.pop(req_id, None)
-            self._sender.pop(req_id, None)
+        self.leases.release(req_id)
 
     def handshake_metadata(self):
         if self._cache is None:
             return {"transport": self.name, "pid": os.getpid(), "host": socket.gethostname()}
         K, V, flags = self._cache
-        with self._lock:
-            leases = {r: list(v) for r, v in self._leases.items()}
+        leases = self.leases.snapshot()
         return {"transport": self.name, "pid": os.getpid(), "host": socket.gethostname(),
                 "device": self.device.index, "shape": list(K.shape),
                 "ptrs": {"k": K.data_ptr(), "v": V.data_ptr(), "flags": flags.data_ptr()},
@@ -241,16 +327,11 @@ class NvlinkTransport(Transport):
         layer1 = L if layer1 is None else layer1
         if not 0 <= layer0 < layer1 <= L:
             raise ValueError(f"nvlink: layers [{layer0}, {layer1}) outside [0, {L})")
-        with self._lock:
-            if req_id not in self._leases:
-                raise KeyError(f"nvlink: no lease for request {req_id!r}")
-            lane, seq = self._leases[req_id]
-            sender = self._sender.get(req_id)
+        lane, seq, sender = self.leases.lookup(req_id)
         return lane, seq, layer1, sender
 
-    def arrived(self, req_id, layer0=0, layer1=None):
-        """Whether the request's layers [layer0, layer1) have landed (one small device->host copy)."""
-        lane, seq, layer1, _ = self._lease(req_id, layer0, layer1)
+    def _read_flags(self, lane):
+        """The lane's per-layer flags on the host: one small device->host copy on a side stream."""
         flags = self._cache[2]
         with self._lock:
             if self._poll_stream is None:
@@ -259,19 +340,19 @@ class NvlinkTransport(Transport):
             with torch.cuda.stream(self._poll_stream):
                 self._poll_host.copy_(flags[lane], non_blocking=True)
             self._poll_stream.synchronize()
-            return bool((self._poll_host[layer0:layer1] >= seq).all())
+            return self._poll_host.tolist()
+
+    def arrived(self, req_id, layer0=0, layer1=None):
+        """Whether the request's layers [layer0, layer1) have landed."""
+        lane, seq, layer1, _ = self._lease(req_id, layer0, layer1)
+        return LaneLeases.landed(self._read_flags(lane), seq, layer0, layer1)
 
     def wait(self, req_id, layer0=0, layer1=None, timeout=5.0):
         """Block until the request's layers [layer0, layer1) have landed; TimeoutError after
         `timeout` seconds.  Host polling of the flags: no kernel waits on another kernel."""
-        t0 = time.perf_counter()
         self._lease(req_id, layer0, layer1)
-        while not self.arrived(req_id, layer0, layer1):
-            if time.perf_counter() - t0 > timeout:
-                raise TimeoutError(f"nvlink: request {req_id!r} layers [{layer0}, {layer1}) did not arrive "
-                                   f"within {timeout}s")
-            time.sleep(20e-6)
-        return time.perf_counter() - t0
+        return poll_until(lambda: self.arrived(req_id, layer0, layer1), timeout,
+                          f"request {req_id!r} layers [{layer0}, {layer1})")
 
     def wait_stream(self, req_id, stream=None, layer0=0, layer1=None, timeout=5.0):
         """Order `stream` after the arrival of the request's layers [layer0, layer1); returns a
@@ -312,7 +393,7 @@ class NvlinkTransport(Transport):
     def lane_views(self, req_id):
         """(K, V) device views of the leased lane, [L, NKV, S, HD] each."""
         K, V, _ = self._cache
-        lane, _ = self._leases[req_id]
+        lane, _, _ = self.leases.lookup(req_id)
         return K[:, lane], V[:, lane]
 
     # ---------------------------------------------------------------- sender
@@ -324,27 +405,31 @@ class NvlinkTransport(Transport):
         with self._lock:
             if key not in self._peers:
                 self._peers[key] = _Peer(meta, self.device)
-            for r, (lane, seq) in meta.get("leases", {}).items():
-                self._remote[r] = (key, lane, seq)
+        self.remote_leases.learn(key, meta.get("leases", {}))
         return key
 
     def add_lease(self, peer_key, ticket):
         """Learn one lease (e.g. a ticket forwarded with the request) for a registered receiver."""
-        with self._lock:
-            self._remote[ticket["req"]] = (peer_key, ticket["lane"], ticket["seq"])
+        self.remote_leases.add(peer_key, ticket)
 
     def _target(self, req_id):
-        with self._lock:
-            if req_id in self._remote:
-                key, lane, seq = self._remote[req_id]
+        known = self.remote_leases.find(req_id)
+        if known is not None:
+            key, lane, seq = known
+            with self._lock:
                 return self._peers[key], lane, seq
-            if req_id in self._leases and self._cache is not None:     # sender and receiver in one object
-                lane, seq = self._leases[req_id]
+        if self._cache is not None:                      # sender and receiver in one object
+            try:
+                lane, seq, _ = self.leases.lookup(req_id)
+            except KeyError:
+                pass
+            else:
                 meta = self.handshake_metadata()
                 key = (meta["host"], meta["pid"], meta["device"], meta["ptrs"]["k"])
-                if key not in self._peers:
-                    self._peers[key] = _Peer(meta, self.device)
-                return self._peers[key], lane, seq
+                with self._lock:
+                    if key not in self._peers:
+                        self._peers[key] = _Peer(meta, self.device)
+                    return self._peers[key], lane, seq
         raise KeyError(f"nvlink: no lease known for request {req_id!r} (set_remote_handshake/add_lease first)")
 
     def push_device(self, req_id, kv, layer0=0, layer1=None, stream=None, tokens=None):
@@ -432,9 +517,8 @@ class NvlinkTransport(Transport):
             for p in self._peers.values():
                 p.close()
             self._peers.clear()
-            self._remote.clear()
-            self._leases.clear()
-            self._sender.clear()
+        self.remote_leases.clear()
+        self.leases.clear()
         if self._status_host is not None:
             _lib.lib.rngd_host_free(ctypes.c_void_p(self._status_host))
             self._status_host = self._status_dev = None

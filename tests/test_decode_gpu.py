@@ -101,7 +101,8 @@ def test_rmsnorm_matches_reference_formula():
     np.testing.assert_allclose(od.cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("S,positions", [(256, [0, 5, 127, 128, 255]), (512, [300, 511, 1])])
+@pytest.mark.parametrize("S,positions", [(256, [0, 5, 127, 128, 255]), (512, [300, 511, 1]),
+                                         (1024, [700, 1023, 0, 129])])
 def test_attention_matches_numpy(S, positions):
     from rngd_pd import _lib
     B, NKV, NH, HD = len(positions), 2, 8, 128
@@ -197,6 +198,39 @@ def test_lane_result_independent_of_batch():
         p4, p1 = [p + 1 for p in p4], [p1[0] + 1]
 
 
+def test_host_kv_intake_round_trips_and_pads_by_repeating_the_last():
+    """The host-KV intake of the reference's decode worker (engines/decode_batch.py:305-351):
+    load_kv = upload_prepared_kv(prepare_kv(...)) places request b in lane b and fills the
+    lanes past the last request with copies of it; download_kv / upload_kv round-trip the
+    resident cache bit for bit; stage_host_kv casts float32 host arrays to bf16; write_slot_kv
+    replaces one lane."""
+    from rngd_pd import synth
+    eng = _small_engine(3, 128)
+    cfg = eng.cfg
+    reqs = [synth.request_kv(cfg, 128, 300 + i, 20 + 30 * i) for i in range(2)]
+    host = [(k.float().cpu().numpy(), v.float().cpu().numpy()) for k, v in reqs]   # [nl, NKV, HD|S, S|HD]
+    Kd, Vd = eng.load_kv([h[0] for h in host], [h[1] for h in host])
+    K, V = eng.download_kv(Kd, Vd)                        # [nl, B, NKV, HD, S] / [nl, B, NKV, S, HD]
+    for lane, src in ((0, 0), (1, 1), (2, 1)):            # lane 2: the last request repeated
+        np.testing.assert_array_equal(K[:, lane], host[src][0])
+        np.testing.assert_array_equal(V[:, lane], host[src][1])
+    prepared = eng.prepare_kv([h[0] for h in host], [h[1] for h in host])
+    Kd2, Vd2 = eng.upload_prepared_kv(prepared)
+    for a, b in zip(Kd + Vd, Kd2 + Vd2):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    Kd3, Vd3 = eng.upload_kv(K, V)
+    for a, b in zip(Kd + Vd, Kd3 + Vd3):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    Ks, Vs = eng.stage_host_kv(K, V)
+    assert Ks.dtype == torch.bfloat16 and not Ks.is_cuda
+    np.testing.assert_array_equal(Ks.float().numpy(), K)
+    new_k, new_v = synth.request_kv(cfg, 128, 999, 50)
+    eng.write_slot_kv(Kd, Vd, 1, new_k, new_v)
+    K4, V4 = eng.download_kv(Kd, Vd)
+    np.testing.assert_array_equal(K4[:, 1], new_k.float().cpu().numpy())
+    np.testing.assert_array_equal(V4[:, 0], host[0][1])
+
+
 def test_bad_inputs_raise():
     eng = _small_engine(2, 128)
     Kd, Vd = eng.blank_kv()
@@ -246,23 +280,50 @@ def test_config1_full_llama_logits_and_64_greedy_steps(full_llama):
         assert cur_d == cur_r, f"greedy tokens diverge at step {step + 1}"
 
 
-@pytest.mark.slow
-def test_config4_B16_128_greedy_steps(full_llama):
-    """BASELINE config 4: B=16 streams, past lengths U[64, 384] (seed 3) so that 128 more steps
-    fit in S=512, seeded bf16 KV ~N(0,1), token ids U[0, V) (seed 2), 128 greedy steps against
-    the CPU fp32 oracle, teacher-forced as the reference's own check is (both sides consume the
-    oracle's token each step, bench/teacher_forced.py), through the public step() API.
+def _parity_log(name, record):
+    """Write a parity record as JSON into $RNGD_PARITY_LOG (a directory) when it is set."""
+    import json
+    import os
+    out = os.environ.get("RNGD_PARITY_LOG")
+    if out:
+        os.makedirs(out, exist_ok=True)
+        with open(os.path.join(out, name), "w") as f:
+            json.dump(record, f, indent=1)
 
-    With random-init weights the top two of 128256 logits are often very close, so over 2048
-    argmax decisions fp32-level differences (summation order) are expected to flip a few near
-    ties.  Checked: the first step's logits within 2e-2 max-abs (the config-1 bar); every
-    step's within 0.1 (bf16 K/V entries that round one ulp apart accumulate in both caches, so
-    the difference grows with the steps); each device choice is the oracle's argmax or a token
-    the oracle scores within twice that row's logit difference of its maximum (a genuine near
-    tie); and such flips are at most 1% of the decisions."""
+
+def _rows_into_oracle(Kd, Vd, Kc, Vc, pos):
+    """Copy the K/V rows the device step just wrote (position pos[b] of lane b, every layer and
+    kv head) into the C oracle's cache, which has the decode layout [L][B][NKV][S][HD] as bf16
+    bits.  Afterwards both caches hold identical bits at every position a later step reads."""
+    B = len(pos)
+    lanes = torch.arange(B, device=Kd[0].device)
+    at = torch.tensor(pos, device=Kd[0].device)
+    NG = Kd[0].shape[0]
+    for g, (kg, vg) in enumerate(zip(Kd, Vd)):
+        rk = kg[:, lanes, :, at, :].view(torch.int16).cpu().numpy().view(np.uint16)   # [B, NG, NKV, HD]
+        rv = vg[:, lanes, :, at, :].view(torch.int16).cpu().numpy().view(np.uint16)
+        for b in range(B):
+            Kc[g * NG:(g + 1) * NG, b, :, pos[b], :] = rk[b]
+            Vc[g * NG:(g + 1) * NG, b, :, pos[b], :] = rv[b]
+
+
+@pytest.mark.slow
+def test_config4_B16_128_steps_per_step_parity(full_llama):
+    """BASELINE config 4: B=16 streams, past lengths U[64, 384] (seed 3) so that 128 more steps
+    fit in S=512, seeded bf16 KV ~N(0,1), token ids U[0, V) (seed 2), 128 steps through the
+    public step() API against the CPU fp32 oracle, teacher-forced as the reference's own check
+    is (bench/teacher_forced.py: both sides consume the oracle's token each step).
+
+    After every step the device's newly written K/V rows are copied into the oracle's cache, so
+    each step starts from identical bits and its logits measure that step's arithmetic alone.
+    Bar: every step's logits within 2e-2 max-abs (north_star's per-step bound).  A greedy
+    choice may still differ where the oracle's top two are closer than the bound allows to
+    separate: with both logit vectors within e = 2e-2, the device can prefer the oracle's
+    second choice only if the oracle's gap is at most 2e = 4e-2.  Each such flip is checked
+    against that fixed bound and recorded."""
     from rngd_pd import synth
     cfg, w, cm = full_llama
-    B, S, steps = 16, 512, 128
+    B, S, steps, tol = 16, 512, 128, 2e-2
     lens = synth.context_lengths(B)
     assert min(lens) >= 64 and max(lens) + steps <= S
     eng = _engine_with(cfg, w, B, S)
@@ -273,7 +334,7 @@ def test_config4_B16_128_greedy_steps(full_llama):
     for b in range(B):
         cm.fill_lane(Kc, Vc, b, 100 + b, lens[b])
     cur, pos = synth.tokens(B, seed=2), list(lens)
-    ties, errs = [], []
+    errs, flips = [], []
     for step in range(steps):
         nxt_ref, lg_ref, _ = cm.decode_step(cur, pos, Kc, Vc)
         nxt_dev, Kd, Vd = eng.step(cur, pos, Kd, Vd)
@@ -281,13 +342,61 @@ def test_config4_B16_128_greedy_steps(full_llama):
         errs.append(float(diff.max()))
         for b in range(B):
             r, d = int(nxt_ref[b]), int(nxt_dev[b])
-            if r == d:
-                continue
-            gap = float(lg_ref[b][r] - lg_ref[b][d])
-            row = float(diff[b].max())
-            assert gap <= 2 * row, f"step {step} stream {b}: device {d} vs oracle {r}, gap {gap} > 2 x {row}"
-            ties.append((step, b, round(gap, 5)))
+            if r != d:
+                flips.append({"step": step, "stream": b, "oracle": r, "device": d,
+                              "gap": float(lg_ref[b][r] - lg_ref[b][d]), "row_err": float(diff[b].max())})
+        _rows_into_oracle(Kd, Vd, Kc, Vc, pos)
         cur, pos = [int(t) for t in nxt_ref], [p + 1 for p in pos]
-    assert errs[0] < 2e-2, f"first-step logits max-abs {errs[0]}"
-    assert max(errs) < 0.1, f"logits max-abs {max(errs)} at step {int(np.argmax(errs))}"
-    assert len(ties) <= 0.01 * steps * B, f"{len(ties)} near-tie flips in {steps * B} decisions: {ties}"
+    _parity_log("config4_teacher_forced.json",
+                {"steps": steps, "streams": B, "tol": tol, "max_err": max(errs), "mean_err": float(np.mean(errs)),
+                 "per_step_max_err": [round(e, 6) for e in errs], "decisions": steps * B, "flips": flips})
+    worst = int(np.argmax(errs))
+    assert errs[worst] < tol, f"step {worst}: logits max-abs {errs[worst]} >= {tol}"
+    for f in flips:
+        assert f["gap"] <= 2 * tol, f"not a near tie: {f}"
+
+
+@pytest.mark.slow
+def test_config4_free_running_first_divergence(full_llama):
+    """Config 4 free-running, as the reference's bench/teacher_forced.py reports it: device and
+    oracle each feed back their own greedy tokens and keep their own caches for 128 steps; the
+    first step where a stream's tokens differ is recorded with the oracle's gap between its
+    choice and the device's.  Random-init logits are 128256 draws of similar size, so their
+    top two often lie within fp32 summation-order noise; a divergence must be such a near tie
+    (the device's token is the oracle's runner-up, less than 0.1 below its maximum, against a
+    typical top-two spacing of ~0.3 here)."""
+    from rngd_pd import synth
+    cfg, w, cm = full_llama
+    B, S, steps = 16, 512, 128
+    lens = synth.context_lengths(B)
+    eng = _engine_with(cfg, w, B, S)
+    Ks, Vs = zip(*[synth.request_kv(cfg, S, 100 + b, lens[b]) for b in range(B)])
+    Kd, Vd = eng.adopt_kv_device(list(Ks), list(Vs))
+    del Ks, Vs
+    Kc, Vc = cm.new_cache(B, S)
+    for b in range(B):
+        cm.fill_lane(Kc, Vc, b, 100 + b, lens[b])
+    dev_tok = ref_tok = synth.tokens(B, seed=2)
+    pos = list(lens)
+    first = None
+    agree_steps = 0
+    for step in range(steps):
+        nxt_ref, lg_ref, _ = cm.decode_step(ref_tok, pos, Kc, Vc)
+        nxt_dev, Kd, Vd = eng.step(dev_tok, pos, Kd, Vd)
+        nxt_ref = [int(t) for t in nxt_ref]
+        if first is None:
+            bad = [b for b in range(B) if nxt_ref[b] != nxt_dev[b]]
+            if bad:
+                b = bad[0]
+                order = np.argsort(-lg_ref[b])
+                first = {"step": step, "stream": b, "oracle": nxt_ref[b], "device": nxt_dev[b],
+                         "gap": float(lg_ref[b][nxt_ref[b]] - lg_ref[b][nxt_dev[b]]),
+                         "device_rank_in_oracle": int(np.where(order == nxt_dev[b])[0][0]),
+                         "streams_diverging": len(bad)}
+            else:
+                agree_steps += 1
+        dev_tok, ref_tok, pos = nxt_dev, nxt_ref, [p + 1 for p in pos]
+    _parity_log("config4_free_running.json", {"steps": steps, "streams": B, "identical_steps": agree_steps,
+                                               "first_divergence": first})
+    if first is not None:
+        assert first["device_rank_in_oracle"] == 1 and first["gap"] < 0.1, f"divergence is not a near tie: {first}"

@@ -5,7 +5,8 @@ framework's CUDA-graph capture or private memory pool, or a host whose allocator
 owns all device memory.  For them, rngd_attn_decode_noalloc keeps its chunk
 partials in a scratch array built into the library instead of a buffer the caller
 allocates.  These tests call it through the C ABI and compare its output with
-rngd_attn_decode given caller-owned scratch, on two calls in a row with different
+rngd_attn_decode given caller-owned scratch and with fp32 numpy attention (up to S=1024),
+on two calls in a row with different
 shapes (the second call must not be affected by what the first left in the shared
 scratch), and check that a request larger than the built-in scratch is refused.
 This file sorts last so that a run stopping at the first failure has already run
@@ -46,6 +47,21 @@ def _attn_noalloc(q, K, V, pos, B, S):
     return ao
 
 
+def _attn_numpy(q, K, V, positions):
+    """Softmax attention over positions 0..pos of each stream, in fp32 numpy."""
+    B = len(positions)
+    Kf, Vf = K.float().cpu().numpy(), V.float().cpu().numpy()
+    qn = q.cpu().numpy().reshape(B, NKV, NH // NKV, HD)
+    out = np.empty((B, NH * HD), np.float32)
+    for b, p in enumerate(positions):
+        sc = np.einsum("kgh,ksh->kgs", qn[b], Kf[b][:, :p + 1]) / np.sqrt(HD)
+        sc -= sc.max(-1, keepdims=True)
+        pr = np.exp(sc)
+        pr /= pr.sum(-1, keepdims=True)
+        out[b] = np.einsum("kgs,ksh->kgh", pr, Vf[b][:, :p + 1]).reshape(-1)
+    return out
+
+
 def test_noalloc_attention_matches_allocating_entry_point():
     # first call: the config-4 shape (16 streams, S=512, long contexts);
     # second call: fewer streams, a wider cache, short contexts, so most of the
@@ -58,6 +74,7 @@ def test_noalloc_attention_matches_allocating_entry_point():
         got = _attn_noalloc(q, K, V, pos, B, S)
         torch.cuda.synchronize()
         np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(got.cpu().numpy(), _attn_numpy(q, K, V, positions), rtol=1e-4, atol=1e-5)
 
 
 def test_noalloc_refuses_requests_beyond_its_scratch():
