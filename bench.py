@@ -168,6 +168,9 @@ class TcGemm:
         import torch
         from rngd_pd import _lib
         L = len(self.W)
+        if trace is not None:        # raises before any capture when the library has no tracing
+            _lib.call("rngd_tc_gemv_trace", _lib.ptr(trace[0]))
+            _lib.call("rngd_tc_gemv_trace", None)
         side = torch.cuda.Stream(device=self.X.device)
         side.wait_stream(stream)
         with torch.cuda.stream(side):
@@ -287,7 +290,7 @@ def run_micro_prefill(args):
 
 
 HANDOFF_BATCHES = (1, 4, 16)
-PEER_COPY_GBS = 770.0      # measured peer copy per direction on this pool's B200s (profiling recipe)
+NVLINK_NOMINAL_GBS = 900.0     # NVLink 5, per direction per GPU (nominal; the measured copy is taken in the run)
 
 
 def handoff_bytes(cfg):
@@ -430,14 +433,46 @@ def handoff_one_process(dsts, reps, warmup):
                     if rep >= 3:
                         ce.append(e0.elapsed_time(e1))
                 del flat
-                row.update(bound="nvlink", frac=gbs / PEER_COPY_GBS, peak=PEER_COPY_GBS,
-                           copy_engine_gbs=n * per_req / statistics.median(ce) / 1e6)
+                copy_gbs = n * per_req / statistics.median(ce) / 1e6
+                row.update(bound="nvlink", peak=copy_gbs, peak_kind="peer copy of the same bytes, measured here",
+                           frac=gbs / copy_gbs, copy_engine_gbs=copy_gbs, frac_of_nominal=gbs / NVLINK_NOMINAL_GBS,
+                           nominal_gbs=NVLINK_NOMINAL_GBS)
             out.append(row)
         if tx is not rx:
             tx.close()
         rx.close()
         del K, V
     return out
+
+
+def config1_measure(eng, steps=20, warmup=3):
+    """BASELINE config 1's decode rate: B=4 streams with 256 past tokens each (KV seeds 100..103,
+    tokens seed 2), a B=4 engine on the weights of `eng`, device time of self-feeding graph
+    replays.  Its roofline bytes: the weights plus the KV read and written per step."""
+    import torch
+    from rngd_pd import synth
+    from rngd_pd.engines.decode_batch import BatchDecodeEngine
+    b4, past = 4, 256
+    e4 = BatchDecodeEngine(eng.cfg, eng.w, B=b4, S=S, group=8)
+    Ks, Vs = zip(*[synth.request_kv(eng.cfg, S, 100 + b, past, device=eng.dev) for b in range(b4)])
+    Kd, Vd = e4.adopt_kv_device(list(Ks), list(Vs))
+    del Ks, Vs
+    toks = synth.tokens(b4, seed=2)
+    e4.step(toks, [past] * b4, Kd, Vd)
+    e4.set_inputs(toks, [past] * b4)
+    e4.step_device(Kd, Vd, warmup)
+    torch.cuda.synchronize(eng.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(e4.stream)
+    e4.step_device(Kd, Vd, steps)
+    e1.record(e4.stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    mid = past + warmup + steps // 2
+    nbytes = WEIGHT_BYTES + b4 * (mid + 1) * KV_BYTES_PER_POS + b4 * KV_BYTES_PER_POS
+    del Kd, Vd, e4
+    return {"workload": "config1: batched decode B=4, S=512, 256 past tokens per stream", "ms_per_step": ms,
+            "tok_s": b4 / ms * 1e3, "bytes_per_step": nbytes, "achieved_gbs": nbytes / ms / 1e6}
 
 
 def prefill_flops(cfg, C):
@@ -547,7 +582,8 @@ def handoff_pairs(rank, world, dev, reps, warmup):
     dist.all_gather_object(metas, None if sender else t.handshake_metadata())
     key = t.set_remote_handshake(metas[partner]) if sender else None
     s = torch.cuda.Stream(device=dev)
-    out, exact = {}, True
+    out, copies, exact = {}, {}, True
+    pdev = torch.device("cuda", partner)
     for n in HANDOFF_BATCHES:
         times = []
         for rep in range(warmup + reps):
@@ -582,12 +618,33 @@ def handoff_pairs(rank, world, dev, reps, warmup):
         ms = torch.tensor([statistics.median(times) if times else 0.0], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         out[n] = float(ms.item())
+        # the copy engine moving the same bytes GPU 2i -> GPU 2i+1 (a peer copy from the sender's
+        # process), the measured peak the handoff is compared with
+        cms = []
+        if sender:
+            flat = torch.empty(n * kvs[0].numel(), dtype=torch.bfloat16, device=pdev)
+            for rep in range(warmup + reps):
+                with torch.cuda.stream(s):
+                    torch.cuda._sleep(SLEEP_CYCLES)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(s)
+                    for b in range(n):
+                        flat[b * kvs[0].numel():(b + 1) * kvs[0].numel()].copy_(kvs[(rep * n + b) % B].view(-1),
+                                                                                non_blocking=True)
+                    e1.record(s)
+                e1.synchronize()
+                if rep >= warmup:
+                    cms.append(e0.elapsed_time(e1))
+            del flat
+        cm = torch.tensor([statistics.median(cms) if cms else 0.0], device=dev)
+        dist.all_reduce(cm, op=dist.ReduceOp.MAX)
+        copies[n] = float(cm.item())
     ok = torch.tensor([1 if exact else 0], device=dev)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     t.close()                      # senders unmap before receivers free
     dist.barrier()
     del K, V, kvs
-    return out, bool(ok.item())
+    return out, copies, bool(ok.item())
 
 
 def run_micro_step_small(args):
@@ -657,6 +714,7 @@ def run_micro_serve_box(args):
             box.gateway.complete({"tokens": [1] * P, "max_tokens": 4})
     box.gateway.window.recs.clear()
     ttft, tpot, done_at, errors = [None] * n_req, [None] * n_req, [None] * n_req, []
+    outs = [None] * n_req
     t_start = time.perf_counter() + 0.2
 
     def client(i):
@@ -668,6 +726,7 @@ def run_micro_serve_box(args):
                                         on_token=lambda t: first.append(time.perf_counter()) if not first else None)
             ttft[i] = (first[0] - t_arr) * 1e3
             tpot[i] = resp["pd"]["tpot_ms"]
+            outs[i] = list(resp["choices"][0]["tokens"])
             done_at[i] = time.perf_counter()
         except Exception as e:   # noqa: BLE001 - reported
             errors.append(repr(e))
@@ -679,6 +738,8 @@ def run_micro_serve_box(args):
     occ = box.occupancy()
     box.close()
     ok = [i for i in range(n_req) if done_at[i] is not None]
+    solo = _solo_tokens(cfg, box.decode_engines, prompts, ok, out_tok) if os.environ.get("SERVE_SOLO", "1") != "0" \
+        else None
     span = max(done_at[i] for i in ok) - (t_start + arrivals[0]) if ok else float("nan")
     pct = lambda v, q: float(np.percentile([x for x in v if x is not None], q)) if ok else None
     print(json.dumps({"micro": "serve_box", "split": f"{split[0]}P:{split[1]}D", "gpus": n,
@@ -690,7 +751,61 @@ def run_micro_serve_box(args):
                       "ttft_ms_p50": pct(ttft, 50), "ttft_ms_p90": pct(ttft, 90),
                       "tpot_ms_p50": pct(tpot, 50), "tpot_ms_p90": pct(tpot, 90),
                       "decode_occupancy": occ, "airm": box.gateway.window.summary(),
+                      "solo": None if solo is None else _solo_report(outs, solo, ok),
                       "status": _lib.device_status()}), flush=True)
+
+
+def _solo_tokens(cfg, engines, prompts, which, out_tok):
+    """Every request of `which` served again as a solo single-GPU run: each decode GPU takes a
+    share and runs prefill and decode on itself (a FullPrefillEngine on the decode engine's
+    weights under a one-card continuous-batching scheduler).  Returns {request: tokens}."""
+    import threading
+    import torch
+    from rngd_pd.engines.prefill_full import FullPrefillEngine
+    from rngd_pd.serving.scheduler import ContinuousScheduler, OneCardProducer
+    got, errs = {}, []
+
+    def card(eng, share):
+        with torch.cuda.device(eng.dev):
+            pre = FullPrefillEngine(cfg, eng.w, C=256, group=2, S=eng.S)
+            pre.add_bucket(512)
+            prod = OneCardProducer(pre)
+            sched = ContinuousScheduler(eng.B, eng, prod.produce, produce_owner=prod, stage_admission=False)
+
+            def one(i):
+                try:
+                    got[i] = list(sched.submit({"tokens": prompts[i], "max_new": out_tok})["tokens"])
+                except Exception as e:   # noqa: BLE001 - reported
+                    errs.append(repr(e))
+            ts = [threading.Thread(target=one, args=(i,)) for i in share]
+            for t in ts:
+                t.start()
+            for t in ts:
+                t.join()
+            sched.close()
+    cards = [threading.Thread(target=card, args=(e, which[k::len(engines)])) for k, e in enumerate(engines)]
+    for t in cards:
+        t.start()
+    for t in cards:
+        t.join()
+    if errs:
+        got["_errors"] = errs[:3]
+    return got
+
+
+def _solo_report(outs, solo, which):
+    same = [i for i in which if solo.get(i) is not None and solo[i] == outs[i]]
+    differ = [i for i in which if i not in same]
+    first = None
+    if differ:
+        i = differ[0]
+        a, b = outs[i] or [], solo.get(i) or []
+        at = next((k for k in range(min(len(a), len(b))) if a[k] != b[k]), min(len(a), len(b)))
+        first = {"request": i, "position": at, "box": a[at:at + 4], "solo": b[at:at + 4]}
+    return {"checked": len(which), "identical": len(same), "first_difference": first,
+            "errors": solo.get("_errors", []),
+            "how": "each decode GPU re-serves its share of the trace alone: prefill and decode on that one GPU "
+                   "(one-card scheduler), greedy tokens compared request by request"}
 
 
 def run_micro_serve(args, pd=False):
@@ -790,7 +905,7 @@ def run_micro_serve(args, pd=False):
 def run_micro(args):
     """One decode GEMM shape alone (small device footprint; for ncu captures of skgemm_kernel)."""
     import torch
-    from rngd_pd import synth
+    from rngd_pd import _lib, synth
     if args.micro == "attn":
         return run_micro_attn(args)
     if args.micro == "step_small":
@@ -824,11 +939,14 @@ def run_micro(args):
     ms = g.time(args.steps, torch.cuda.current_stream(dev))
     # traced graph of 4 launches: per launch, CTA stamps relative to launch 0's earliest start (us)
     tr = torch.zeros((4, 1024, 16), dtype=torch.int64, device=dev)
-    g.time(4, torch.cuda.current_stream(dev), trace=tr)
-    t = tr.cpu().double()
-    t0 = t[0, :, 0][t[0, :, 0] > 0].min()
     timeline = []
-    for i in range(4):
+    try:
+        g.time(4, torch.cuda.current_stream(dev), trace=tr)
+    except _lib.RngdError:           # a product build (no TRACE=1): the stamps are compiled out
+        tr = None
+    t = tr.cpu().double() if tr is not None else None
+    t0 = t[0, :, 0][t[0, :, 0] > 0].min() if t is not None else None
+    for i in range(4 if t is not None else 0):
         ti = t[i][t[i, :, 0] > 0]
         rel = (ti - t0) / 1e3
         q = lambda col: [round(float(v), 2) for v in (rel[:, col].min(), rel[:, col].median(), rel[:, col].max())]
@@ -932,6 +1050,7 @@ def run_ours(args):
                            "so these timings are not valid")
 
     roof = gemm_roofline(eng) if rank == 0 else None
+    config1 = config1_measure(eng) if rank == 0 else None
     prefill = prefill_measure(eng) if rank == 0 else None
     prefill_chunk = prefill_chunk_measure(eng) if rank == 0 else None
 
@@ -940,13 +1059,16 @@ def run_ours(args):
     per_req = handoff_bytes(_MC.llama31_8b())
     hreps = 10
     if world >= 2 and world % 2 == 0:
-        hms, hexact = handoff_pairs(rank, world, dev, hreps, 3)
+        hms, hcopy, hexact = handoff_pairs(rank, world, dev, hreps, 3)
         pairs = world // 2
         handoff = {"unit": "GB/s", "pairs": pairs, "per_request_bytes": per_req, "byte_exact": hexact,
                    "path": "GPU 2i -> GPU 2i+1, separate processes, CUDA IPC + NVLink P2P stores",
                    "results": [{"requests": n, "ms": ms, "gbs": pairs * n * per_req / ms / 1e6,
-                                "frac": n * per_req / ms / 1e6 / PEER_COPY_GBS, "peak": PEER_COPY_GBS,
-                                "bound": "nvlink"} for n, ms in hms.items()]}
+                                "gbs_per_pair": n * per_req / ms / 1e6,
+                                "peak": n * per_req / hcopy[n] / 1e6, "peak_kind": "peer copy of the same bytes, "
+                                "measured here (max over pairs)",
+                                "frac": hcopy[n] / ms, "frac_of_nominal": n * per_req / ms / 1e6 / NVLINK_NOMINAL_GBS,
+                                "nominal_gbs": NVLINK_NOMINAL_GBS, "bound": "nvlink"} for n, ms in hms.items()]}
     elif rank == 0:
         rows = handoff_one_process([local], hreps, 3)
         handoff = {"unit": "GB/s", "pairs": 0, "per_request_bytes": per_req,
@@ -1000,6 +1122,8 @@ def run_ours(args):
         "handoff": handoff,
         "prefill": prefill,
         "prefill_chunk": prefill_chunk,
+        "config1": None if config1 is None else dict(config1, frac=config1["achieved_gbs"] / hbm, peak=hbm,
+                                                     unit="GB/s", peak_kind=peak_kind),
     }
     print(json.dumps(line), flush=True)
 

@@ -245,13 +245,14 @@ int rngd_gemv_bf16(const void* W, int N, int K, const float* X, int ldx, int B, 
 int rngd_tc_gemv(const void* W, int N, int K, const float* X, int ldx, int B, float* Y, int ldy, void* act,
                  float* partial, int32_t* counters, int prep, rngd_stream_t stream);
 int rngd_tc_gemv_workspace(int N, int K, size_t* partial_floats, size_t* counters);
-/* Diagnostics: when trace != NULL, later rngd_tc_gemv launches record per CTA sixteen
+/* Diagnostics, compiled in only by `make TRACE=1` (otherwise a non-NULL trace returns
+ * RNGD_ERR_UNSUPPORTED): when trace != NULL, later rngd_tc_gemv launches record per CTA sixteen
  * %globaltimer slots (ns) [start, operand ready, last weight TMA issued, last stage
  * arrived, last MMA committed, last accumulator ready, epilogue done, end, then five
  * steps of the last segment's epilogue] into trace[cta*16 ..] (device memory,
  * >= 16 * SM count entries). */
 int rngd_tc_gemv_trace(uint64_t* trace);
-/* Diagnostics: the next `launches` decode GEMM launches (layers, lm_head) record the
+/* Diagnostics (TRACE=1 builds only, as above): the next `launches` decode GEMM launches record the
  * same sixteen slots per CTA into consecutive blocks trace[i*1024*16 ..] (device memory,
  * launches * 16384 entries); NULL turns it off. */
 int rngd_trace_decode_gemms(uint64_t* trace, int launches);

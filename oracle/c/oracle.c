@@ -209,8 +209,27 @@ static int argmax_first(const float* v, int n) {
  * Kc, Vc: bf16 caches [L][B][NKV][S][HD], updated at pos[b].  Writes fp32 logits
  * [B][V] when logits != NULL, next tokens when next != NULL, final hidden [B][H]
  * when hidden != NULL. */
+static void decode_impl(const OrcModel* m, int B, int S, const int64_t* toks, const int64_t* pos, uint16_t* Kc,
+                        uint16_t* Vc, float* logits, int64_t* next, float* hidden, int keep_rows, uint16_t* own_k,
+                        uint16_t* own_v);
+
 void orc_decode_step(const OrcModel* m, int B, int S, const int64_t* toks, const int64_t* pos,
                      uint16_t* Kc, uint16_t* Vc, float* logits, int64_t* next, float* hidden) {
+  decode_impl(m, B, S, toks, pos, Kc, Vc, logits, next, hidden, 0, NULL, NULL);
+}
+
+/* The same step for a per-step parity check: the cache rows at pos[b] are left as the caller
+ * put them (keep_rows = 1: e.g. the device's rows of this step), and the rows this oracle
+ * computes are written to own_k / own_v ([L][B][NKV*HD] bf16 bits) when those are non-NULL. */
+void orc_decode_step_rows(const OrcModel* m, int B, int S, const int64_t* toks, const int64_t* pos,
+                          uint16_t* Kc, uint16_t* Vc, float* logits, int64_t* next, float* hidden, int keep_rows,
+                          uint16_t* own_k, uint16_t* own_v) {
+  decode_impl(m, B, S, toks, pos, Kc, Vc, logits, next, hidden, keep_rows, own_k, own_v);
+}
+
+static void decode_impl(const OrcModel* m, int B, int S, const int64_t* toks, const int64_t* pos, uint16_t* Kc,
+                        uint16_t* Vc, float* logits, int64_t* next, float* hidden, int keep_rows, uint16_t* own_k,
+                        uint16_t* own_v) {
   int H = m->H, NH = m->NH, NKV = m->NKV, HD = m->HD, G = NH / NKV;
   int QN = NH * HD, KN = NKV * HD;
   float* x = (float*)malloc(sizeof(float) * (size_t)B * H);
@@ -233,9 +252,15 @@ void orc_decode_step(const OrcModel* m, int B, int S, const int64_t* toks, const
       rope(k + (size_t)b * KN, NKV, HD, (int)pos[b], m->inv);
       for (int kh = 0; kh < NKV; kh++) {
         size_t base = ((((size_t)l * B + b) * NKV + kh) * S + (size_t)pos[b]) * HD;
+        size_t own = (((size_t)l * B + b) * NKV + kh) * HD;
         for (int d = 0; d < HD; d++) {
-          Kc[base + d] = f2bf(k[(size_t)b * KN + kh * HD + d]);
-          Vc[base + d] = f2bf(v[(size_t)b * KN + kh * HD + d]);
+          uint16_t kb = f2bf(k[(size_t)b * KN + kh * HD + d]), vb = f2bf(v[(size_t)b * KN + kh * HD + d]);
+          if (own_k) own_k[own + d] = kb;
+          if (own_v) own_v[own + d] = vb;
+          if (!keep_rows) {
+            Kc[base + d] = kb;
+            Vc[base + d] = vb;
+          }
         }
       }
     }

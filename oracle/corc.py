@@ -39,6 +39,8 @@ def lib():
         L.orc_model_free.argtypes = [ctypes.c_void_p]
         L.orc_decode_step.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _i64p, _i64p,
                                       _u16p, _u16p, _f32p, _i64p, _f32p]
+        L.orc_decode_step_rows.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _i64p, _i64p,
+                                           _u16p, _u16p, _f32p, _i64p, _f32p, ctypes.c_int, _u16p, _u16p]
         L.orc_prefill.argtypes = [ctypes.c_void_p, ctypes.c_int, _i64p, ctypes.c_int, _u16p, _u16p,
                                   _f32p, _i64p, _f32p]
         L.orc_kv_fill_lane.argtypes = [_u16p, _u16p] + [ctypes.c_int] * 6 + [ctypes.c_uint64,
@@ -106,6 +108,22 @@ class CModel:
                               _p(lg, _f32p) if lg is not None else None, _p(nxt, _i64p),
                               _p(hid, _f32p) if hid is not None else None)
         return nxt, lg, hid
+
+    def decode_step_given_rows(self, toks, pos, Kc, Vc):
+        """decode_step over a cache whose rows at pos[b] the caller has already written (kept as
+        given); returns (next, logits, own_k, own_v), own_* = the bf16 rows this oracle computes
+        for those positions, [L][B][NKV][HD] bits."""
+        d = self.d
+        B, S = Kc.shape[1], Kc.shape[3]
+        t = np.ascontiguousarray(toks, np.int64)
+        p = np.ascontiguousarray(pos, np.int64)
+        lg = np.empty((B, d.V), np.float32)
+        nxt = np.empty(B, np.int64)
+        own_k = np.empty((d.L, B, d.NKV, d.HD), np.uint16)
+        own_v = np.empty_like(own_k)
+        lib().orc_decode_step_rows(self.h, B, S, _p(t, _i64p), _p(p, _i64p), _p(Kc, _u16p), _p(Vc, _u16p),
+                                   _p(lg, _f32p), _p(nxt, _i64p), None, 1, _p(own_k, _u16p), _p(own_v, _u16p))
+        return nxt, lg, own_k, own_v
 
     def prefill(self, toks, S, want_hidden=False):
         d = self.d

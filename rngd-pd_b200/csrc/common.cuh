@@ -13,6 +13,13 @@
 
 #include "../../include/rngd_b200.h"
 
+// Per-CTA %globaltimer stamps in the decode GEMM (rngd_tc_gemv_trace, rngd_trace_decode_gemms)
+// are diagnostics: compiled in only by `make TRACE=1`.  In the product build the stamps fold away
+// and those two entries return RNGD_ERR_UNSUPPORTED for a non-NULL buffer.
+#ifndef RNGD_TRACE
+#define RNGD_TRACE 0
+#endif
+
 namespace rngd {
 
 void set_error(const char* fmt, ...);

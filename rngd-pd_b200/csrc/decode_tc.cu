@@ -158,7 +158,8 @@ __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constan
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   const long f0 = (long)cta * a.total / G, f1 = (long)(cta + 1) * a.total / G;
-  unsigned long long* tr = a.trace != nullptr ? a.trace + (size_t)cta * 16 : nullptr;
+  // RNGD_TRACE == 0 (the product build): tr is a constant null and every stamp below folds away
+  unsigned long long* tr = (RNGD_TRACE && a.trace != nullptr) ? a.trace + (size_t)cta * 16 : nullptr;
   if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer();
 
   if (threadIdx.x == 0) {
@@ -751,7 +752,7 @@ static unsigned long long* g_seq = nullptr;
 static int g_seq_left = 0;
 
 static void seq_trace(GemmArgs* a) {
-  if (a->trace == nullptr && g_seq != nullptr && g_seq_left > 0) {
+  if (RNGD_TRACE && a->trace == nullptr && g_seq != nullptr && g_seq_left > 0) {
     a->trace = g_seq;
     g_seq += 1024 * 16;
     g_seq_left--;
@@ -869,12 +870,20 @@ extern "C" int rngd_decode_attn_workspace(const rngd_model_t* m, int Bcap, int S
 static unsigned long long* g_trace = nullptr;  // set by rngd_tc_gemv_trace (diagnostics)
 
 extern "C" int rngd_tc_gemv_trace(uint64_t* trace) {
+  if (!RNGD_TRACE && trace != nullptr) {
+    set_error("tc_gemv_trace: this library was built without tracing (make TRACE=1)");
+    return RNGD_ERR_UNSUPPORTED;
+  }
   g_trace = (unsigned long long*)trace;
   return RNGD_OK;
 }
 
 extern "C" int rngd_trace_decode_gemms(uint64_t* trace, int launches) {
   RNGD_REQUIRE(launches >= 0, "trace_decode_gemms: negative launch count");
+  if (!RNGD_TRACE && trace != nullptr) {
+    set_error("trace_decode_gemms: this library was built without tracing (make TRACE=1)");
+    return RNGD_ERR_UNSUPPORTED;
+  }
   g_seq = (unsigned long long*)trace;
   g_seq_left = trace != nullptr ? launches : 0;
   return RNGD_OK;

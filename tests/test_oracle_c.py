@@ -82,3 +82,31 @@ def test_chunked_prefill_driver_matches_whole_prompt_prefill():
         np.testing.assert_allclose(K2, K1, rtol=1e-2, atol=2e-3)
         np.testing.assert_allclose(V2, V1, rtol=1e-2, atol=2e-3)
         np.testing.assert_allclose(l2, l1, rtol=1e-4, atol=1e-4)
+
+
+def test_given_rows_step_equals_the_plain_step_on_its_own_rows():
+    """orc_decode_step_rows with the rows decode_step itself writes reproduces decode_step bit for
+    bit, reports those rows, and leaves the caller's rows in place."""
+    d, S, B = SMALL, 16, 2
+    cm = corc.CModel(d, seed=0)
+    Ka, Va = cm.new_cache(B, S)
+    for b in range(B):
+        cm.fill_lane(Ka, Va, b, 200 + b, 5 + b)
+    Kb, Vb = Ka.copy(), Va.copy()
+    toks, pos = [3, 77], [5, 6]
+    nxt_a, lg_a, _ = cm.decode_step(toks, pos, Ka, Va)
+    for b in range(B):                                   # the rows step A wrote, put in by hand
+        Kb[:, b, :, pos[b]] = Ka[:, b, :, pos[b]]
+        Vb[:, b, :, pos[b]] = Va[:, b, :, pos[b]]
+    nxt_b, lg_b, own_k, own_v = cm.decode_step_given_rows(toks, pos, Kb, Vb)
+    np.testing.assert_array_equal(lg_a, lg_b)
+    assert list(nxt_a) == list(nxt_b)
+    for b in range(B):
+        np.testing.assert_array_equal(own_k[:, b], Ka[:, b, :, pos[b]])
+        np.testing.assert_array_equal(own_v[:, b], Va[:, b, :, pos[b]])
+    Kc, Vc = Kb.copy(), Vb.copy()
+    Kc[:, 0, :, pos[0]] = 0                              # different rows are used as given
+    _, lg_c, own_c, _ = cm.decode_step_given_rows(toks, pos, Kc, Vc)
+    assert not (Kc[:, 0, :, pos[0]]).any() and not np.array_equal(lg_c, lg_a)
+    np.testing.assert_array_equal(own_c[:, 1], own_k[:, 1])
+    cm.close()
