@@ -563,7 +563,7 @@ def handoff_pairs(rank, world, dev, reps, warmup):
     {requests: max-over-senders ms} and whether every receiver's lanes were byte-exact."""
     import torch
     import torch.distributed as dist
-    from rngd_pd import synth
+    from rngd_pd import _lib, synth
     from rngd_pd.engines.model import ModelConfig
     from rngd_pd.nvlink import NvlinkTransport, ipc_empty
     cfg = ModelConfig.llama31_8b()
@@ -622,6 +622,7 @@ def handoff_pairs(rank, world, dev, reps, warmup):
         # process), the measured peak the handoff is compared with
         cms = []
         if sender:
+            _lib.call("rngd_peer_enable", dev.index, partner)          # a direct copy over NVLink
             flat = torch.empty(n * kvs[0].numel(), dtype=torch.bfloat16, device=pdev)
             for rep in range(warmup + reps):
                 with torch.cuda.stream(s):

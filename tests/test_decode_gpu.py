@@ -303,12 +303,20 @@ def _device_rows(Kd, Vd, pos):
     return bits(rk), bits(rv)
 
 
-def _bf16_close(a, b):
-    """Element-wise: bf16 bit patterns a and b within one unit in the last place of the larger
-    magnitude (2^-7 relative bounds one bf16 ulp), or within 1e-6 absolute near zero."""
+def _bf16_rows_close(a, b):
+    """K/V rows [L][B][NKV][HD] as bf16 bits: (all elements close, max |a - b| / rms of the row).
+
+    Two fp32 computations of the same row (different summation orders over K = 4096..14336
+    terms, 32 layers deep) differ by a small fraction of the row's scale, and rounding each to
+    bf16 then differs by at most one unit in the last place -- except for elements near zero,
+    where that same absolute difference spans more units.  Close: |a - b| <= one bf16 ulp of
+    the larger magnitude (2^-7 relative bounds it) + 2^-9 of the row's rms."""
     fa = (a.astype(np.uint32) << 16).view(np.float32)
     fb = (b.astype(np.uint32) << 16).view(np.float32)
-    return np.abs(fa - fb) <= np.maximum(np.abs(fa), np.abs(fb)) * 2.0 ** -7 + 1e-6
+    rms = np.sqrt(np.mean(fb.astype(np.float64) ** 2, axis=-1, keepdims=True)).astype(np.float32)
+    d = np.abs(fa - fb)
+    ok = d <= np.maximum(np.abs(fa), np.abs(fb)) * 2.0 ** -7 + rms * 2.0 ** -9
+    return bool(ok.all()), float((d / np.maximum(rms, 1e-30)).max())
 
 
 @pytest.mark.slow
@@ -322,8 +330,8 @@ def test_config4_B16_128_steps_per_step_parity(full_llama):
     the oracle's cache, and the oracle steps over that cache keeping those rows and reporting
     the rows it computes itself.  So both sides read identical bits at every cache position,
     and two things are measured per step: (a) the device's new K/V rows against the oracle's,
-    each element within one bf16 ulp; (b) the logits within 2e-2 max-abs (north_star's per-step
-    bound).  A greedy choice may still differ where the oracle's top two are closer than that
+    each element within one bf16 ulp plus 2^-9 of its row's rms (_bf16_rows_close); (b) the
+    logits within 2e-2 max-abs (north_star's per-step bound).  A greedy choice may still differ where the oracle's top two are closer than that
     bound can separate: with both logit vectors within e = 2e-2, the device can prefer the
     oracle's runner-up only if the oracle's gap is at most 2e = 4e-2; each such flip is checked
     against that fixed bound and recorded."""
@@ -340,7 +348,7 @@ def test_config4_B16_128_steps_per_step_parity(full_llama):
     for b in range(B):
         cm.fill_lane(Kc, Vc, b, 100 + b, lens[b])
     cur, pos = synth.tokens(B, seed=2), list(lens)
-    errs, flips, row_same, row_close = [], [], [], []
+    errs, flips, row_same, row_close, row_dev = [], [], [], [], []
     for step in range(steps):
         nxt_dev, Kd, Vd = eng.step(cur, pos, Kd, Vd)
         lg_dev = eng.logits_bv().cpu().numpy()
@@ -350,7 +358,9 @@ def test_config4_B16_128_steps_per_step_parity(full_llama):
             Vc[:, b, :, pos[b]] = dv[:, b]
         nxt_ref, lg_ref, ok_, ov_ = cm.decode_step_given_rows(cur, pos, Kc, Vc)
         row_same.append(float(np.mean(np.concatenate([(dk == ok_).ravel(), (dv == ov_).ravel()]))))
-        row_close.append(bool(_bf16_close(dk, ok_).all() and _bf16_close(dv, ov_).all()))
+        (ck, dk_rel), (cv, dv_rel) = _bf16_rows_close(dk, ok_), _bf16_rows_close(dv, ov_)
+        row_close.append(ck and cv)
+        row_dev.append(max(dk_rel, dv_rel))
         diff = np.abs(lg_dev - lg_ref)
         errs.append(float(diff.max()))
         for b in range(B):
@@ -362,9 +372,10 @@ def test_config4_B16_128_steps_per_step_parity(full_llama):
     _parity_log("config4_teacher_forced.json",
                 {"steps": steps, "streams": B, "tol": tol, "max_err": max(errs), "mean_err": float(np.mean(errs)),
                  "per_step_max_err": [round(e, 6) for e in errs], "kv_rows_bit_identical": float(np.mean(row_same)),
-                 "kv_rows_min_identical_step": min(row_same), "kv_rows_within_1ulp_all_steps": all(row_close),
+                 "kv_rows_min_identical_step": min(row_same), "kv_rows_close_all_steps": all(row_close),
+                 "kv_rows_max_dev_over_rms": max(row_dev),
                  "decisions": steps * B, "flips": flips})
-    assert all(row_close), f"K/V rows beyond one bf16 ulp at steps {[i for i, c in enumerate(row_close) if not c]}"
+    assert all(row_close), f"K/V rows not close at steps {[i for i, c in enumerate(row_close) if not c]}"
     worst = int(np.argmax(errs))
     assert errs[worst] < tol, f"step {worst}: logits max-abs {errs[worst]} >= {tol}"
     for f in flips:
