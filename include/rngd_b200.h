@@ -163,6 +163,9 @@ typedef struct rngd_prefill_io {
   float* ss;            /* fp32 [H/128][C] per-128-column sums of squares of x */
   float* partial;       /* fp32 split-K scratch, rngd_prefill_workspace() floats */
   int32_t* counters;    /* int32 tile counters, rngd_prefill_workspace() entries, zeroed once */
+  int32_t operand_lo;   /* 1: GEMM operands as bf16 hi + lo rows (W*hi + W*lo, fp32-level accuracy);
+                           0: the hi row alone, one bf16 operand as the reference's graph takes bf16
+                           activations (kernels/prefill_full.py:56-76) at half the tensor work */
 } rngd_prefill_io_t;
 
 int rngd_prefill_workspace(const rngd_model_t* m, int C, size_t* partial_floats, size_t* counters);

@@ -83,7 +83,10 @@ class CModel:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:        # interpreter shutdown: the library may already be gone
+            pass
 
     def new_cache(self, B, S):
         d = self.d

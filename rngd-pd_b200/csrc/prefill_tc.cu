@@ -62,6 +62,7 @@ struct PArgs {
   float* partial;  // [units][maxseg][MT][NT][128] pieces of split units (slot 0's never stored)
   int* counters;   // [units] split epochs, then [units][maxseg] piece flags; zeroed once
   int nunits, tag;  // units of this launch; 1..15, distinct for GEMM shapes sharing the scratch
+  int lo;           // 1: W*hi + W*lo (fp32-level operand); 0: W*hi only (one bf16 operand row)
   const float* ss_in;  // [ss_tiles][C]
   int ss_tiles;
   float eps, inv_h;
@@ -115,6 +116,8 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
   // are far apart in u, so different CTAs stream the same weights at about the same time
   // and the second read hits L2 instead of HBM
   const int ngrp = a.N / (MT * PBM);
+  const bool use_lo = a.lo != 0;
+  const uint32_t stage_tx = (uint32_t)(Cfg::A_BYTES + (use_lo ? 2 : 1) * Cfg::B_BYTES);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
         const long u = f / a.nkb;
         const int kb = (int)(f - u * a.nkb), mg = (int)(u % ngrp);
         uint8_t* st = base + i * Cfg::STAGE;
-        mbar_arrive_expect_tx(&full[i], Cfg::STAGE);
+        mbar_arrive_expect_tx(&full[i], stage_tx);
         tma_load_3d(st, &tmW, &full[i], kb * PBK, mg * MT * PBM, a.layer);
       }
       grid_dep_wait();
@@ -158,7 +161,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
         const int kb = (int)(f - u * a.nkb), jt = (int)(u / ngrp);
         uint8_t* st = base + i * Cfg::STAGE;
         tma_load_2d(st + Cfg::A_BYTES, &tmX, &full[i], kb * PBK, jt * NT);
-        tma_load_2d(st + Cfg::A_BYTES + Cfg::B_BYTES, &tmX, &full[i], kb * PBK, a.C + jt * NT);
+        if (use_lo) tma_load_2d(st + Cfg::A_BYTES + Cfg::B_BYTES, &tmX, &full[i], kb * PBK, a.C + jt * NT);
       }
       for (long i = pre; i < nk; i++) {
         const int s = (int)(i % STAGES);
@@ -168,10 +171,10 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
         const long u = f / a.nkb;
         const int kb = (int)(f - u * a.nkb), mg = (int)(u % ngrp), jt = (int)(u / ngrp);
         uint8_t* st = base + s * Cfg::STAGE;
-        mbar_arrive_expect_tx(&full[s], Cfg::STAGE);
+        mbar_arrive_expect_tx(&full[s], stage_tx);
         tma_load_3d(st, &tmW, &full[s], kb * PBK, mg * MT * PBM, a.layer);
         tma_load_2d(st + Cfg::A_BYTES, &tmX, &full[s], kb * PBK, jt * NT);
-        tma_load_2d(st + Cfg::A_BYTES + Cfg::B_BYTES, &tmX, &full[s], kb * PBK, a.C + jt * NT);
+        if (use_lo) tma_load_2d(st + Cfg::A_BYTES + Cfg::B_BYTES, &tmX, &full[s], kb * PBK, a.C + jt * NT);
       }
       grid_dep_launch();
     }
@@ -205,7 +208,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
               const uint64_t ad = sw128_kmajor_desc(sa + tt * PBM * 128 + kk * 32);
               const uint32_t dt = d + (uint32_t)(tt * NT);
               umma_bf16(dt, ad, hd, idesc, (g != f || kk != 0) ? 1u : 0u);
-              umma_bf16(dt, ad, ld_, idesc, 1u);
+              if (use_lo) umma_bf16(dt, ad, ld_, idesc, 1u);
             }
           }
           umma_commit(&empty[s]);
@@ -759,6 +762,7 @@ static int check_pio(const rngd_model_t* m, const rngd_prefill_io_t* io) {
   RNGD_REQUIRE(io->C >= 128 && io->C % 128 == 0 && io->C <= 4096, "prefill: C=%d must be a multiple of 128", io->C);
   RNGD_REQUIRE(io->P >= 1 && io->P <= io->C && io->P <= io->S, "prefill: P=%d outside 1..min(C=%d, S=%d)", io->P,
                io->C, io->S);
+  RNGD_REQUIRE(io->operand_lo == 0 || io->operand_lo == 1, "prefill: operand_lo=%d must be 0 or 1", io->operand_lo);
   RNGD_REQUIRE(io->kv && io->toks && io->x && io->q && io->act && io->act_o && io->act2 && io->ss && io->partial &&
                    io->counters,
                "prefill: null buffer");
@@ -839,6 +843,7 @@ extern "C" int rngd_prefill_layers(const rngd_model_t* m, const rngd_prefill_io_
     PArgs a = {};
     a.C = io->C;
     a.P = io->P;
+    a.lo = io->operand_lo;
     a.partial = io->partial;
     a.counters = io->counters;
     a.ss_in = io->ss;
@@ -888,6 +893,7 @@ extern "C" int rngd_tc_gemm_tokens(const void* W, int N, int K, const float* X, 
   a.x = Y;
   a.ldx = N;
   a.tag = 5;
+  a.lo = 1;
   return launch_pf_any<PEPI_RESID>(W, 1, 0, N, K, act, K, a, s);
 }
 

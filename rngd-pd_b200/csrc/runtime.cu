@@ -52,7 +52,7 @@ extern "C" int rngd_last_error(char* buf, size_t n) {
   return RNGD_OK;
 }
 
-extern "C" int rngd_abi_version(void) { return 4; }
+extern "C" int rngd_abi_version(void) { return 5; }
 
 extern "C" int rngd_synth_gauss_bf16(void* dst, uint64_t n, uint64_t seed, uint64_t tid, uint64_t start,
                                      float scale, rngd_stream_t stream) {

@@ -58,7 +58,7 @@ class PrefillIO(ctypes.Structure):
     """rngd_prefill_io_t"""
     _fields_ = [("C", _i32), ("P", _i32), ("S", _i32), ("kv_layers", _i32), ("kv", _vp), ("toks", _vp),
                 ("x", _vp), ("q", _vp), ("act", _vp), ("act_o", _vp), ("act2", _vp), ("ss", _vp),
-                ("partial", _vp), ("counters", _vp)]
+                ("partial", _vp), ("counters", _vp), ("operand_lo", _i32)]
 
 
 def _sig(name, *args):

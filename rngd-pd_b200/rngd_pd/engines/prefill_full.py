@@ -12,6 +12,7 @@ layer, one 256-byte row per position; `prefill_kv_device`), which is what the
 NVLink handoff moves.  The reference layouts K [nl, NKV, HD, S] / V [nl, NKV, S, HD]
 are produced at the API boundary (`prefill`, `prefill_device`, `prefill_stream`).
 """
+import os
 import time
 
 import numpy as np
@@ -75,6 +76,12 @@ class FullPrefillEngine:
         self.w = sd if isinstance(sd, DeviceWeights) else DeviceWeights(cfg, sd, self.dev)
         self._m = self.w.model_struct()
         self.stream = torch.cuda.Stream(device=self.dev)
+        # GEMM operand precision ($RNGD_PREFILL_OPERAND): "hilo" = bf16 hi + lo rows (fp32-level),
+        # "bf16" = one bf16 row, as the reference's graph takes its activations
+        mode = os.environ.get("RNGD_PREFILL_OPERAND", "hilo")
+        if mode not in ("hilo", "bf16"):
+            raise ValueError(f"RNGD_PREFILL_OPERAND={mode!r}: expected 'hilo' or 'bf16'")
+        self.operand_lo = 1 if mode == "hilo" else 0
         self.buckets = {}
         self.last_C = None
         self.last_compute_ms = self.last_download_ms = 0.0
@@ -142,6 +149,7 @@ class FullPrefillEngine:
     def _io(self, b, kv_group, P):
         p = lambda t: t.data_ptr()
         return _lib.PrefillIO(C=b["C"], P=P, S=self.S, kv_layers=self.NG, kv=p(kv_group), toks=p(b["toks"]),
+                              operand_lo=self.operand_lo,
                               x=p(b["x"]), q=p(b["q"]), act=p(b["act"]), act_o=p(b["act_o"]), act2=p(b["act2"]),
                               ss=p(b["ss"]), partial=p(b["partial"]), counters=p(b["counters"]))
 

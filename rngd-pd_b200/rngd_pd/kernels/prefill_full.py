@@ -45,6 +45,7 @@ class _PassBuffers:
     def io(self, C, nl, kv):
         p = lambda t: t.data_ptr()
         return _lib.PrefillIO(C=C, P=C, S=C, kv_layers=nl, kv=p(kv), toks=p(self.toks), x=p(self.x), q=p(self.q),
+                              operand_lo=1,
                               act=p(self.act), act_o=p(self.act_o), act2=p(self.act2), ss=p(self.ss),
                               partial=p(self.partial), counters=p(self.counters))
 
