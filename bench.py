@@ -354,7 +354,7 @@ def handoff_one_process(dsts, reps, warmup):
     (one launch per batch) from GPU 0 into decode lanes on each GPU of `dsts` (GPU 0: HBM -> HBM;
     another GPU: over NVLink with peer access); byte-exact check of every lane.  Per batch size:
     the kernel's device time, and the API time (push_many + the receiver's wait() seeing every
-    flag, host wall clock); for a peer, a copy-engine peer copy of the same bytes as comparator."""
+    flag through wait_all, host wall clock); for a peer, a copy-engine peer copy of the same bytes.""" 
     import torch
     from rngd_pd import synth
     from rngd_pd.engines.model import ModelConfig
@@ -402,8 +402,7 @@ def handoff_one_process(dsts, reps, warmup):
                 else:
                     t0 = time.perf_counter()
                     tx.push_many(items, stream=s)
-                    for r in ids:
-                        rx.wait(r, timeout=10)
+                    rx.wait_all(ids, timeout=10)
                     if rep // 2 >= warmup:
                         api_ms.append((time.perf_counter() - t0) * 1e3)
                 for r in ids:
@@ -687,9 +686,12 @@ def run_micro_serve_box(args):
     P prefill GPUs push each prompt's cache over NVLink into the lanes of D decode GPUs, each a
     continuous-batching scheduler (B=16, S=512) behind one gateway.  SERVE_SPLIT picks the split
     ("2P:6D"; default half and half, i.e. 1P:1D pairs), SERVE_N the requests (default 512),
-    SERVE_RATE the Poisson arrival rate (default 40 req/s per decode GPU).  Prompts U[128, 448]
-    tokens, 64 output tokens, seeded.  Box tok/s = output tokens / (last completion - first
-    arrival); TTFT = arrival -> first token; TPOT = a request's median decode step."""
+    SERVE_RATE the Poisson arrival rate of the box (default 40 req/s per decode GPU) or
+    SERVE_RATES a sweep of per-decode-GPU rates ("24,40"), all on the same box and prompts.
+    Prompts U[128, 448] tokens, 64 output tokens, seeded.  Box tok/s = output tokens / (last
+    completion - first arrival); TTFT = arrival -> first token; TPOT = a request's median decode
+    step.  Afterwards every request is served again solo on one GPU (SERVE_SOLO=0 skips it) and
+    its greedy tokens compared with each run's."""
     import threading
     import numpy as np
     import torch
@@ -705,54 +707,70 @@ def run_micro_serve_box(args):
     cfg = ModelConfig.llama31_8b()
     box = build_pd(cfg, synth.SyntheticState(cfg, seed=0), split=split, B=B, S=S)
     out_tok = 64
-    rate = float(os.environ.get("SERVE_RATE", str(40.0 * split[1])))
     n_req = int(os.environ.get("SERVE_N", "512"))
+    if os.environ.get("SERVE_RATES"):        # per decode GPU, a sweep
+        rates = [float(r) * split[1] for r in os.environ["SERVE_RATES"].split(",")]
+    else:
+        rates = [float(os.environ.get("SERVE_RATE", str(40.0 * split[1])))]
     rng = np.random.default_rng(5)
-    arrivals = np.cumsum(rng.exponential(1.0 / rate, n_req))
     prompts = [rng.integers(0, cfg.vocab, int(rng.integers(128, 449))).tolist() for _ in range(n_req)]
     for P in (200, 400):                    # warm-up outside the trace: both buckets on every pairing
         for _ in range(max(split)):
             box.gateway.complete({"tokens": [1] * P, "max_tokens": 4})
-    box.gateway.window.recs.clear()
-    ttft, tpot, done_at, errors = [None] * n_req, [None] * n_req, [None] * n_req, []
-    outs = [None] * n_req
-    t_start = time.perf_counter() + 0.2
+    pct = lambda v, q: float(np.percentile([x for x in v if x is not None], q)) if any(
+        x is not None for x in v) else None
+    runs = []
+    for k, rate in enumerate(rates):
+        box.gateway.window.recs.clear()
+        arrivals = np.cumsum(np.random.default_rng(6 + k).exponential(1.0 / rate, n_req))
+        ttft, tpot, done_at, errors = [None] * n_req, [None] * n_req, [None] * n_req, []
+        outs = [None] * n_req
+        lane0 = [(sc.steps, sc.lane_steps) for sc in box.schedulers]
+        t_start = time.perf_counter() + 0.2
 
-    def client(i):
-        t_arr = t_start + arrivals[i]
-        time.sleep(max(0.0, t_arr - time.perf_counter()))
-        first = []
-        try:
-            resp = box.gateway.complete({"tokens": prompts[i], "max_tokens": out_tok},
-                                        on_token=lambda t: first.append(time.perf_counter()) if not first else None)
-            ttft[i] = (first[0] - t_arr) * 1e3
-            tpot[i] = resp["pd"]["tpot_ms"]
-            outs[i] = list(resp["choices"][0]["tokens"])
-            done_at[i] = time.perf_counter()
-        except Exception as e:   # noqa: BLE001 - reported
-            errors.append(repr(e))
-    threads = [threading.Thread(target=client, args=(i,)) for i in range(n_req)]
-    for t in threads:
-        t.start()
-    for t in threads:
-        t.join()
-    occ = box.occupancy()
+        def client(i):
+            t_arr = t_start + arrivals[i]
+            time.sleep(max(0.0, t_arr - time.perf_counter()))
+            first = []
+            try:
+                resp = box.gateway.complete({"tokens": prompts[i], "max_tokens": out_tok},
+                                            on_token=lambda t: first.append(time.perf_counter()) if not first else None)
+                ttft[i] = (first[0] - t_arr) * 1e3
+                tpot[i] = resp["pd"]["tpot_ms"]
+                outs[i] = list(resp["choices"][0]["tokens"])
+                done_at[i] = time.perf_counter()
+            except Exception as e:   # noqa: BLE001 - reported
+                errors.append(repr(e))
+        threads = [threading.Thread(target=client, args=(i,)) for i in range(n_req)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        ok = [i for i in range(n_req) if done_at[i] is not None]
+        span = max(done_at[i] for i in ok) - (t_start + arrivals[0]) if ok else float("nan")
+        occ = [(sc.lane_steps - l0) / max((sc.steps - s0) * sc.B, 1) for sc, (s0, l0) in zip(box.schedulers, lane0)]
+        runs.append({"rate_req_s": rate, "rate_per_decode_gpu": rate / split[1], "requests": n_req,
+                     "completed": len(ok), "errors": errors[:3],
+                     "box_tok_s": len(ok) * out_tok / span if ok else 0.0, "span_s": span,
+                     "ttft_ms_p50": pct(ttft, 50), "ttft_ms_p90": pct(ttft, 90),
+                     "tpot_ms_p50": pct(tpot, 50), "tpot_ms_p90": pct(tpot, 90),
+                     "decode_occupancy": occ, "airm": box.gateway.window.summary(), "_outs": outs, "_ok": ok})
+        print(json.dumps({"micro": "serve_box", "split": f"{split[0]}P:{split[1]}D", "gpus": n,
+                          **{k2: v for k2, v in runs[-1].items() if not k2.startswith("_")}}), flush=True)
     box.close()
-    ok = [i for i in range(n_req) if done_at[i] is not None]
-    solo = _solo_tokens(cfg, box.decode_engines, prompts, ok, out_tok) if os.environ.get("SERVE_SOLO", "1") != "0" \
-        else None
-    span = max(done_at[i] for i in ok) - (t_start + arrivals[0]) if ok else float("nan")
-    pct = lambda v, q: float(np.percentile([x for x in v if x is not None], q)) if ok else None
+    solo = None
+    if os.environ.get("SERVE_SOLO", "1") != "0":
+        every = sorted(set(i for r in runs for i in r["_ok"]))
+        got = _solo_tokens(cfg, box.decode_engines, prompts, every, out_tok)
+        solo = [dict(_solo_report(r["_outs"], got, r["_ok"]), rate_req_s=r["rate_req_s"]) for r in runs]
+    best = max(runs, key=lambda r: r["box_tok_s"])
     print(json.dumps({"micro": "serve_box", "split": f"{split[0]}P:{split[1]}D", "gpus": n,
                       "workload": "PD box in one process: prefill GPUs -> NVLink -> decode lanes, continuous "
                                   "batching B=16, S=512, seeded Poisson trace, prompts U[128,448], 64 output "
                                   "tokens, Llama-3.1-8B shape",
-                      "rate_req_s": rate, "requests": n_req, "completed": len(ok), "errors": errors[:3],
-                      "box_tok_s": len(ok) * out_tok / span if ok else 0.0, "span_s": span,
-                      "ttft_ms_p50": pct(ttft, 50), "ttft_ms_p90": pct(ttft, 90),
-                      "tpot_ms_p50": pct(tpot, 50), "tpot_ms_p90": pct(tpot, 90),
-                      "decode_occupancy": occ, "airm": box.gateway.window.summary(),
-                      "solo": None if solo is None else _solo_report(outs, solo, ok),
+                      "runs": [{k2: v for k2, v in r.items() if not k2.startswith("_")} for r in runs],
+                      "box_tok_s": best["box_tok_s"], "ttft_ms_p50": best["ttft_ms_p50"],
+                      "tpot_ms_p50": best["tpot_ms_p50"], "solo": solo,
                       "status": _lib.device_status()}), flush=True)
 
 

@@ -261,10 +261,12 @@ class NvlinkTransport(Transport):
         self._status_host = self._status_dev = None
         self._status_next = 0
         self._poll_stream = self._poll_host = None
+        self._poll_all = None
         # sender state
         self._peers = {}            # peer key -> _Peer
         self.remote_leases = SenderLeases()
         self._done = {}             # stream handle -> completion counter of that stream's handoffs
+        self._items = None          # the launch's rngd_kv_item_t array, reused
         self.measurements = collections.deque(maxlen=1024)
 
     # ------------------------------------------------------------- receiver
@@ -341,6 +343,33 @@ class NvlinkTransport(Transport):
                 self._poll_host.copy_(flags[lane], non_blocking=True)
             self._poll_stream.synchronize()
             return self._poll_host.tolist()
+
+    def _read_all_flags(self):
+        """Every lane's flags on the host ([Bcap][L] list of lists): one small copy for all."""
+        flags = self._cache[2]
+        with self._lock:
+            if getattr(self, "_poll_all", None) is None or self._poll_all.shape != flags.shape:
+                if self._poll_stream is None:
+                    self._poll_stream = torch.cuda.Stream(device=self.device)
+                self._poll_all = torch.zeros(flags.shape, dtype=torch.int64).pin_memory()
+            with torch.cuda.stream(self._poll_stream):
+                self._poll_all.copy_(flags, non_blocking=True)
+            self._poll_stream.synchronize()
+            return self._poll_all.tolist()
+
+    def arrived_all(self, req_ids, layer0=0, layer1=None):
+        """Whether every request of `req_ids` has layers [layer0, layer1) landed."""
+        leases = [self._lease(r, layer0, layer1) for r in req_ids]
+        rows = self._read_all_flags()
+        return all(LaneLeases.landed(rows[lane], seq, layer0, l1) for lane, seq, l1, _ in leases)
+
+    def wait_all(self, req_ids, layer0=0, layer1=None, timeout=5.0):
+        """wait() for several requests at once: each poll reads every lane's flags in one copy."""
+        req_ids = list(req_ids)
+        for r in req_ids:
+            self._lease(r, layer0, layer1)
+        return poll_until(lambda: self.arrived_all(req_ids, layer0, layer1), timeout,
+                          f"requests {req_ids[:3]}{'...' if len(req_ids) > 3 else ''} layers [{layer0}, {layer1})")
 
     def arrived(self, req_id, layer0=0, layer1=None):
         """Whether the request's layers [layer0, layer1) have landed."""
@@ -440,18 +469,25 @@ class NvlinkTransport(Transport):
 
     def push_many(self, items, layer0=0, layer1=None, stream=None):
         """push_device for several requests [(req_id, kv, tokens or None), ...]: one launch per
-        receiver and per 16 requests (rngd_kv_handoff_batch).  Returns the bytes moved."""
+        receiver and per 16 requests (rngd_kv_handoff_batch).  Returns the bytes moved.
+
+        The host path stays short: K / V source addresses are computed from the cache tensor's
+        address (no views are made), each cache is recorded once on the launch stream, and the
+        launch's item array is a reused ctypes buffer."""
         groups = {}
         for req_id, kv, tokens in items:
             peer, lane, seq = self._target(req_id)
             l1 = peer.L if layer1 is None else layer1
-            if kv.dtype != BF or not kv.is_contiguous() or kv.device != self.device:
+            nl = l1 - layer0
+            if kv.dtype != BF or kv.device != self.device or not kv.is_contiguous():
                 raise ValueError(f"nvlink: kv must be a contiguous bf16 tensor on {self.device}")
-            blk = kv if kv.shape[0] == l1 - layer0 else kv[layer0:l1]
-            if tuple(blk.shape[1:]) != (2, peer.NKV, peer.S, peer.HD) or blk.shape[0] != l1 - layer0:
-                raise ValueError(f"nvlink: kv layer block {tuple(blk.shape)} does not match the receiver's "
-                                 f"[{l1 - layer0}, 2, {peer.NKV}, {peer.S}, {peer.HD}]")
-            groups.setdefault(id(peer), (peer, l1, []))[2].append((lane, seq, blk[:, 0], blk[:, 1], tokens))
+            shape = kv.shape
+            if shape[1:] != (2, peer.NKV, peer.S, peer.HD) or shape[0] not in (nl, peer.L):
+                raise ValueError(f"nvlink: kv layer block {tuple(shape)} does not match the receiver's "
+                                 f"[{nl}, 2, {peer.NKV}, {peer.S}, {peer.HD}]")
+            plane = peer.NKV * peer.S * peer.HD * 2                     # bytes of one layer's K (or V)
+            k_ptr = kv.data_ptr() + (0 if shape[0] == nl else layer0) * 2 * plane
+            groups.setdefault(id(peer), (peer, l1, []))[2].append((lane, seq, k_ptr, k_ptr + plane, tokens, kv))
         moved = 0
         for peer, l1, reqs in groups.values():
             for i in range(0, len(reqs), _lib.KV_MAX_BATCH):
@@ -467,7 +503,8 @@ class NvlinkTransport(Transport):
                     tuple(t.shape) != (peer.NKV, peer.S, peer.HD):
                 raise ValueError(f"nvlink: layer tensors must be contiguous bf16 [{peer.NKV}, {peer.S}, "
                                  f"{peer.HD}] on {self.device}")
-        return self._launch(peer, [(lane, seq, k, v, tokens)], 0, layer, layer + 1, stream)
+        return self._launch(peer, [(lane, seq, k.data_ptr(), v.data_ptr(), tokens, k, v)], 0, layer, layer + 1,
+                            stream)
 
     def _counter(self, s):
         key = s.cuda_stream
@@ -478,22 +515,31 @@ class NvlinkTransport(Transport):
         return c
 
     def _launch(self, peer, reqs, stride, layer0, layer1, stream):
-        """One rngd_kv_handoff_batch launch: reqs = [(lane, seq, k, v, tokens), ...] (<= 16)."""
+        """One rngd_kv_handoff_batch launch: reqs = [(lane, seq, k address, v address, tokens,
+        *tensors the addresses point into), ...] (<= 16)."""
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
-        arr = (_lib.KvItem * len(reqs))()
-        moved = 0
-        for i, (lane, seq, k, v, tokens) in enumerate(reqs):
-            tokens = peer.S if tokens is None else int(tokens)
-            # the caller may drop its cache right after this call: keep the allocator from handing
-            # the memory to other work before the handoff kernel on `s` has read it
-            k.record_stream(s)
-            v.record_stream(s)
-            arr[i] = _lib.KvItem(k.data_ptr(), v.data_ptr(), lane, tokens, seq)
-            moved += (layer1 - layer0) * 2 * peer.NKV * tokens * peer.HD * 2
-        with torch.cuda.device(self.device):
-            _lib.call("rngd_kv_handoff_batch", arr, len(reqs), stride, ctypes.c_void_p(peer.k),
-                      ctypes.c_void_p(peer.v), peer.L, peer.NKV, peer.S, peer.HD, peer.Bcap, layer0, layer1,
-                      _lib.ptr(self._counter(s)), ctypes.c_void_p(peer.flags), _lib.stream_handle(s))
+        with self._lock:
+            arr = self._items
+            if arr is None:
+                arr = self._items = (_lib.KvItem * _lib.KV_MAX_BATCH)()
+            moved = 0
+            for i, (lane, seq, k_ptr, v_ptr, tokens, *owners) in enumerate(reqs):
+                tokens = peer.S if tokens is None else int(tokens)
+                # the caller may drop its cache right after this call: keep the allocator from
+                # handing the memory to other work before the handoff kernel on `s` has read it
+                for t in owners:
+                    t.record_stream(s)
+                it = arr[i]
+                it.src_k, it.src_v, it.lane, it.tokens, it.seq = k_ptr, v_ptr, lane, tokens, seq
+                moved += (layer1 - layer0) * 2 * peer.NKV * tokens * peer.HD * 2
+            args = (arr, len(reqs), stride, ctypes.c_void_p(peer.k), ctypes.c_void_p(peer.v), peer.L, peer.NKV,
+                    peer.S, peer.HD, peer.Bcap, layer0, layer1, _lib.ptr(self._counter(s)),
+                    ctypes.c_void_p(peer.flags), _lib.stream_handle(s))
+            if torch.cuda.current_device() == self.device.index:
+                _lib.call("rngd_kv_handoff_batch", *args)
+            else:
+                with torch.cuda.device(self.device):
+                    _lib.call("rngd_kv_handoff_batch", *args)
         return moved
 
     def record(self, seconds, nbytes):

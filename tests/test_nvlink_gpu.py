@@ -328,3 +328,24 @@ def test_ipc_cache_allocation_is_usable_by_the_engine():
     dec.step([1, 2], [0, 5], Kd, Vd)
     assert torch.isfinite(dec.logits_bv()).all()
     t.close()
+
+
+def test_push_many_with_a_layer_block_and_wait_all(rx):
+    """push_many of three requests in one launch -- a whole cache, another whole cache, and a
+    layer block [1, 3) of a third -- lands byte-exact; wait_all sees all three with one flag
+    read per poll, and a request whose layers have not all landed is not reported as arrived."""
+    t, K, V = rx
+    kv = [_kv(20 + i) for i in range(3)]
+    for i in range(3):
+        t.reserve(f"m{i}", i)
+    blk = kv[2][1:3].contiguous()
+    t.push_many([("m0", kv[0], None), ("m1", kv[1], None)])
+    t.push_many([("m2", blk, None)], layer0=1, layer1=3)
+    t.wait_all(["m0", "m1"], timeout=5)
+    t.wait_all(["m2"], layer0=1, layer1=3, timeout=5)
+    assert not t.arrived_all(["m0", "m2"])             # m2's layers 0 and 3 were never pushed
+    for i in range(2):
+        assert torch.equal(_bits(K[:, i]), _bits(kv[i][:, 0])) and torch.equal(_bits(V[:, i]), _bits(kv[i][:, 1]))
+    assert torch.equal(_bits(K[1:3, 2]), _bits(blk[:, 0])) and not K[0, 2].any() and not K[3, 2].any()
+    with pytest.raises(TimeoutError):
+        t.wait_all(["m2"], timeout=0.05)
