@@ -13,6 +13,7 @@ position's 128-dim key is one 256-byte row, which is what the attention
 kernel streams); the reference's K [NKV][HD][S] layout is used only at the
 host/connector boundary (load_kv, write_slot_kv, download_kv, upload_kv).
 """
+import ctypes
 import os
 
 import numpy as np
@@ -24,6 +25,20 @@ from rngd_pd.engines.weights import DeviceWeights
 BF = torch.bfloat16
 MAXB = 16          # lanes a single step kernel set handles
 ATTN_CHUNK = 128   # split-S chunk of the decode attention kernel
+
+
+class PrefillKV:
+    """A request's cache as a prefill engine leaves it on the device: kv bf16 [L][2][NKV][S][HD]
+    (K then V per layer, FullPrefillEngine.prefill_kv_device) and the prompt length `tokens`.
+    BatchDecodeEngine.write_slot_kv moves its positions [0, tokens) straight into a decode lane
+    with the handoff kernel (one launch per layer group, no relayout on the host or through
+    torch); positions past the prompt keep whatever the lane held, which no step reads before
+    the step at that position writes it."""
+
+    __slots__ = ("kv", "tokens")
+
+    def __init__(self, kv, tokens):
+        self.kv, self.tokens = kv, int(tokens)
 
 
 def greedy_tokens(logits, Vp, V, B):
@@ -107,6 +122,7 @@ class BatchDecodeEngine:
         self.use_graph = os.environ.get("RNGD_CUDA_GRAPH", "1") != "0"
         self._graphs = {}
         self._copied = torch.cuda.Event()
+        self._fill = None                     # lane-fill state: private flags, counter, item, sequence
         # embed + operand; per layer: QKV gemm, fused attention, O gemm, gate/up gemm, down gemm;
         # lm_head gemm, argmax finalize; advance
         self.launches_per_step = 2 + self.nl * 5 + 2 + 1
@@ -204,15 +220,52 @@ class BatchDecodeEngine:
     @_lib.on_device
     def write_slot_kv(self, Kd, Vd, idx, K, V):
         """Replace lane idx of the resident cache in place (engines/decode_batch.py:357-377).
-        K [nl, NKV, HD, S] / V [nl, NKV, S, HD]: host float32/bf16 or device tensors."""
+        K [nl, NKV, HD, S] / V [nl, NKV, S, HD]: host float32/bf16 or device tensors; or K a
+        PrefillKV (a prefill-layout cache on this device, V unused), moved by the handoff kernel."""
         if not 0 <= idx < self.B:
             raise IndexError(f"lane {idx} outside 0..{self.B - 1}")
+        if isinstance(K, PrefillKV):
+            return self._fill_lane(Kd, Vd, idx, K)
         Kt = (K if torch.is_tensor(K) else self._bf16_host(K)).to(self.dev, BF).transpose(-1, -2)
         Vt = (V if torch.is_tensor(V) else self._bf16_host(V)).to(self.dev, BF)
         for g in range(self.ngroups):
             sl = slice(g * self.NG, (g + 1) * self.NG)
             Kd[g][:, idx].copy_(Kt[sl])
             Vd[g][:, idx].copy_(Vt[sl])
+        return Kd, Vd
+
+    def _fill_lane(self, Kd, Vd, idx, pk):
+        """Positions [0, pk.tokens) of a prefill-layout cache into lane idx, on self.stream: one
+        rngd_kv_handoff_batch launch per layer group with this GPU's cache as the destination.
+        The kernel's layer flags go to a private array nobody waits on: the steps that read the
+        lane are queued after the fill on the same stream."""
+        c = self.cfg
+        kv, tokens = pk.kv, pk.tokens
+        want = (self.nl, 2, c.n_kv, self.S, c.head_dim)
+        if kv.dtype != BF or kv.device != self.dev or not kv.is_contiguous() or tuple(kv.shape) != want:
+            raise ValueError(f"PrefillKV: kv must be a contiguous bf16 {want} tensor on {self.dev}, "
+                             f"got {tuple(kv.shape)} {kv.dtype} on {kv.device}")
+        if not 1 <= tokens <= self.S:
+            raise ValueError(f"PrefillKV: {tokens} tokens outside 1..{self.S}")
+        self._check_cache(Kd, Vd)
+        if self._fill is None:
+            self._fill = {"flags": torch.zeros((self.B, self.NG), dtype=torch.int64, device=self.dev),
+                          "done": torch.zeros(_lib.KV_MAX_BATCH, dtype=torch.int32, device=self.dev),
+                          "item": (_lib.KvItem * 1)(), "seq": 0}
+        f = self._fill
+        f["seq"] += 1
+        s = self.stream
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        kv.record_stream(s)                   # the caller may drop kv before the fill has read it
+        plane = c.n_kv * self.S * c.head_dim  # elements of one layer's K (or V) block
+        h = _lib.stream_handle(s)
+        it = f["item"][0]
+        for g in range(self.ngroups):
+            base = kv.data_ptr() + g * self.NG * 2 * plane * 2
+            it.src_k, it.src_v, it.lane, it.tokens, it.seq = base, base + plane * 2, idx, tokens, f["seq"]
+            _lib.call("rngd_kv_handoff_batch", f["item"], 1, 2 * plane, ctypes.c_void_p(Kd[g].data_ptr()),
+                      ctypes.c_void_p(Vd[g].data_ptr()), self.NG, c.n_kv, self.S, c.head_dim, self.B, 0, self.NG,
+                      _lib.ptr(f["done"]), _lib.ptr(f["flags"]), h)
         return Kd, Vd
 
     @_lib.on_device

@@ -54,6 +54,11 @@ class _DevicePrefillStage:
         K, V = self.e.reference_layout(self.kv)
         return K, V, nxt
 
+    @_lib.on_device
+    def result_kv(self):
+        """(kv in the prefill layout [L][2][NKV][S][HD], next token), without a relayout."""
+        return self.kv, self.e._finish(self._b)
+
 
 class FullPrefillEngine:
     def __init__(self, cfg, sd, C=256, group=2, chip=0, cache_dir=None, S=0):

@@ -304,15 +304,19 @@ class ContinuousScheduler:
 
 class OneCardProducer:
     """Prefill on the decode card and hand the scheduler the device cache directly (the
-    reference's SoloWorker producers, serving/cluster.py:747-776)."""
+    reference's SoloWorker producers, serving/cluster.py:747-776).  The cache stays in the
+    prefill layout (a PrefillKV): the decode engine's write_slot_kv moves the prompt's positions
+    into the lane with the handoff kernel."""
 
     def __init__(self, prefill_engine):
         self.pre = prefill_engine
 
     def produce(self, item):
+        from rngd_pd.engines.decode_batch import PrefillKV
         t0 = time.perf_counter()
-        K, V, nxt = self.pre.prefill_device(item["tokens"])
-        return K, V, nxt, len(item["tokens"]), (time.perf_counter() - t0) * 1e3
+        P = len(item["tokens"])
+        kv, nxt = self.pre.prefill_kv_device(item["tokens"])
+        return PrefillKV(kv, P), None, nxt, P, (time.perf_counter() - t0) * 1e3
 
     def begin_produce(self, item):
         stage = self.pre.begin_device_prefill(item["tokens"])
@@ -324,8 +328,9 @@ class OneCardProducer:
                 return stage.advance(n)
 
             def result(self):
-                K, V, nxt = stage.result()
-                return K, V, nxt, P, (time.perf_counter() - t0) * 1e3
+                from rngd_pd.engines.decode_batch import PrefillKV
+                kv, nxt = stage.result_kv()
+                return PrefillKV(kv, P), None, nxt, P, (time.perf_counter() - t0) * 1e3
 
         return _Stage()
 

@@ -173,3 +173,30 @@ def _ordered(bits):
     """bf16 bit patterns -> integers whose differences count ulps across zero."""
     b = bits.astype(np.int32)
     return np.where(b & 0x8000, -(b & 0x7FFF), b)
+
+
+def test_prefill_kv_fills_a_lane_like_the_reference_layout_copy(small):
+    """write_slot_kv of a PrefillKV (the prefill-layout cache, moved by the handoff kernel on the
+    engine's stream) writes the prompt's positions of the lane bit for bit as the reference-layout
+    lane copy does, and leaves the lane's later positions and every other lane untouched."""
+    from rngd_pd.engines.decode_batch import BatchDecodeEngine, PrefillKV
+    eng, _ = small
+    dec = BatchDecodeEngine(eng.cfg, eng.w, B=3, S=eng.S, group=1)
+    P = 150
+    toks = [(17 * i + 3) % SMALL.V for i in range(P)]
+    kv, _nxt = eng.prefill_kv_device(toks)
+    K, V = eng.reference_layout(kv)
+    Ka, Va = dec.blank_kv()
+    Kb, Vb = dec.blank_kv()
+    for t in Ka + Va + Kb + Vb:
+        t.fill_(7.0)                                   # what an earlier request left behind
+    dec.write_slot_kv(Ka, Va, 1, K, V)
+    dec.write_slot_kv(Kb, Vb, 1, PrefillKV(kv, P), None)
+    torch.cuda.synchronize()
+    bits = lambda t: t.contiguous().view(torch.int16)
+    for ga, gb in zip(Ka + Va, Kb + Vb):
+        assert torch.equal(bits(ga[:, 1, :, :P]), bits(gb[:, 1, :, :P]))
+        assert bool((gb[:, 1, :, P:] == 7.0).all())
+        assert bool((gb[:, 0] == 7.0).all()) and bool((gb[:, 2] == 7.0).all())
+    with pytest.raises(ValueError):
+        dec.write_slot_kv(Kb, Vb, 0, PrefillKV(kv[:1].contiguous(), P), None)   # wrong shape
