@@ -136,435 +136,501 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// ------------------------------------------------------------------ the GEMM's three roles
+// Shared-memory layout of a GEMM CTA (the same for every phase of a fused launch).
+struct Ring {
+  uint8_t* sA;
+  uint8_t* sB;
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* acc_full;   // [2]
+  uint64_t* acc_empty;  // [2]
+  uint64_t* epi_done;   // the epilogue threads are past their last TMEM read
+  uint32_t* tmem_slot;
+  float* s_scale;       // [16]
+  int* s_pos;           // [16]
+  int* s_lane;          // [16] cache lane of each stream
+  float* ys;
+  unsigned long long* s_red;  // [4][16]
+};
+
+__device__ __forceinline__ Ring ring_layout(uint8_t* smem_raw) {
+  Ring R;
+  uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  R.sA = base;
+  R.sB = base + STAGES * A_BYTES;
+  R.full = (uint64_t*)(R.sB + STAGES * B_BYTES);
+  R.empty = R.full + STAGES;
+  R.acc_full = R.empty + STAGES;
+  R.acc_empty = R.acc_full + 2;
+  R.epi_done = R.acc_empty + 2;
+  uint8_t* tail = (uint8_t*)R.full + kBarBytes;
+  R.tmem_slot = (uint32_t*)tail;
+  R.s_scale = (float*)(tail + 64);
+  R.s_pos = (int*)(tail + 128);
+  R.s_lane = (int*)(tail + 192);
+  R.ys = (float*)(tail + 256);
+  R.s_red = (unsigned long long*)(R.ys + BM * YS_LD);
+  return R;
+}
+
+// Barrier init (thread 0) and TMEM allocation (warp 1), then a CTA-wide sync.  Returns the
+// TMEM base of the two accumulators.
+__device__ __forceinline__ uint32_t ring_setup(const Ring& R) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&R.full[s], 1);
+      mbar_init(&R.empty[s], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&R.acc_full[i], 1);
+      mbar_init(&R.acc_empty[i], EPI_THREADS);
+    }
+    mbar_init(R.epi_done, EPI_THREADS);
+    fence_mbar_init();
+  }
+  if ((threadIdx.x >> 5) == 1) {
+    tmem_alloc(R.tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  return *R.tmem_slot;
+}
+
+// TMA loads of one GEMM's k-steps [f0, f1) through the ring, from ring position i on (the
+// positions continue across the phases of a fused launch).  The weight tiles of the first
+// min(f1 - f0, STAGES) steps are requested as soon as their ring slots are free and before
+// wait_operand(): weights never depend on earlier work, so they stream while the previous
+// kernel or phase finishes.  The operand tiles follow wait_operand().  Returns the ring
+// position after the phase, or -1 when a bounded wait gave up (the status word is set).
+template <class WaitOperand>
+__device__ __forceinline__ long produce_phase(const CUtensorMap* tmW, const CUtensorMap* tmX, const GemmArgs& a,
+                                              const Ring& R, long i, long f0, long f1, WaitOperand wait_operand) {
+  const long nk = f1 - f0;
+  const long pre = nk < STAGES ? nk : STAGES;
+  long issued = 0;
+  for (; issued < pre; issued++) {
+    const long q = i + issued;
+    const int s = (int)(q % STAGES);
+    if (!mbar_wait(&R.empty[s], ((uint32_t)(q / STAGES) & 1u) ^ 1u, ST_TMA_WAIT, &g_status_decode)) break;
+    const long f = f0 + issued;
+    const int tile = (int)(f / a.nkb), kb = (int)(f - (long)tile * a.nkb);
+    mbar_arrive_expect_tx(&R.full[s], A_BYTES + B_BYTES);
+    tma_load_3d(R.sA + s * A_BYTES, tmW, &R.full[s], kb * BK, tile * BM, a.layer);
+  }
+  wait_operand();
+  for (long j = 0; j < issued; j++) {
+    const int s = (int)((i + j) % STAGES);
+    tma_load_2d(R.sB + s * B_BYTES, tmX, &R.full[s], (int)((f0 + j) % a.nkb) * BK, 0);
+  }
+  if (issued < pre) return -1;
+  for (long j = pre; j < nk; j++) {
+    const long q = i + j;
+    const int s = (int)(q % STAGES);
+    if (!mbar_wait(&R.empty[s], ((uint32_t)(q / STAGES) & 1u) ^ 1u, ST_TMA_WAIT, &g_status_decode)) return -1;
+    const long f = f0 + j;
+    const int tile = (int)(f / a.nkb), kb = (int)(f - (long)tile * a.nkb);
+    mbar_arrive_expect_tx(&R.full[s], A_BYTES + B_BYTES);
+    tma_load_3d(R.sA + s * A_BYTES, tmW, &R.full[s], kb * BK, tile * BM, a.layer);
+    tma_load_2d(R.sB + s * B_BYTES, tmX, &R.full[s], kb * BK, 0);
+  }
+  return i + nk;
+}
+
+// MMAs of one GEMM's k-steps [f0, f1): 4 x (128x32x16) per K block into the segment's TMEM
+// accumulator; the ring position i and the segment count seg continue across phases.
+__device__ __forceinline__ bool mma_phase(const GemmArgs& a, const Ring& R, uint32_t tmem, long& i, int& seg,
+                                          long f0, long f1, unsigned long long* tr) {
+  const uint32_t idesc = idesc_bf16_f32(BM, BNC);
+  bool ok = true;
+  for (long f = f0; f < f1 && ok; seg++) {
+    const int tile = (int)(f / a.nkb);
+    const long fend = ((long)tile + 1) * a.nkb < f1 ? ((long)tile + 1) * a.nkb : f1;
+    const int buf = seg & 1;
+    const uint32_t aph = (uint32_t)(seg >> 1) & 1u;
+    ok = mbar_wait(&R.acc_empty[buf], aph ^ 1u, ST_MMA_WAIT, &g_status_decode);
+    tc_fence_after();
+    const uint32_t d = tmem + (uint32_t)(buf * BNC);
+    for (long g = f; g < fend && ok; g++, i++) {
+      const int s = (int)(i % STAGES);
+      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+      ok = mbar_wait(&R.full[s], ph, ST_MMA_WAIT, &g_status_decode);
+      if (!ok) break;
+      if (tr != nullptr && g + 1 == f1) tr[3] = globaltimer();
+      tc_fence_after();
+      const uint32_t aBase = smem_u32(R.sA + s * A_BYTES), bBase = smem_u32(R.sB + s * B_BYTES);
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; kk++)
+        umma_bf16(d, sw128_kmajor_desc(aBase + kk * 32), sw128_kmajor_desc(bBase + kk * 32), idesc,
+                  (g != f || kk != 0) ? 1u : 0u);
+      umma_commit(&R.empty[s]);
+    }
+    umma_commit(&R.acc_full[buf]);
+    f = fend;
+  }
+  return ok;
+}
+
+// Epilogue of one GEMM's k-steps [f0, f1) on the 256 epilogue threads: two warpgroups over
+// the same 128 TMEM lanes; thread (group g, row r) owns row r of the tile (TMEM lane r) for the
+// streams 8g .. 8g+7, which halves each thread's serial work on the GEMM's tail.  The caller
+// has already waited for the data the GEMM consumes (the previous kernel or phase).  seg
+// continues across phases.  Values other CTAs write earlier in the same launch (x, the sums of
+// squares) are read with L1-bypassing loads.
+template <int EPI>
+__device__ __forceinline__ void epilogue_phase(const GemmArgs& a, const Ring& R, uint32_t tmem, int& seg, long f0,
+                                               long f1, unsigned long long* tr) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int r = ((warp & 3) << 5) | lane;
+  const int ep = threadIdx.x - 64;   // 0..255 among the epilogue threads
+  const int sb = (ep >> 7) * SPG;    // first stream of this thread's group
+  // Per-launch constants, read once with independent loads: a chain of dependent global
+  // loads inside each segment's epilogue was most of the GEMM's tail.  The RMS sums are
+  // added in the same order as ever (t = 0, 1, ...), so the scale is bit-identical.
+  if (EPI != EPI_RESID && a.ss_in != nullptr && ep < MAXB) {
+    float ssum = 0.f;
+    for (int t0 = 0; t0 < a.ss_tiles; t0 += 16) {
+      float v16[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) v16[j] = t0 + j < a.ss_tiles ? __ldcg(a.ss_in + (t0 + j) * MAXB + ep) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+        if (t0 + j < a.ss_tiles) ssum += v16[j];
+    }
+    R.s_scale[ep] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
+  }
+  // RoPE factors of this step for this thread's frequency (r mod 64) and streams, computed
+  // while the weights stream rather than on the GEMM's tail
+  float rcos[SPG], rsin[SPG];
+  if constexpr (EPI == EPI_QKV) {
+    if (ep < MAXB) {
+      R.s_pos[ep] = ep < a.B ? a.pos[ep] : -1;
+      R.s_lane[ep] = ep < a.B ? (a.lanes != nullptr ? a.lanes[ep] : ep) : 0;
+    }
+    const float invf = a.inv[r & 63];
+#pragma unroll
+    for (int i = 0; i < SPG; i++) {
+      const int p = sb + i < a.B ? a.pos[sb + i] : -1;
+      sincosf((float)p * invf, &rsin[i], &rcos[i]);
+    }
+  }
+  epi_sync();
+  for (long f = f0; f < f1; seg++) {
+    const int tile = (int)(f / a.nkb);
+    const long tstart = (long)tile * a.nkb;
+    const long fend = tstart + a.nkb < f1 ? tstart + a.nkb : f1;
+    const int buf = seg & 1;
+    const int n = tile * BM + r;
+    // the residual row and norm weight do not depend on this GEMM: fetch them while the
+    // accumulator is still being computed (only the tile's reducing CTA writes x[.][n])
+    float xo[SPG];
+    float wn = 0.f;
+    // epoch of the tile's split (read before the accumulator wait; only the tile's first owner
+    // advances it, after every piece of this launch was stored under the value read here)
+    const int epoch = a.maxseg > 1 ? __ldcg(a.counters + tile) : 0;
+    if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+      for (int i = 0; i < SPG; i++) xo[i] = sb + i < a.B ? __ldcg(a.x + (size_t)(sb + i) * a.ldx + n) : 0.f;
+      if (a.act_next != nullptr) wn = a.w_next[n];
+    }
+    const int first = owner_of(tstart, a.total, G), last = owner_of(tstart + a.nkb - 1, a.total, G);
+    const int nseg = last - first + 1;
+    const int slot = cta - first;
+    // piece layout [stream pair][row][2 words]: the 32 rows of a warp read or write 512
+    // contiguous bytes per instruction.  This thread's pairs are sb/2 .. sb/2 + SPG/2 - 1.
+    constexpr size_t kPieceWords = (size_t)BM * MAXB;
+    constexpr size_t kPairWords = (size_t)BM * 2;
+    unsigned long long* pw = reinterpret_cast<unsigned long long*>(a.partial) +
+                             (size_t)tile * a.maxseg * kPieceWords + ((size_t)(sb / 2) * BM + r) * 2;
+    // a tile's first owner reads the first batch of later pieces while its own accumulator is
+    // still being computed: pieces already stored cost no round trip after it
+    unsigned long long w[kRedBatch][SPG];
+    if (nseg > 1 && slot == 0) {
+#pragma unroll
+      for (int q = 0; q < kRedBatch; q++) {
+        if (1 + q < nseg) {
+#pragma unroll
+          for (int j = 0; j < SPG / 2; j++)
+            ld_piece(pw + (size_t)(1 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
+        }
+      }
+    }
+    mbar_wait(&R.acc_full[buf], (uint32_t)(seg >> 1) & 1u, ST_EPI_WAIT, &g_status_decode);
+    if (tr != nullptr && ep == 0 && fend == f1) tr[5] = globaltimer();
+    __syncwarp();
+    tc_fence_after();
+    float vh[SPG], vl[SPG];  // the hi and lo operand columns of this group's streams
+    const uint32_t tb = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * BNC);
+    tmem_ld_32x32b_2x8(tb + sb, tb + MAXB + sb, vh, vl);
+    tc_fence_before();
+    mbar_arrive(&R.acc_empty[buf]);
+    const bool tlast = tr != nullptr && ep == 0 && fend == f1;
+    if (tlast) tr[8] = globaltimer();
+    float y[SPG];
+#pragma unroll
+    for (int i = 0; i < SPG; i++) y[i] = vh[i] + vl[i];
+
+    bool run = true;
+    if (nseg > 1) {
+      const uint32_t flag = ((uint32_t)a.tag << 28) | ((uint32_t)(epoch + 1) & 0x0FFFFFFFu);
+      if (slot > 0) {
+        // a later piece of the tile: publish it, no wait
+        unsigned long long* dst = pw + (size_t)slot * kPieceWords;
+#pragma unroll
+        for (int j = 0; j < SPG / 2; j++) st_piece(dst + j * kPairWords, flag, y[2 * j], y[2 * j + 1]);
+        run = false;
+      } else {
+        // the tile's first piece is this CTA's own: wait (bounded) until all of this thread's
+        // words of the later pieces carry the flag, re-reading every missing piece together
+        // (one L2 round trip per poll, not per piece), then add them in K order
+        bool ok = true;
+        for (int s0 = 1; s0 < nseg; s0 += kRedBatch) {
+          uint32_t pend = 0;
+#pragma unroll
+          for (int q = 0; q < kRedBatch; q++) {
+            if (s0 + q < nseg) {
+              pend |= 1u << q;
+              if (s0 > 1) {  // the first batch was read before the accumulator wait
+#pragma unroll
+                for (int j = 0; j < SPG / 2; j++)
+                  ld_piece(pw + (size_t)(s0 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
+              }
+            }
+          }
+          uint64_t t0 = 0;
+          int polls = 0;
+          while (true) {
+#pragma unroll
+            for (int q = 0; q < kRedBatch; q++) {
+              if (pend & (1u << q)) {
+                bool ready = true;
+#pragma unroll
+                for (int i = 0; i < SPG; i++) ready &= (uint32_t)(w[q][i] >> 32) == flag;
+                if (ready) pend &= ~(1u << q);
+              }
+            }
+            if (pend == 0 || !ok) break;
+            polls++;
+            const uint64_t now = globaltimer();
+            if (t0 == 0) {
+              t0 = now;
+            } else if (now - t0 > kWaitTimeoutNs) {
+              atomicCAS(&g_status_decode, 0, ST_PIECE_WAIT);
+              ok = false;
+              break;
+            }
+#pragma unroll
+            for (int q = 0; q < kRedBatch; q++) {
+              if (pend & (1u << q)) {
+#pragma unroll
+                for (int j = 0; j < SPG / 2; j++)
+                  ld_piece(pw + (size_t)(s0 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
+              }
+            }
+          }
+          if (tlast) tr[9] = (unsigned long long)polls;
+#pragma unroll
+          for (int q = 0; q < kRedBatch; q++) {
+            if (s0 + q < nseg) {
+#pragma unroll
+              for (int i = 0; i < SPG; i++) y[i] += __uint_as_float((uint32_t)w[q][i]);
+            }
+          }
+        }
+        // every piece of this launch is in: the next launch uses the next epoch
+        if (ep == 0) a.counters[tile] = epoch + 1;
+        if (tlast) tr[10] = globaltimer();
+      }
+    }
+    if (run) {
+      if (EPI != EPI_RESID && a.ss_in != nullptr) {
+#pragma unroll
+        for (int i = 0; i < SPG; i++) y[i] *= R.s_scale[sb + i];
+      }
+      if constexpr (EPI == EPI_RESID) {
+        // every stream of the group is computed (streams >= B hold zeros) so the per-stream
+        // chains interleave; only the stores are predicated on B
+        float xs[SPG];
+#pragma unroll
+        for (int i = 0; i < SPG; i++) {
+          xs[i] = xo[i] + y[i];
+          if (sb + i < a.B) a.x[(size_t)(sb + i) * a.ldx + n] = xs[i];
+        }
+        if (tlast) tr[13] = globaltimer();
+        if (a.act_next != nullptr) {
+#pragma unroll
+          for (int i = 0; i < SPG; i++) {
+            const float h = xs[i] * wn;
+            const uint16_t hi = f2bf_bits(h);
+            const uint16_t lo = f2bf_bits(h - bf2f(hi));
+            if (sb + i < a.B) {
+              a.act_next[(size_t)(sb + i) * a.ld_next + n] = hi;
+              a.act_next[(size_t)(MAXB + sb + i) * a.ld_next + n] = lo;
+            }
+          }
+          if (tlast) tr[14] = globaltimer();
+          // per-tile sum of squares of the new x: the same xor butterfly for every stream,
+          // the group's 8 interleaved
+          float sq[SPG];
+#pragma unroll
+          for (int i = 0; i < SPG; i++) sq[i] = xs[i] * xs[i];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int i = 0; i < SPG; i++) sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], o);
+          }
+          if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < SPG; i++) R.ys[(warp & 3) * YS_LD + sb + i] = sq[i];
+          }
+          if (tlast) tr[15] = globaltimer();
+          epi_sync();
+          if (ep < a.B) {
+            const float t4 = (R.ys[0 * YS_LD + ep] + R.ys[1 * YS_LD + ep]) + (R.ys[2 * YS_LD + ep] + R.ys[3 * YS_LD + ep]);
+            a.ss_out[tile * MAXB + ep] = t4;
+          }
+        }
+      } else if constexpr (EPI == EPI_QKV) {
+#pragma unroll
+        for (int i = 0; i < SPG; i++) R.ys[r * YS_LD + sb + i] = y[i];
+        epi_sync();
+        const int head = tile;  // one 128-row tile = one head
+        const bool lo_half = r < 64;
+        const int partner = r ^ 64;
+        if (head < a.NH + a.NKV) {
+          if (tlast) tr[13] = globaltimer();
+          float o[SPG];
+#pragma unroll
+          for (int i = 0; i < SPG; i++) {  // all streams (pos -1 past B), stores predicated
+            const float other = R.ys[partner * YS_LD + sb + i];
+            o[i] = lo_half ? y[i] * rcos[i] - other * rsin[i] : y[i] * rcos[i] + other * rsin[i];
+          }
+          if (tlast) tr[14] = globaltimer();
+#pragma unroll
+          for (int i = 0; i < SPG; i++) {
+            const int b = sb + i, p = R.s_pos[b];
+            if (b < a.B) {
+              if (head < a.NH) {
+                a.q[(size_t)b * a.ldq + n] = o[i];
+              } else if (p >= 0 && p < a.S) {
+                a.kc[(((size_t)R.s_lane[b] * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o[i]);
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < SPG; i++) {
+            const int b = sb + i, p = R.s_pos[b];
+            if (b < a.B && p >= 0 && p < a.S)
+              a.vc[(((size_t)R.s_lane[b] * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[i]);
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll
+        for (int i = 0; i < SPG; i++) R.ys[r * YS_LD + sb + i] = y[i];
+        epi_sync();
+        if (r < 64) {
+          const int fcol = tile * 64 + r;
+#pragma unroll
+          for (int i = 0; i < SPG; i++) {
+            const float g = y[i], u = R.ys[(r + 64) * YS_LD + sb + i];
+            const float act = g / (1.0f + expf(-g)) * u;
+            const uint16_t hi = f2bf_bits(act);
+            const uint16_t lo = f2bf_bits(act - bf2f(hi));
+            if (sb + i < a.B) {
+              a.act_out[(size_t)(sb + i) * a.ld_act + fcol] = hi;
+              a.act_out[(size_t)(MAXB + sb + i) * a.ld_act + fcol] = lo;
+            }
+          }
+        }
+      } else if constexpr (EPI == EPI_LOGITS) {
+        unsigned long long key[SPG];
+#pragma unroll
+        for (int i = 0; i < SPG; i++) {
+          key[i] = 0;
+          if (n < a.V) {
+            if (sb + i < a.B) a.logits[(size_t)(sb + i) * a.V + n] = y[i];
+            key[i] = ((unsigned long long)orderable(y[i]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+          for (int i = 0; i < SPG; i++) {
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, key[i], o);
+            key[i] = t > key[i] ? t : key[i];
+          }
+        }
+        if (lane == 0) {
+#pragma unroll
+          for (int i = 0; i < SPG; i++) R.s_red[(warp & 3) * MAXB + sb + i] = key[i];
+        }
+        epi_sync();
+        if (ep < a.B) {
+          unsigned long long k = R.s_red[ep];
+          for (int w = 1; w < 4; w++) k = R.s_red[w * MAXB + ep] > k ? R.s_red[w * MAXB + ep] : k;
+          atomicMax(&a.best[ep], k);
+        }
+      }
+      if (tlast) tr[11] = globaltimer();
+      epi_sync();  // R.ys / R.s_red are reused by the next segment
+      if (tlast) tr[12] = globaltimer();
+    }
+    f = fend;
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1) skgemm_kernel(const __grid_constant__ CUtensorMap tmW,
                                                             const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = base;
-  uint8_t* sB = sA + STAGES * A_BYTES;
-  uint64_t* full = (uint64_t*)(sB + STAGES * B_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;   // [2]
-  uint64_t* acc_empty = acc_full + 2;    // [2]
-  uint64_t* epi_done = acc_empty + 2;    // the 128 epilogue threads are past their last TMEM read
-  uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + kBarBytes);
-  float* s_scale = (float*)((uint8_t*)full + kBarBytes + 64);  // [16]
-  int* s_pos = (int*)((uint8_t*)full + kBarBytes + 128);       // [16]
-  int* s_lane = (int*)((uint8_t*)full + kBarBytes + 192);      // [16] cache lane of each stream
-  float* ys = (float*)((uint8_t*)full + kBarBytes + 256);
-  unsigned long long* s_red = (unsigned long long*)(ys + BM * YS_LD);  // [4][16]
-
+  const Ring R = ring_layout(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   const long f0 = (long)cta * a.total / G, f1 = (long)(cta + 1) * a.total / G;
   // RNGD_TRACE == 0 (the product build): tr is a constant null and every stamp below folds away
   unsigned long long* tr = (RNGD_TRACE && a.trace != nullptr) ? a.trace + (size_t)cta * 16 : nullptr;
   if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer();
-
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int i = 0; i < 2; i++) {
-      mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], EPI_THREADS);
-    }
-    mbar_init(epi_done, EPI_THREADS);
-    fence_mbar_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
   }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = ring_setup(R);
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer
-      const long nk = f1 - f0;
-      const long pre = nk < STAGES ? nk : STAGES;
-      // weights do not depend on the previous kernel: start streaming them now
-      for (long i = 0; i < pre; i++) {
-        const long f = f0 + i;
-        const int tile = (int)(f / a.nkb), kb = (int)(f - (long)tile * a.nkb);
-        mbar_arrive_expect_tx(&full[i], A_BYTES + B_BYTES);
-        tma_load_3d(sA + i * A_BYTES, &tmW, &full[i], kb * BK, tile * BM, a.layer);
-      }
-      grid_dep_wait();  // the activation operand is written by the previous kernel
-      if (tr != nullptr) tr[1] = globaltimer();
-      for (long i = 0; i < pre; i++) {
-        const long f = f0 + i;
-        const int kb = (int)(f % a.nkb);
-        tma_load_2d(sB + i * B_BYTES, &tmX, &full[i], kb * BK, 0);
-      }
-      for (long i = pre; i < nk; i++) {
-        const int s = (int)(i % STAGES);
-        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, ST_TMA_WAIT, &g_status_decode)) break;
-        const long f = f0 + i;
-        const int tile = (int)(f / a.nkb), kb = (int)(f - (long)tile * a.nkb);
-        mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
-        tma_load_3d(sA + s * A_BYTES, &tmW, &full[s], kb * BK, tile * BM, a.layer);
-        tma_load_2d(sB + s * B_BYTES, &tmX, &full[s], kb * BK, 0);
-      }
+      // the activation operand is written by the previous kernel
+      produce_phase(&tmW, &tmX, a, R, 0, f0, f1, [&] {
+        grid_dep_wait();
+        if (tr != nullptr) tr[1] = globaltimer();
+      });
       if (tr != nullptr) tr[2] = globaltimer();
       grid_dep_launch();  // all weight reads issued: the next kernel may start prefetching
-
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---------------- MMA issuer: 4 x (128x32x16) per K block into the segment's accumulator
-      const uint32_t idesc = idesc_bf16_f32(BM, BNC);
       long i = 0;
       int seg = 0;
-      bool ok = true;
-      for (long f = f0; f < f1 && ok; seg++) {
-        const int tile = (int)(f / a.nkb);
-        const long fend = ((long)tile + 1) * a.nkb < f1 ? ((long)tile + 1) * a.nkb : f1;
-        const int buf = seg & 1;
-        const uint32_t aph = (uint32_t)(seg >> 1) & 1u;
-        ok = mbar_wait(&acc_empty[buf], aph ^ 1u, ST_MMA_WAIT, &g_status_decode);
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * BNC);
-        for (long g = f; g < fend && ok; g++, i++) {
-          const int s = (int)(i % STAGES);
-          const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-          ok = mbar_wait(&full[s], ph, ST_MMA_WAIT, &g_status_decode);
-          if (!ok) break;
-          if (tr != nullptr && g + 1 == f1) tr[3] = globaltimer();
-          tc_fence_after();
-          const uint32_t aBase = smem_u32(sA + s * A_BYTES), bBase = smem_u32(sB + s * B_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; kk++)
-            umma_bf16(d, sw128_kmajor_desc(aBase + kk * 32), sw128_kmajor_desc(bBase + kk * 32), idesc,
-                      (g != f || kk != 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
-        }
-        umma_commit(&acc_full[buf]);
-        f = fend;
-      }
+      mma_phase(a, R, tmem, i, seg, f0, f1, tr);
       if (tr != nullptr) tr[4] = globaltimer();
       // TMEM is freed below only after every epilogue thread has read its last accumulator
-      mbar_wait(epi_done, 0u, ST_EPI_WAIT, &g_status_decode);
+      mbar_wait(R.epi_done, 0u, ST_EPI_WAIT, &g_status_decode);
       tc_fence_after();
       if (tr != nullptr) tr[7] = globaltimer();
     }
     __syncwarp();
     tmem_dealloc(tmem, TMEM_COLS);
   } else {
-    // ---------------- epilogue warps 2..9: two warpgroups over the same 128 TMEM lanes.  Thread
-    // (group g, row r) owns row r of the tile (TMEM lane r) for the streams 8g .. 8g+7, which
-    // halves each thread's serial work on the GEMM's tail.
     grid_dep_wait();
-    const int r = ((warp & 3) << 5) | lane;
-    const int ep = threadIdx.x - 64;   // 0..255 among the epilogue threads
-    const int sb = (ep >> 7) * SPG;    // first stream of this thread's group
-    // Per-launch constants, read once with independent loads: a chain of dependent global
-    // loads inside each segment's epilogue was most of the GEMM's tail.  The RMS sums are
-    // added in the same order as ever (t = 0, 1, ...), so the scale is bit-identical.
-    if (EPI != EPI_RESID && a.ss_in != nullptr && ep < MAXB) {
-      float ssum = 0.f;
-      for (int t0 = 0; t0 < a.ss_tiles; t0 += 16) {
-        float v16[16];
-#pragma unroll
-        for (int j = 0; j < 16; j++) v16[j] = t0 + j < a.ss_tiles ? a.ss_in[(t0 + j) * MAXB + ep] : 0.f;
-#pragma unroll
-        for (int j = 0; j < 16; j++)
-          if (t0 + j < a.ss_tiles) ssum += v16[j];
-      }
-      s_scale[ep] = 1.0f / sqrtf(ssum * a.inv_h + a.eps);
-    }
-    // RoPE factors of this step for this thread's frequency (r mod 64) and streams, computed
-    // while the weights stream rather than on the GEMM's tail
-    float rcos[SPG], rsin[SPG];
-    if constexpr (EPI == EPI_QKV) {
-      if (ep < MAXB) {
-        s_pos[ep] = ep < a.B ? a.pos[ep] : -1;
-        s_lane[ep] = ep < a.B ? (a.lanes != nullptr ? a.lanes[ep] : ep) : 0;
-      }
-      const float invf = a.inv[r & 63];
-#pragma unroll
-      for (int i = 0; i < SPG; i++) {
-        const int p = sb + i < a.B ? a.pos[sb + i] : -1;
-        sincosf((float)p * invf, &rsin[i], &rcos[i]);
-      }
-    }
-    epi_sync();
     int seg = 0;
-    for (long f = f0; f < f1; seg++) {
-      const int tile = (int)(f / a.nkb);
-      const long tstart = (long)tile * a.nkb;
-      const long fend = tstart + a.nkb < f1 ? tstart + a.nkb : f1;
-      const int buf = seg & 1;
-      const int n = tile * BM + r;
-      // the residual row and norm weight do not depend on this GEMM: fetch them while the
-      // accumulator is still being computed (only the tile's reducing CTA writes x[.][n])
-      float xo[SPG];
-      float wn = 0.f;
-      // epoch of the tile's split (read before the accumulator wait; only the tile's first owner
-      // advances it, after every piece of this launch was stored under the value read here)
-      const int epoch = a.maxseg > 1 ? __ldcg(a.counters + tile) : 0;
-      if constexpr (EPI == EPI_RESID) {
-#pragma unroll
-        for (int i = 0; i < SPG; i++) xo[i] = sb + i < a.B ? a.x[(size_t)(sb + i) * a.ldx + n] : 0.f;
-        if (a.act_next != nullptr) wn = a.w_next[n];
-      }
-      const int first = owner_of(tstart, a.total, G), last = owner_of(tstart + a.nkb - 1, a.total, G);
-      const int nseg = last - first + 1;
-      const int slot = cta - first;
-      // piece layout [stream pair][row][2 words]: the 32 rows of a warp read or write 512
-      // contiguous bytes per instruction.  This thread's pairs are sb/2 .. sb/2 + SPG/2 - 1.
-      constexpr size_t kPieceWords = (size_t)BM * MAXB;
-      constexpr size_t kPairWords = (size_t)BM * 2;
-      unsigned long long* pw = reinterpret_cast<unsigned long long*>(a.partial) +
-                               (size_t)tile * a.maxseg * kPieceWords + ((size_t)(sb / 2) * BM + r) * 2;
-      // a tile's first owner reads the first batch of later pieces while its own accumulator is
-      // still being computed: pieces already stored cost no round trip after it
-      unsigned long long w[kRedBatch][SPG];
-      if (nseg > 1 && slot == 0) {
-#pragma unroll
-        for (int q = 0; q < kRedBatch; q++) {
-          if (1 + q < nseg) {
-#pragma unroll
-            for (int j = 0; j < SPG / 2; j++)
-              ld_piece(pw + (size_t)(1 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
-          }
-        }
-      }
-      mbar_wait(&acc_full[buf], (uint32_t)(seg >> 1) & 1u, ST_EPI_WAIT, &g_status_decode);
-      if (tr != nullptr && ep == 0 && fend == f1) tr[5] = globaltimer();
-      __syncwarp();
-      tc_fence_after();
-      float vh[SPG], vl[SPG];  // the hi and lo operand columns of this group's streams
-      const uint32_t tb = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(buf * BNC);
-      tmem_ld_32x32b_2x8(tb + sb, tb + MAXB + sb, vh, vl);
-      tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
-      const bool tlast = tr != nullptr && ep == 0 && fend == f1;
-      if (tlast) tr[8] = globaltimer();
-      float y[SPG];
-#pragma unroll
-      for (int i = 0; i < SPG; i++) y[i] = vh[i] + vl[i];
-
-      bool run = true;
-      if (nseg > 1) {
-        const uint32_t flag = ((uint32_t)a.tag << 28) | ((uint32_t)(epoch + 1) & 0x0FFFFFFFu);
-        if (slot > 0) {
-          // a later piece of the tile: publish it, no wait
-          unsigned long long* dst = pw + (size_t)slot * kPieceWords;
-#pragma unroll
-          for (int j = 0; j < SPG / 2; j++) st_piece(dst + j * kPairWords, flag, y[2 * j], y[2 * j + 1]);
-          run = false;
-        } else {
-          // the tile's first piece is this CTA's own: wait (bounded) until all of this thread's
-          // words of the later pieces carry the flag, re-reading every missing piece together
-          // (one L2 round trip per poll, not per piece), then add them in K order
-          bool ok = true;
-          for (int s0 = 1; s0 < nseg; s0 += kRedBatch) {
-            uint32_t pend = 0;
-#pragma unroll
-            for (int q = 0; q < kRedBatch; q++) {
-              if (s0 + q < nseg) {
-                pend |= 1u << q;
-                if (s0 > 1) {  // the first batch was read before the accumulator wait
-#pragma unroll
-                  for (int j = 0; j < SPG / 2; j++)
-                    ld_piece(pw + (size_t)(s0 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
-                }
-              }
-            }
-            uint64_t t0 = 0;
-            int polls = 0;
-            while (true) {
-#pragma unroll
-              for (int q = 0; q < kRedBatch; q++) {
-                if (pend & (1u << q)) {
-                  bool ready = true;
-#pragma unroll
-                  for (int i = 0; i < SPG; i++) ready &= (uint32_t)(w[q][i] >> 32) == flag;
-                  if (ready) pend &= ~(1u << q);
-                }
-              }
-              if (pend == 0 || !ok) break;
-              polls++;
-              const uint64_t now = globaltimer();
-              if (t0 == 0) {
-                t0 = now;
-              } else if (now - t0 > kWaitTimeoutNs) {
-                atomicCAS(&g_status_decode, 0, ST_PIECE_WAIT);
-                ok = false;
-                break;
-              }
-#pragma unroll
-              for (int q = 0; q < kRedBatch; q++) {
-                if (pend & (1u << q)) {
-#pragma unroll
-                  for (int j = 0; j < SPG / 2; j++)
-                    ld_piece(pw + (size_t)(s0 + q) * kPieceWords + j * kPairWords, w[q][2 * j], w[q][2 * j + 1]);
-                }
-              }
-            }
-            if (tlast) tr[9] = (unsigned long long)polls;
-#pragma unroll
-            for (int q = 0; q < kRedBatch; q++) {
-              if (s0 + q < nseg) {
-#pragma unroll
-                for (int i = 0; i < SPG; i++) y[i] += __uint_as_float((uint32_t)w[q][i]);
-              }
-            }
-          }
-          // every piece of this launch is in: the next launch uses the next epoch
-          if (ep == 0) a.counters[tile] = epoch + 1;
-          if (tlast) tr[10] = globaltimer();
-        }
-      }
-      if (run) {
-        if (EPI != EPI_RESID && a.ss_in != nullptr) {
-#pragma unroll
-          for (int i = 0; i < SPG; i++) y[i] *= s_scale[sb + i];
-        }
-        if constexpr (EPI == EPI_RESID) {
-          // every stream of the group is computed (streams >= B hold zeros) so the per-stream
-          // chains interleave; only the stores are predicated on B
-          float xs[SPG];
-#pragma unroll
-          for (int i = 0; i < SPG; i++) {
-            xs[i] = xo[i] + y[i];
-            if (sb + i < a.B) a.x[(size_t)(sb + i) * a.ldx + n] = xs[i];
-          }
-          if (tlast) tr[13] = globaltimer();
-          if (a.act_next != nullptr) {
-#pragma unroll
-            for (int i = 0; i < SPG; i++) {
-              const float h = xs[i] * wn;
-              const uint16_t hi = f2bf_bits(h);
-              const uint16_t lo = f2bf_bits(h - bf2f(hi));
-              if (sb + i < a.B) {
-                a.act_next[(size_t)(sb + i) * a.ld_next + n] = hi;
-                a.act_next[(size_t)(MAXB + sb + i) * a.ld_next + n] = lo;
-              }
-            }
-            if (tlast) tr[14] = globaltimer();
-            // per-tile sum of squares of the new x: the same xor butterfly for every stream,
-            // the group's 8 interleaved
-            float sq[SPG];
-#pragma unroll
-            for (int i = 0; i < SPG; i++) sq[i] = xs[i] * xs[i];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-              for (int i = 0; i < SPG; i++) sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], o);
-            }
-            if (lane == 0) {
-#pragma unroll
-              for (int i = 0; i < SPG; i++) ys[(warp & 3) * YS_LD + sb + i] = sq[i];
-            }
-            if (tlast) tr[15] = globaltimer();
-            epi_sync();
-            if (ep < a.B) {
-              const float t4 = (ys[0 * YS_LD + ep] + ys[1 * YS_LD + ep]) + (ys[2 * YS_LD + ep] + ys[3 * YS_LD + ep]);
-              a.ss_out[tile * MAXB + ep] = t4;
-            }
-          }
-        } else if constexpr (EPI == EPI_QKV) {
-#pragma unroll
-          for (int i = 0; i < SPG; i++) ys[r * YS_LD + sb + i] = y[i];
-          epi_sync();
-          const int head = tile;  // one 128-row tile = one head
-          const bool lo_half = r < 64;
-          const int partner = r ^ 64;
-          if (head < a.NH + a.NKV) {
-            if (tlast) tr[13] = globaltimer();
-            float o[SPG];
-#pragma unroll
-            for (int i = 0; i < SPG; i++) {  // all streams (pos -1 past B), stores predicated
-              const float other = ys[partner * YS_LD + sb + i];
-              o[i] = lo_half ? y[i] * rcos[i] - other * rsin[i] : y[i] * rcos[i] + other * rsin[i];
-            }
-            if (tlast) tr[14] = globaltimer();
-#pragma unroll
-            for (int i = 0; i < SPG; i++) {
-              const int b = sb + i, p = s_pos[b];
-              if (b < a.B) {
-                if (head < a.NH) {
-                  a.q[(size_t)b * a.ldq + n] = o[i];
-                } else if (p >= 0 && p < a.S) {
-                  a.kc[(((size_t)s_lane[b] * a.NKV + (head - a.NH)) * a.S + p) * 128 + r] = f2bf_bits(o[i]);
-                }
-              }
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < SPG; i++) {
-              const int b = sb + i, p = s_pos[b];
-              if (b < a.B && p >= 0 && p < a.S)
-                a.vc[(((size_t)s_lane[b] * a.NKV + (head - a.NH - a.NKV)) * a.S + p) * 128 + r] = f2bf_bits(y[i]);
-            }
-          }
-        } else if constexpr (EPI == EPI_SWIGLU) {
-#pragma unroll
-          for (int i = 0; i < SPG; i++) ys[r * YS_LD + sb + i] = y[i];
-          epi_sync();
-          if (r < 64) {
-            const int fcol = tile * 64 + r;
-#pragma unroll
-            for (int i = 0; i < SPG; i++) {
-              const float g = y[i], u = ys[(r + 64) * YS_LD + sb + i];
-              const float act = g / (1.0f + expf(-g)) * u;
-              const uint16_t hi = f2bf_bits(act);
-              const uint16_t lo = f2bf_bits(act - bf2f(hi));
-              if (sb + i < a.B) {
-                a.act_out[(size_t)(sb + i) * a.ld_act + fcol] = hi;
-                a.act_out[(size_t)(MAXB + sb + i) * a.ld_act + fcol] = lo;
-              }
-            }
-          }
-        } else if constexpr (EPI == EPI_LOGITS) {
-          unsigned long long key[SPG];
-#pragma unroll
-          for (int i = 0; i < SPG; i++) {
-            key[i] = 0;
-            if (n < a.V) {
-              if (sb + i < a.B) a.logits[(size_t)(sb + i) * a.V + n] = y[i];
-              key[i] = ((unsigned long long)orderable(y[i]) << 32) | (0xFFFFFFFFu - (uint32_t)n);
-            }
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (int i = 0; i < SPG; i++) {
-              const unsigned long long t = __shfl_xor_sync(0xffffffffu, key[i], o);
-              key[i] = t > key[i] ? t : key[i];
-            }
-          }
-          if (lane == 0) {
-#pragma unroll
-            for (int i = 0; i < SPG; i++) s_red[(warp & 3) * MAXB + sb + i] = key[i];
-          }
-          epi_sync();
-          if (ep < a.B) {
-            unsigned long long k = s_red[ep];
-            for (int w = 1; w < 4; w++) k = s_red[w * MAXB + ep] > k ? s_red[w * MAXB + ep] : k;
-            atomicMax(&a.best[ep], k);
-          }
-        }
-        if (tlast) tr[11] = globaltimer();
-        epi_sync();  // ys / s_red are reused by the next segment
-        if (tlast) tr[12] = globaltimer();
-      }
-      f = fend;
-    }
-    if (tr != nullptr && ep == 0) tr[6] = globaltimer();
+    epilogue_phase<EPI>(a, R, tmem, seg, f0, f1, tr);
+    if (tr != nullptr && threadIdx.x == 64) tr[6] = globaltimer();
     tc_fence_before();
-    mbar_arrive(epi_done);
+    mbar_arrive(R.epi_done);
   }
 }
 
@@ -914,6 +980,47 @@ extern "C" int rngd_tc_gemv_workspace(int N, int K, size_t* partial_floats, size
   return RNGD_OK;
 }
 
+// Arguments of one of a decode layer's GEMMs (kind 0 QKV, 1 O, 2 gate/up, 3 down) at layer l of
+// a call that holds layers [layer0, ..) in io's cache block.
+static GemmArgs layer_args(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, int l, int kind,
+                           const size_t off[5]) {
+  const int H = m->H, QN = m->NH * m->HD;
+  const int ld_act = H > QN ? H : QN;
+  const size_t lane_elems = (size_t)m->NKV * io->S * m->HD;
+  GemmArgs a = {};
+  a.B = io->B;
+  a.partial = io->partial;
+  a.counters = io->counters + off[kind];
+  a.tag = kind + 1;
+  a.ss_in = io->ss;
+  a.ss_tiles = H / BM;
+  a.eps = m->eps;
+  a.inv_h = 1.0f / (float)H;
+  if (kind == 0) {  // RoPE + KV append at pos; q for the attention
+    a.pos = io->pos;
+    a.inv = m->inv_freq;
+    a.q = io->q;
+    a.ldq = QN;
+    a.kc = (uint16_t*)io->kcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
+    a.vc = (uint16_t*)io->vcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
+    a.lanes = io->lanes;
+    a.NH = m->NH;
+    a.NKV = m->NKV;
+    a.S = io->S;
+  } else if (kind == 2) {  // SwiGLU into the down projection's operand
+    a.act_out = (uint16_t*)io->act2;
+    a.ld_act = m->M;
+  } else {  // residual; the O GEMM writes x * n2[l], the down GEMM x * n1[l+1] (or the final norm)
+    a.x = io->x;
+    a.ldx = H;
+    a.w_next = kind == 1 ? m->n2 + (size_t)l * H : (l + 1 < m->L ? m->n1 + (size_t)(l + 1) * H : m->norm);
+    a.act_next = (uint16_t*)io->act;
+    a.ld_next = ld_act;
+    a.ss_out = io->ss;
+  }
+  return a;
+}
+
 extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t* io, int layer0, int layer1,
                                   rngd_stream_t stream) {
   RNGD_TRY(check_tc_io(m, io));
@@ -921,44 +1028,31 @@ extern "C" int rngd_decode_layers(const rngd_model_t* m, const rngd_decode_io_t*
                layer0, layer1, m->L);
   RNGD_REQUIRE(layer1 - layer0 <= io->kv_layers, "decode: %d layers requested but the cache block holds %d",
                layer1 - layer0, io->kv_layers);
+  if (layer0 == layer1) return RNGD_OK;
   cudaStream_t s = (cudaStream_t)stream;
   const int H = m->H, Mi = m->M, QN = m->NH * m->HD, KN = m->NKV * m->HD, NQKV = QN + 2 * KN;
-  const int B = io->B;
   const int ld_act = H > QN ? H : QN;
   const size_t lane_elems = (size_t)m->NKV * io->S * m->HD;
   size_t off[5], pf, ct;
   decode_shapes(m, off, &pf, &ct);
+  auto attention = [&](int l) {
+    const uint16_t* kc = (const uint16_t*)io->kcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
+    const uint16_t* vc = (const uint16_t*)io->vcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
+    return launch_attn_decode_act(io->q, QN, kc, vc, io->pos, io->lanes, io->B, m->NH, m->NKV, m->HD, io->S,
+                                  io->attn_part, io->act_o, QN, s);
+  };
+  // layer0's QKV GEMM reads io->act = x * n1[layer0] (the prologue's or the previous call's)
+  RNGD_TRY(launch_skgemm<EPI_QKV>(m->wqkv, m->L, layer0, NQKV, H, io->act, ld_act,
+                                  layer_args(m, io, layer0, layer0, 0, off), s));
   for (int l = layer0; l < layer1; l++) {
-    uint16_t* kc = (uint16_t*)io->kcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
-    uint16_t* vc = (uint16_t*)io->vcache + (size_t)(l - layer0) * io->Bcap * lane_elems;
-    GemmArgs a = {};
-    a.B = B;
-    a.partial = io->partial;
-    a.counters = io->counters;
-    a.ss_in = io->ss;
-    a.ss_tiles = H / BM;
-    a.eps = m->eps;
-    a.inv_h = 1.0f / (float)H;
-    // attention block: io->act holds x * n1[l] (written by the prologue or the previous layer)
-    a.pos = io->pos; a.inv = m->inv_freq; a.q = io->q; a.ldq = QN; a.kc = kc; a.vc = vc; a.lanes = io->lanes;
-    a.NH = m->NH; a.NKV = m->NKV; a.S = io->S;
-    a.counters = io->counters + off[0]; a.tag = 1;
-    RNGD_TRY(launch_skgemm<EPI_QKV>(m->wqkv, m->L, l, NQKV, H, io->act, ld_act, a, s));
-    RNGD_TRY(launch_attn_decode_act(io->q, QN, kc, vc, io->pos, io->lanes, B, m->NH, m->NKV, m->HD, io->S, io->attn_part,
-                                    io->act_o, QN, s));
-    // O projection + residual; writes x * n2[l] for the MLP
-    a.x = io->x; a.ldx = H;
-    a.w_next = m->n2 + (size_t)l * H; a.act_next = (uint16_t*)io->act; a.ld_next = ld_act; a.ss_out = io->ss;
-    a.counters = io->counters + off[1]; a.tag = 2;
-    RNGD_TRY(launch_skgemm<EPI_RESID>(m->wo, m->L, l, H, QN, io->act_o, QN, a, s));
-    // MLP block
-    a.act_out = (uint16_t*)io->act2; a.ld_act = Mi;
-    a.counters = io->counters + off[2]; a.tag = 3;
-    RNGD_TRY(launch_skgemm<EPI_SWIGLU>(m->wgu, m->L, l, 2 * Mi, H, io->act, ld_act, a, s));
-    // down projection + residual; writes x * n1[l+1] (or the final norm) for what follows
-    a.w_next = l + 1 < m->L ? m->n1 + (size_t)(l + 1) * H : m->norm;
-    a.counters = io->counters + off[3]; a.tag = 4;
-    RNGD_TRY(launch_skgemm<EPI_RESID>(m->wd, m->L, l, H, Mi, io->act2, Mi, a, s));
+    RNGD_TRY(attention(l));
+    RNGD_TRY(launch_skgemm<EPI_RESID>(m->wo, m->L, l, H, QN, io->act_o, QN, layer_args(m, io, layer0, l, 1, off), s));
+    RNGD_TRY(launch_skgemm<EPI_SWIGLU>(m->wgu, m->L, l, 2 * Mi, H, io->act, ld_act,
+                                       layer_args(m, io, layer0, l, 2, off), s));
+    RNGD_TRY(launch_skgemm<EPI_RESID>(m->wd, m->L, l, H, Mi, io->act2, Mi, layer_args(m, io, layer0, l, 3, off), s));
+    if (l + 1 < layer1)
+      RNGD_TRY(launch_skgemm<EPI_QKV>(m->wqkv, m->L, l + 1, NQKV, H, io->act, ld_act,
+                                      layer_args(m, io, layer0, l + 1, 0, off), s));
   }
   return RNGD_OK;
 }

@@ -17,7 +17,14 @@ namespace rngd {
 
 
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
-enum : int { ST_TMA_WAIT = 1, ST_MMA_WAIT = 2, ST_EPI_WAIT = 3, ST_FLAG_WAIT = 4, ST_PIECE_WAIT = 5, ST_ATTN_WAIT = 6 };
+enum : int {
+  ST_TMA_WAIT = 1,
+  ST_MMA_WAIT = 2,
+  ST_EPI_WAIT = 3,
+  ST_FLAG_WAIT = 4,
+  ST_PIECE_WAIT = 5,
+  ST_ATTN_WAIT = 6
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);

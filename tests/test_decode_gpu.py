@@ -426,3 +426,4 @@ def test_config4_free_running_first_divergence(full_llama):
                                                "first_divergence": first})
     if first is not None:
         assert first["device_rank_in_oracle"] == 1 and first["gap"] < 0.1, f"divergence is not a near tie: {first}"
+
