@@ -355,8 +355,9 @@ def handoff_one_process(dsts, reps, warmup):
     another GPU: over NVLink with peer access); byte-exact check of every lane.  Per batch size:
     the kernel's device time, and the API time (push_many + the receiver's wait() seeing every
     flag through wait_all, host wall clock); for a peer, a copy-engine peer copy of the same bytes.""" 
+    import ctypes
     import torch
-    from rngd_pd import synth
+    from rngd_pd import _lib, synth
     from rngd_pd.engines.model import ModelConfig
     from rngd_pd.nvlink import NvlinkTransport
     cfg = ModelConfig.llama31_8b()
@@ -425,8 +426,8 @@ def handoff_one_process(dsts, reps, warmup):
                         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         e0.record(s)
                         for b in range(n):
-                            flat[b * (per_req // 2):(b + 1) * (per_req // 2)].copy_(
-                                kvs[(rep * n + b) % B].view(-1), non_blocking=True)
+                            _lib.call("rngd_peer_copy", ctypes.c_void_p(flat.data_ptr() + b * per_req), dst,
+                                      _lib.ptr(kvs[(rep * n + b) % B]), 0, per_req, _lib.stream_handle(s))
                         e1.record(s)
                     e1.synchronize()
                     if rep >= 3:
@@ -560,6 +561,7 @@ def handoff_pairs(rank, world, dev, reps, warmup):
     """Config 3 across processes: GPU 2i prefills (seeded caches) and pushes into GPU 2i+1's
     decode cache, mapped through CUDA IPC; 1/4/16 requests per batch.  Returns, on every rank,
     {requests: max-over-senders ms} and whether every receiver's lanes were byte-exact."""
+    import ctypes
     import torch
     import torch.distributed as dist
     from rngd_pd import _lib, synth
@@ -623,14 +625,15 @@ def handoff_pairs(rank, world, dev, reps, warmup):
         if sender:
             _lib.call("rngd_peer_enable", dev.index, partner)          # a direct copy over NVLink
             flat = torch.empty(n * kvs[0].numel(), dtype=torch.bfloat16, device=pdev)
+            nbytes = kvs[0].numel() * 2
             for rep in range(warmup + reps):
                 with torch.cuda.stream(s):
                     torch.cuda._sleep(SLEEP_CYCLES)
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record(s)
                     for b in range(n):
-                        flat[b * kvs[0].numel():(b + 1) * kvs[0].numel()].copy_(kvs[(rep * n + b) % B].view(-1),
-                                                                                non_blocking=True)
+                        _lib.call("rngd_peer_copy", ctypes.c_void_p(flat.data_ptr() + b * nbytes), partner,
+                                  _lib.ptr(kvs[(rep * n + b) % B]), dev.index, nbytes, _lib.stream_handle(s))
                     e1.record(s)
                 e1.synchronize()
                 if rep >= warmup:
@@ -761,7 +764,10 @@ def run_micro_serve_box(args):
     solo = None
     if os.environ.get("SERVE_SOLO", "1") != "0":
         every = sorted(set(i for r in runs for i in r["_ok"]))
-        got = _solo_tokens(cfg, box.decode_engines, prompts, every, out_tok)
+        # the gateway keeps a prompt's first S - max_tokens - 1 tokens (as the reference's gateway
+        # does, serving/cluster.py:1516); the solo run is given the same prompt
+        served = [p[:S - out_tok - 1] for p in prompts]
+        got = _solo_tokens(cfg, box.decode_engines, served, every, out_tok)
         solo = [dict(_solo_report(r["_outs"], got, r["_ok"]), rate_req_s=r["rate_req_s"]) for r in runs]
     best = max(runs, key=lambda r: r["box_tok_s"])
     print(json.dumps({"micro": "serve_box", "split": f"{split[0]}P:{split[1]}D", "gpus": n,

@@ -195,6 +195,10 @@ int rngd_ipc_close(void* ptr);
 int rngd_ipc_handle_size(void);
 /* Enable direct access from `device` to `peer` (one process driving both GPUs). */
 int rngd_peer_enable(int device, int peer);
+/* The copy engine moving `bytes` from src on src_device to dst on dst_device (cudaMemcpyPeerAsync,
+ * direct over NVLink once rngd_peer_enable(src_device, dst_device) ran): the comparator the fused
+ * handoff is measured against.  It has no counterpart in the reference, whose handoff is host-staged. */
+int rngd_peer_copy(void* dst, int dst_device, const void* src, int src_device, size_t bytes, rngd_stream_t stream);
 /* Pinned host memory mapped into the device address space (status words). */
 int rngd_host_alloc_mapped(size_t bytes, void** host, void** dev);
 int rngd_host_free(void* host);
@@ -226,6 +230,10 @@ typedef struct {
 int rngd_kv_handoff_batch(const rngd_kv_item_t* items, int n, size_t src_layer_stride, void* dst_k, void* dst_v,
                           int L, int NKV, int S, int HD, int Bcap, int layer0, int layer1, uint32_t* done,
                           int64_t* flags, rngd_stream_t stream);
+/* Copies n int64 handoff flags (device memory) into `host` (pinned) on `stream` and waits for the
+ * copy: the receiver's host poll of which layers have landed, one call per poll for every lane
+ * (the reference's receiver polls its store the same way, connector/transport.py:80-101). */
+int rngd_kv_read_flags(const int64_t* flags, int64_t* host, size_t n, rngd_stream_t stream);
 /* Bounded device wait until flags[l] >= seq for l in [layer0, layer1): writes 0,
  * or RNGD_ERR_TIMEOUT's wait code 4 after timeout_ns (<= 10 s), to *status
  * (e.g. host-mapped); later work on `stream` is ordered after the arrival. */

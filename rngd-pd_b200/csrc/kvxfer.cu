@@ -234,6 +234,21 @@ extern "C" int rngd_kv_handoff(const void* src_k, const void* src_v, size_t src_
                                flags - (long)lane * L, stream);
 }
 
+extern "C" int rngd_peer_copy(void* dst, int dst_device, const void* src, int src_device, size_t bytes,
+                              rngd_stream_t stream) {
+  RNGD_REQUIRE(dst != nullptr && src != nullptr, "peer_copy: null pointer");
+  return check_cuda(cudaMemcpyPeerAsync(dst, dst_device, src, src_device, bytes, (cudaStream_t)stream),
+                    "cudaMemcpyPeerAsync");
+}
+
+extern "C" int rngd_kv_read_flags(const int64_t* flags, int64_t* host, size_t n, rngd_stream_t stream) {
+  RNGD_REQUIRE(flags != nullptr && host != nullptr && n > 0, "kv_read_flags: null or empty buffer");
+  cudaStream_t s = (cudaStream_t)stream;
+  RNGD_TRY(check_cuda(cudaMemcpyAsync(host, flags, n * sizeof(int64_t), cudaMemcpyDeviceToHost, s),
+                      "cudaMemcpyAsync (handoff flags)"));
+  return check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize (handoff flags)");
+}
+
 extern "C" int rngd_kv_wait(const int64_t* flags, int layer0, int layer1, int64_t seq, int64_t timeout_ns,
                             int32_t* status, rngd_stream_t stream) {
   RNGD_REQUIRE(flags && status, "kv_wait: null pointer");

@@ -118,6 +118,8 @@ KV_MAX_BATCH = 16
 _sig("rngd_kv_handoff_batch", ctypes.POINTER(KvItem), ctypes.c_int, ctypes.c_size_t, _vp, _vp, ctypes.c_int,
      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp)
 _sig("rngd_kv_wait", _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _vp, _vp)
+_sig("rngd_kv_read_flags", _vp, _vp, ctypes.c_size_t, _vp)
+_sig("rngd_peer_copy", _vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_size_t, _vp)
 _sig("rngd_device_status", ctypes.POINTER(ctypes.c_int), ctypes.c_int)
 _sig("rngd_gemv_bf16", _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
      ctypes.c_int, _vp)

@@ -203,7 +203,8 @@ class LaneLeases:
     @staticmethod
     def landed(flag_row, seq, layer0, layer1):
         """Whether layers [layer0, layer1) of a lane's flags (a sequence of ints) reached seq."""
-        return all(int(f) >= seq for f in flag_row[layer0:layer1])
+        row = flag_row[layer0:layer1]
+        return len(row) == 0 or int(min(row)) >= seq
 
 
 class SenderLeases:
@@ -232,14 +233,19 @@ class SenderLeases:
             self._known.clear()
 
 
-def poll_until(check, timeout, what, pause=20e-6):
+def poll_until(check, timeout, what, pause=20e-6, spin=2e-3):
     """Call check() until it is true; TimeoutError naming `what` after `timeout` seconds.
-    Returns the seconds waited."""
+    Returns the seconds waited.  For the first `spin` seconds the checks run back to back (a
+    check is itself a device->host copy of ~10 us, while time.sleep rounds a pause this short up
+    to ~60 us, which would dominate a handoff of tens of microseconds); after that each check
+    is followed by a pause."""
     t0 = time.perf_counter()
     while not check():
-        if time.perf_counter() - t0 > timeout:
+        waited = time.perf_counter() - t0
+        if waited > timeout:
             raise TimeoutError(f"nvlink: {what} did not arrive within {timeout}s")
-        time.sleep(pause)
+        if waited > spin:
+            time.sleep(pause)
     return time.perf_counter() - t0
 
 
@@ -260,8 +266,8 @@ class NvlinkTransport(Transport):
         self.leases = LaneLeases(0)
         self._status_host = self._status_dev = None
         self._status_next = 0
-        self._poll_stream = self._poll_host = None
-        self._poll_all = None
+        self._poll_stream = None
+        self._poll_all = self._poll_np = None
         # sender state
         self._peers = {}            # peer key -> _Peer
         self.remote_leases = SenderLeases()
@@ -281,6 +287,9 @@ class NvlinkTransport(Transport):
         if flags is None:
             flags = ipc_empty((Bcap, L), torch.int64, self.device) if ipc_handle(K) else \
                 torch.zeros((Bcap, L), dtype=torch.int64, device=self.device)
+        elif (tuple(flags.shape) != (Bcap, L) or flags.dtype != torch.int64 or not flags.is_contiguous()
+              or flags.device != self.device):
+            raise ValueError(f"bind_cache: flags must be a contiguous int64 [{Bcap}, {L}] tensor on {self.device}")
         with self._lock:
             self._cache = (K, V, flags)
             self.leases = LaneLeases(Bcap)
@@ -332,30 +341,23 @@ class NvlinkTransport(Transport):
         lane, seq, sender = self.leases.lookup(req_id)
         return lane, seq, layer1, sender
 
-    def _read_flags(self, lane):
-        """The lane's per-layer flags on the host: one small device->host copy on a side stream."""
-        flags = self._cache[2]
-        with self._lock:
-            if self._poll_stream is None:
-                self._poll_stream = torch.cuda.Stream(device=self.device)
-                self._poll_host = torch.zeros(flags.shape[1], dtype=torch.int64).pin_memory()
-            with torch.cuda.stream(self._poll_stream):
-                self._poll_host.copy_(flags[lane], non_blocking=True)
-            self._poll_stream.synchronize()
-            return self._poll_host.tolist()
-
     def _read_all_flags(self):
-        """Every lane's flags on the host ([Bcap][L] list of lists): one small copy for all."""
+        """Every lane's per-layer flags on the host, a [Bcap][L] int64 array: one device->host copy
+        of the whole flag block on a side stream (rngd_kv_read_flags), into a pinned buffer."""
         flags = self._cache[2]
         with self._lock:
-            if getattr(self, "_poll_all", None) is None or self._poll_all.shape != flags.shape:
+            if self._poll_all is None or tuple(self._poll_all.shape) != tuple(flags.shape):
                 if self._poll_stream is None:
                     self._poll_stream = torch.cuda.Stream(device=self.device)
                 self._poll_all = torch.zeros(flags.shape, dtype=torch.int64).pin_memory()
-            with torch.cuda.stream(self._poll_stream):
-                self._poll_all.copy_(flags, non_blocking=True)
-            self._poll_stream.synchronize()
-            return self._poll_all.tolist()
+                self._poll_np = self._poll_all.numpy()
+            _lib.call("rngd_kv_read_flags", _lib.ptr(flags), _lib.ptr(self._poll_all), flags.numel(),
+                      _lib.stream_handle(self._poll_stream))
+            return self._poll_np.copy()
+
+    def _read_flags(self, lane):
+        """The lane's per-layer flags on the host."""
+        return self._read_all_flags()[lane]
 
     def arrived_all(self, req_ids, layer0=0, layer1=None):
         """Whether every request of `req_ids` has layers [layer0, layer1) landed."""

@@ -1,9 +1,9 @@
 """The NVLink handoff's lease / handshake protocol across two processes on the host (no GPU).
 
 The receiver is the real NvlinkTransport (reserve, release, handshake_metadata, arrived, wait,
-lane_views and the rm-core wait that turns a timeout into a failed TransferResult) with its
-cache and per-lane flags in shared host memory instead of HBM: only the flag read is swapped
-for a read of that memory.  The sender is a spawned process that learns leases through the
+arrived_all, wait_all, lane_views and the rm-core wait that turns a timeout into a failed
+TransferResult) with its cache and per-lane flags in shared host memory instead of HBM: only
+the flag read is swapped for a read of that memory.  The sender is a spawned process that learns leases through the
 real SenderLeases (from the receiver's handshake metadata, or from a ticket forwarded with a
 request) and stores a request's bytes into its leased lane, then publishes the lease's
 sequence number in each layer's flag -- the order the handoff kernel keeps (data, fence,
@@ -72,7 +72,7 @@ def _host_receiver(flags):
     t.leases = LaneLeases(BCAP)
     for b in range(BCAP):
         t.leases.start_after(b, int(flags[b].max()))
-    t._read_flags = lambda lane: flags[lane].tolist()
+    t._read_all_flags = lambda: flags.copy()
     return t
 
 
@@ -136,6 +136,19 @@ def test_lease_handshake_push_and_stale_flags_across_processes(pair):
     assert rx.arrived("r2", 0, L // 2) and not rx.arrived("r2")
     _push(q_in, q_out, "r2", L // 2, L, 9)
     assert rx.wait("r2", timeout=5) < 5 and (lanes[2] == 9).all()
+
+    # several requests waited at once: one flag read per poll, complete only when both landed
+    rx.release("r2")
+    ta, tb = rx.reserve("ra", 0), rx.reserve("rb", 1)
+    q_in.put(("ticket", key, ta))
+    q_in.put(("ticket", key, tb))
+    _push(q_in, q_out, "ra", 0, L, 3)
+    assert not rx.arrived_all(["ra", "rb"]) and rx.arrived_all(["ra"])
+    with pytest.raises(TimeoutError):
+        rx.wait_all(["ra", "rb"], timeout=0.05)
+    _push(q_in, q_out, "rb", 0, L, 4)
+    assert rx.wait_all(["ra", "rb"], timeout=5) < 5
+    assert (lanes[0] == 3).all() and (lanes[1] == 4).all()
 
     # a request the sender holds no lease for is refused, and nothing is written
     before = lanes.copy()
