@@ -519,6 +519,49 @@ def prefill_measure(eng, reps=5, warmup=2):
             "flops_per_pass": flops, "note": "GEMMs issue hi and lo activation halves: tensor work is ~2x the useful"}
 
 
+def prefill_timeline(eng, layers=2):
+    """Per-CTA timelines of the first `layers` layers' prefill GEMM launches of one config-2 pass
+    (needs a library built with `make TRACE=1`; None for a product build).  Per launch, in us
+    from its earliest CTA start, [min, median, max] over CTAs of: start, TMA past the dependency
+    wait, first full stage, last MMA commit, last unit's accumulator ready / pieces acquired /
+    epilogue done; plus the median MMA span, the tail from the last commit to the last epilogue,
+    and the median epilogue time of the CTAs that finish their last unit themselves."""
+    import torch
+    from rngd_pd import _lib, synth
+    from rngd_pd.engines.prefill_full import FullPrefillEngine
+    n = 4 * layers
+    tr = torch.zeros((n, 1024, 16), dtype=torch.int64, device=eng.dev)
+    try:
+        _lib.call("rngd_trace_decode_gemms", _lib.ptr(tr), 0)     # records nothing: a support check
+    except _lib.RngdError:           # a product build: the stamps are compiled out
+        return None
+    pf = FullPrefillEngine(eng.cfg, eng.w, C=256, group=2, S=S)
+    toks = synth.tokens(256, seed=4)
+    pf.prefill_kv_device(toks)
+    _lib.call("rngd_trace_decode_gemms", _lib.ptr(tr), n)
+    try:
+        pf.prefill_kv_device(toks)
+        torch.cuda.synchronize(eng.dev)
+    finally:
+        _lib.call("rngd_trace_decode_gemms", None, 0)
+    out = []
+    for i in range(n):
+        t = tr[i].cpu().double()
+        t = t[t[:, 0] > 0]
+        rel = (t - t[:, 0].min()) / 1e3
+        q = lambda c: [round(float(v), 1) for v in (rel[:, c].min(), rel[:, c].median(), rel[:, c].max())]
+        own = t[:, 9] == 0
+        row = {"gemm": ("qkv", "o", "gate_up", "down")[i % 4], "layer": i // 4}
+        row.update({k: q(c) for k, c in (("start", 0), ("tma_dep", 1), ("first_full", 2), ("last_commit", 3),
+                                         ("last_acc", 4), ("pieces", 5), ("epi_done", 6))})
+        row["mma_span_med"] = round(float(((t[:, 3] - t[:, 2]) / 1e3).median()), 1)
+        row["tail"] = round(float((t[:, 6].max() - t[:, 3].max()) / 1e3), 1)
+        row["last_unit_epi_med"] = round(float(((t[own, 6] - t[own, 5]) / 1e3).median()), 1) if own.any() else None
+        out.append(row)
+    del pf
+    return out
+
+
 def prefill_chunk_measure(eng, reps=3, warmup=1):
     """Chunked prefill (ChunkPrefillEngine, engines/prefill_chunk.py): one 256-token prompt
     (seed 4) in chunks of 16 positions against a one-lane cache, on the decode engine's card and
@@ -949,8 +992,11 @@ def run_micro(args):
         cfg = ModelConfig.llama31_8b() if args.micro == "prefill" else ModelConfig.from_dims(L=2)
         eng = BatchDecodeEngine(cfg, synth.SyntheticState(cfg, seed=0), B=B, S=S,
                                 group=8 if args.micro == "prefill" else 2)
-        print(json.dumps({"micro": args.micro, **prefill_measure(eng, reps=args.steps, warmup=args.warmup)}),
-              flush=True)
+        res = prefill_measure(eng, reps=args.steps, warmup=args.warmup)
+        tl = prefill_timeline(eng)
+        if tl is not None:
+            res["timeline_us"] = tl
+        print(json.dumps({"micro": args.micro, **res}), flush=True)
         return
     if args.micro.startswith("pf_"):
         return run_micro_prefill(args)

@@ -261,11 +261,14 @@ int rngd_tc_gemv_workspace(int N, int K, size_t* partial_floats, size_t* counter
  * %globaltimer slots (ns) [start, operand ready, last weight TMA issued, last stage
  * arrived, last MMA committed, last accumulator ready, epilogue done, end, then five
  * steps of the last segment's epilogue] into trace[cta*16 ..] (device memory,
- * >= 16 * SM count entries). */
+ * >= 16 * SM count entries).  rngd_tc_gemm_tokens launches record into the same buffer their
+ * own slots [start, TMA past the dependency wait, first full stage, last MMA committed, last
+ * unit's accumulator ready / pieces acquired / epilogue done, first accumulator ready, last
+ * unit's owner count, this CTA's slot in it, epilogue past the dependency wait]. */
 int rngd_tc_gemv_trace(uint64_t* trace);
-/* Diagnostics (TRACE=1 builds only, as above): the next `launches` decode GEMM launches record the
- * same sixteen slots per CTA into consecutive blocks trace[i*1024*16 ..] (device memory,
- * launches * 16384 entries); NULL turns it off. */
+/* Diagnostics (TRACE=1 builds only, as above): the next `launches` decode or prefill GEMM
+ * launches record their sixteen slots per CTA into consecutive blocks trace[i*1024*16 ..] (device
+ * memory, launches * 16384 entries); NULL turns it off. */
 int rngd_trace_decode_gemms(uint64_t* trace, int launches);
 /* Token-tile form (the prefill GEMM): Y[t][n] += sum_k W[n][k] * X[t][k] for
  * C tokens (C % 128 == 0) on tcgen05, X fp32 [C][K] split into bf16 hi/lo rows

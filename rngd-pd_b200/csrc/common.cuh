@@ -13,9 +13,9 @@
 
 #include "../../include/rngd_b200.h"
 
-// Per-CTA %globaltimer stamps in the decode GEMM (rngd_tc_gemv_trace, rngd_trace_decode_gemms)
-// are diagnostics: compiled in only by `make TRACE=1`.  In the product build the stamps fold away
-// and those two entries return RNGD_ERR_UNSUPPORTED for a non-NULL buffer.
+// Per-CTA %globaltimer stamps in the decode and prefill GEMMs (rngd_tc_gemv_trace,
+// rngd_trace_decode_gemms) are diagnostics: compiled in only by `make TRACE=1`.  In the product
+// build the stamps fold away and those two entries return RNGD_ERR_UNSUPPORTED for a non-NULL buffer.
 #ifndef RNGD_TRACE
 #define RNGD_TRACE 0
 #endif
@@ -23,6 +23,8 @@
 namespace rngd {
 
 void set_error(const char* fmt, ...);
+unsigned long long* gemm_trace();      // the buffer set by rngd_tc_gemv_trace (null unless tracing)
+unsigned long long* next_seq_trace();  // next block of rngd_trace_decode_gemms' sequence, or null
 
 // Returns RNGD_ERR_CUDA and records the message when a launch or call failed.
 inline int check_cuda(cudaError_t e, const char* what) {

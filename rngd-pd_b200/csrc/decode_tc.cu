@@ -817,12 +817,17 @@ static int max_segments(int N, int K, int grid) {
 static unsigned long long* g_seq = nullptr;
 static int g_seq_left = 0;
 
+// the next block of the launch-sequence trace (null when off or used up)
+unsigned long long* next_seq_trace() {
+  if (!RNGD_TRACE || g_seq == nullptr || g_seq_left <= 0) return nullptr;
+  unsigned long long* t = g_seq;
+  g_seq += 1024 * 16;
+  g_seq_left--;
+  return t;
+}
+
 static void seq_trace(GemmArgs* a) {
-  if (RNGD_TRACE && a->trace == nullptr && g_seq != nullptr && g_seq_left > 0) {
-    a->trace = g_seq;
-    g_seq += 1024 * 16;
-    g_seq_left--;
-  }
+  if (RNGD_TRACE && a->trace == nullptr) a->trace = next_seq_trace();
 }
 
 template <int EPI>
@@ -934,6 +939,8 @@ extern "C" int rngd_decode_attn_workspace(const rngd_model_t* m, int Bcap, int S
 }
 
 static unsigned long long* g_trace = nullptr;  // set by rngd_tc_gemv_trace (diagnostics)
+
+unsigned long long* rngd::gemm_trace() { return g_trace; }
 
 extern "C" int rngd_tc_gemv_trace(uint64_t* trace) {
   if (!RNGD_TRACE && trace != nullptr) {

@@ -83,6 +83,8 @@ struct PArgs {
   // SWIGLU
   uint16_t* act_out;
   int ld_act;
+  // per-CTA timeline [grid][16] (diagnostics; only a library built with RNGD_TRACE=1 records it)
+  unsigned long long* trace;
 };
 
 // named barriers: 1 + g = epilogue warpgroup g (128 threads), 3 = both warpgroups
@@ -117,6 +119,12 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
   // and the second read hits L2 instead of HBM
   const int ngrp = a.N / (MT * PBM);
   const bool use_lo = a.lo != 0;
+  // RNGD_TRACE == 0 (the product build): tr is a constant null and every stamp below folds away.
+  // Slots: 0 start, 1 TMA past the dependency wait, 2 first full stage, 3 last MMA commit,
+  // 4 / 5 / 6 last unit: accumulator ready / pieces acquired / epilogue done, 7 first accumulator
+  // ready, 8 last unit's owners, 9 this CTA's slot in it, 10 epilogue past the dependency wait
+  unsigned long long* tr = (RNGD_TRACE && a.trace != nullptr) ? a.trace + (size_t)cta * 16 : nullptr;
+  if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer();
   const uint32_t stage_tx = (uint32_t)(Cfg::A_BYTES + (use_lo ? 2 : 1) * Cfg::B_BYTES);
 
   if (threadIdx.x == 0) {
@@ -155,6 +163,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
         tma_load_3d(st, &tmW, &full[i], kb * PBK, mg * MT * PBM, a.layer);
       }
       grid_dep_wait();
+      if (tr != nullptr) tr[1] = globaltimer();
       for (long i = 0; i < pre; i++) {
         const long f = f0 + i;
         const long u = f / a.nkb;
@@ -197,6 +206,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
           const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
           ok = mbar_wait(&full[s], ph, ST_MMA_WAIT, &g_status_prefill);
           if (!ok) break;
+          if (tr != nullptr && i == 0) tr[2] = globaltimer();
           tc_fence_after();
           const uint32_t sa = smem_u32(base + s * Cfg::STAGE);
           const uint32_t sh = sa + Cfg::A_BYTES, sl = sh + Cfg::B_BYTES;
@@ -216,6 +226,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
         umma_commit(&acc_full[buf]);
         f = fend;
       }
+      if (tr != nullptr) tr[3] = globaltimer();
     }
     __syncwarp();
   } else {
@@ -226,6 +237,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
     grid_dep_wait();
     const int r = ((warp & 3) << 5) | lane;
     const int et = threadIdx.x - 64;   // 0 .. P_EPI-1
+    if (tr != nullptr && et == 0) tr[10] = globaltimer();
     const int g = et >> 7;             // warpgroup
     const int eg = et & 127;           // index within the warpgroup
     float* ys = ys_all + g * PBM * P_YS_LD;
@@ -265,6 +277,13 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
       tc_fence_after();
       const int first = owner_of(ustart, a.total, G), last = owner_of(ustart + a.nkb - 1, a.total, G);
       const int nseg = last - first + 1;
+      const bool tlast = tr != nullptr && et == 0 && fend == f1;
+      if (tr != nullptr && et == 0 && seg == 0) tr[7] = globaltimer();
+      if (tlast) {
+        tr[4] = globaltimer();
+        tr[8] = (unsigned long long)nseg;
+        tr[9] = (unsigned long long)(cta - first);
+      }
       const uint32_t tbase0 = tmem + lane_base + (uint32_t)(buf * MT * NT);
       bool run = true;
       const int slot = cta - first;
@@ -285,6 +304,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
         pf_arrive(&acc_empty[buf]);
         pf_sync_all();  // every thread's piece stores precede the release below
         if (et == 0) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(pflags + slot), "r"(flag) : "memory");
+        if (tlast) tr[5] = tr[6] = globaltimer();
         run = false;
       } else if (nseg > 1) {
         // the unit's first piece is this CTA's own (in TMEM): wait (bounded) for the others'
@@ -308,6 +328,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
         }
         pf_sync_all();
       }
+      if (tlast && run) tr[5] = globaltimer();
       if (run) {
        for (int tt = 0; tt < MT; tt++) {
         const int mt = mg * MT + tt;  // weight tile of this accumulator
@@ -436,6 +457,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
           pf_sync_g(g);  // ys / s_red reused by the next chunk
         }
        }
+        if (tlast) tr[6] = globaltimer();
         tc_fence_before();
         pf_arrive(&acc_empty[buf]);
         if (nseg > 1 && et == 0) a.counters[u] = epoch + 1;  // read by the next launch only
@@ -710,6 +732,7 @@ static int launch_pf(const void* W, int L, int layer, int N, int K, const void* 
   a.maxseg = pf_maxseg(units, a.nkb, grid);
   a.nunits = (int)units;
   a.layer = layer;
+  if (RNGD_TRACE && a.trace == nullptr) a.trace = next_seq_trace();
   RNGD_REQUIRE(a.maxseg == 1 || (a.partial && a.counters), "prefill GEMM: split tiles need partial/counters");
   RNGD_REQUIRE(a.tag >= 1 && a.tag <= 15, "prefill GEMM: shape tag %d outside 1..15", a.tag);
   static std::atomic<unsigned long long> attr_set{0};
@@ -894,6 +917,7 @@ extern "C" int rngd_tc_gemm_tokens(const void* W, int N, int K, const float* X, 
   a.ldx = N;
   a.tag = 5;
   a.lo = 1;
+  a.trace = RNGD_TRACE ? gemm_trace() : nullptr;
   return launch_pf_any<PEPI_RESID>(W, 1, 0, N, K, act, K, a, s);
 }
 
