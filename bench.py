@@ -557,6 +557,9 @@ def prefill_timeline(eng, layers=2):
         row["mma_span_med"] = round(float(((t[:, 3] - t[:, 2]) / 1e3).median()), 1)
         row["tail"] = round(float((t[:, 6].max() - t[:, 3].max()) / 1e3), 1)
         row["last_unit_epi_med"] = round(float(((t[own, 6] - t[own, 5]) / 1e3).median()), 1) if own.any() else None
+        row["last_unit_epi_by_owners"] = {int(k): round(float(((t[own & (t[:, 8] == k), 6] - t[own & (t[:, 8] == k), 5])
+                                                                / 1e3).median()), 1)
+                                          for k in sorted(set(t[own, 8].long().tolist()))}
         out.append(row)
     del pf
     return out
