@@ -33,9 +33,10 @@ namespace rngd {
 __device__ int g_status_prefill = 0;
 
 constexpr int PBM = 128, PBK = 64;
-constexpr int P_EPI = 256;     // epilogue threads: two warpgroups, each half of every 32-token chunk
-constexpr int P_HALF = 16;     // tokens of a chunk per warpgroup
-constexpr int P_YS_LD = 17;    // smem pitch of a warpgroup's [128][16] exchange buffer
+constexpr int P_GROUPS = 4;    // epilogue warpgroups, each a quarter of every 32-token chunk
+constexpr int P_EPI = 128 * P_GROUPS;  // epilogue threads
+constexpr int P_HALF = 32 / P_GROUPS;  // tokens of a chunk per warpgroup
+constexpr int P_YS_LD = P_HALF + 1;    // smem pitch (odd) of a warpgroup's [128][P_HALF] exchange buffer
 constexpr int P_MAXPIECE = 4;  // split-unit pieces whose loads are issued together
 
 // MT weight tiles (128 rows each) share every token tile: with MT = 2 a 64 KB stage
@@ -49,9 +50,9 @@ struct PCfg {
   static constexpr int STAGES = MT == 2 ? 3 : 4;
   static constexpr int TMEM_COLS = 2 * MT * NT;       // MT accumulators, double-buffered
   static constexpr size_t BAR_BYTES = (2 * STAGES + 5) * 8;
-  // ring | barriers | tmem slot, flag | s_scale [NT] | ys [2][128][P_YS_LD] | s_red [2][4][16]
-  static constexpr size_t SMEM =
-      1024 + STAGES * STAGE + BAR_BYTES + 64 + NT * 4 + 2 * PBM * P_YS_LD * 4 + 2 * 4 * P_HALF * 4;
+  // ring | barriers | tmem slot, flag | s_scale [NT] | ys [P_GROUPS][128][P_YS_LD] | s_red [P_GROUPS][4][P_HALF]
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE + BAR_BYTES + 64 + NT * 4 +
+                                 P_GROUPS * PBM * P_YS_LD * 4 + P_GROUPS * 4 * P_HALF * 4;
 };
 
 enum PEpi : int { PEPI_QKV = 0, PEPI_RESID = 1, PEPI_SWIGLU = 2 };
@@ -87,9 +88,18 @@ struct PArgs {
   unsigned long long* trace;
 };
 
-// named barriers: 1 + g = epilogue warpgroup g (128 threads), 3 = both warpgroups
+// named barriers: 1 + g = epilogue warpgroup g (128 threads), 1 + P_GROUPS = all of them
 __device__ __forceinline__ void pf_sync_g(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
-__device__ __forceinline__ void pf_sync_all() { asm volatile("bar.sync 3, %0;" ::"n"(P_EPI) : "memory"); }
+__device__ __forceinline__ void pf_sync_all() {
+  asm volatile("bar.sync %0, %1;" ::"n"(1 + P_GROUPS), "n"(P_EPI) : "memory");
+}
+// this thread's P_HALF accumulator columns from TMEM
+__device__ __forceinline__ void pf_tmem_ld(uint32_t taddr, float* v) {
+  if constexpr (P_HALF == 16)
+    tmem_ld_32x32b_x16(taddr, v);
+  else
+    tmem_ld_32x32b_x8(taddr, v);
+}
 __device__ __forceinline__ void pf_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -108,8 +118,8 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
   uint64_t* epi_done = acc_empty + 2;   // the epilogue threads are past their last TMEM read
   uint32_t* tmem_slot = (uint32_t*)((uint8_t*)full + Cfg::BAR_BYTES);
   float* s_scale = (float*)((uint8_t*)full + Cfg::BAR_BYTES + 64);   // [NT] RMS scale of the unit's tokens
-  float* ys_all = s_scale + NT;                                      // [2][128][P_YS_LD]
-  float* s_red_all = ys_all + 2 * PBM * P_YS_LD;                     // [2][4][16]
+  float* ys_all = s_scale + NT;                                      // [P_GROUPS][128][P_YS_LD]
+  float* s_red_all = ys_all + P_GROUPS * PBM * P_YS_LD;              // [P_GROUPS][4][P_HALF]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -230,10 +240,11 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue warps 2..9: two warpgroups over the same 128 TMEM lanes.  Thread
-    // (group g, row r) owns row r of the tile for tokens 16g .. 16g+15 of every 32-token chunk,
-    // so each thread's serial work on the tail is half a chunk, with its global loads issued
-    // together (one L2 round trip per half chunk).
+    // ---------------- epilogue warps 2..: P_GROUPS warpgroups over the same 128 TMEM lanes.
+    // Thread (group g, row r) owns row r of the tile for tokens P_HALF*g .. P_HALF*g + P_HALF-1 of
+    // every 32-token chunk.  The last unit's epilogue is on the critical path of the pass (the
+    // next GEMM reads every column it writes), and it shortens with more warps sharing it: with
+    // two warpgroups instead of one it took 0.56-0.70x as long.
     grid_dep_wait();
     const int r = ((warp & 3) << 5) | lane;
     const int et = threadIdx.x - 64;   // 0 .. P_EPI-1
@@ -256,7 +267,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
       // RMS scales of this unit's NT tokens, read while the accumulator is still being built:
       // token jt*NT + i's sum over the ss tiles in tile order, loads batched 16 at a time
       if (EPI != PEPI_RESID && a.ss_in != nullptr) {
-        pf_sync_all();  // both warpgroups are past the previous unit's scales
+        pf_sync_all();  // every warpgroup is past the previous unit's scales
         for (int i = et; i < NT; i += P_EPI) {
           const int tok = jt * NT + i;
           float ssum = 0.f;
@@ -295,7 +306,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
           float* pdst = a.partial + (((size_t)u * a.maxseg + slot) * MT + tt) * NT * PBM;
           for (int cc = 0; cc < NT / 32; cc++) {
             float v[P_HALF];
-            tmem_ld_32x32b_x16(tbase0 + tt * NT + cc * 32 + g * P_HALF, v);
+            pf_tmem_ld(tbase0 + tt * NT + cc * 32 + g * P_HALF, v);
 #pragma unroll
             for (int i = 0; i < P_HALF; i++) __stcg(pdst + (size_t)(cc * 32 + g * P_HALF + i) * PBM + r, v[i]);
           }
@@ -341,7 +352,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
             for (int i = 0; i < P_HALF; i++) xo[i] = a.x[(size_t)(t0 + i) * a.ldx + n];
           }
           float y[P_HALF];
-          tmem_ld_32x32b_x16(tbase0 + tt * NT + cc * 32 + g * P_HALF, y);  // piece 0: this CTA's own
+          pf_tmem_ld(tbase0 + tt * NT + cc * 32 + g * P_HALF, y);  // piece 0: this CTA's own
           if (nseg > 1) {
             for (int s0 = 1; s0 < nseg; s0 += P_MAXPIECE) {  // later pieces added in K order
               float pv[P_MAXPIECE][P_HALF];
@@ -421,7 +432,7 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
               }
             } else {
               const int vh = head - a.NH - a.NKV;
-              uint32_t packed[P_HALF / 2];  // this dimension's 16 tokens for V^T (zero past the prompt)
+              uint32_t packed[P_HALF / 2];  // this dimension's P_HALF tokens for V^T (zero past the prompt)
 #pragma unroll
               for (int i = 0; i < P_HALF; i += 2) {
                 const int t = t0 + i;
@@ -437,8 +448,8 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
             }
           } else if constexpr (EPI == PEPI_SWIGLU) {
             // rows r < 64 hold the gate and rows r + 64 the up projection of feature r: both rows
-            // land in the exchange buffer, then the thread of row r handles tokens 0..7 and the
-            // thread of row r + 64 tokens 8..15 of the half chunk
+            // land in the exchange buffer, then the thread of row r handles the first P_HALF/2
+            // tokens of the warpgroup's slice and the thread of row r + 64 the rest
 #pragma unroll
             for (int i = 0; i < P_HALF; i++) ys[r * P_YS_LD + i] = y[i];
             pf_sync_g(g);

@@ -187,6 +187,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// One 8-column piece of the 32x32b layout (columns [c, c+8) of this warp's 32 lanes).
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, float* v) {
+  uint32_t a[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; i++) v[i] = __uint_as_float(a[i]);
+}
+
 // Two 8-column pieces of the 32x32b layout (columns [c0, c0+8) and [c1, c1+8) of this warp's
 // 32 lanes), one wait for both.
 __device__ __forceinline__ void tmem_ld_32x32b_2x8(uint32_t taddr0, uint32_t taddr1, float* v0, float* v1) {
