@@ -507,9 +507,11 @@ __global__ void __launch_bounds__(64 + P_EPI, 1) pfgemm_kernel(const __grid_cons
 constexpr int kAQ = 32;               // query tokens per CTA (x 4 heads = 128 MMA rows)
 constexpr int kAK = 128;              // keys per chunk
 constexpr int kABox = 16384;          // one 128-row x 128-byte swizzled box
-constexpr int kAttnT = 64 + 256;      // TMA warp, MMA warp, two softmax warpgroups
-// smem: Q, K, V^T, P boxes | barriers and TMEM slot (128 B) | row max / sum halves [2][2][128]
-constexpr size_t kAttnTcSmem = 1024 + 12 * (size_t)kABox + 128 + 2 * 2 * 128 * 4;
+constexpr int kAttnG = 4;             // softmax / output warpgroups
+constexpr int kAttnKpt = kAK / kAttnG;  // keys of a chunk, and output dims, per softmax thread
+constexpr int kAttnT = 64 + 128 * kAttnG;  // TMA warp, MMA warp, the softmax warpgroups
+// smem: Q, K, V^T, P boxes | barriers and TMEM slot (128 B) | row max / sum parts [2][kAttnG][128]
+constexpr size_t kAttnTcSmem = 1024 + 12 * (size_t)kABox + 128 + 2 * kAttnG * 128 * 4;
 
 __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                             const __grid_constant__ CUtensorMap tmK,
@@ -529,8 +531,8 @@ __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_cons
   uint64_t* o_full = bar + 4;
   uint64_t* epi_done = bar + 5;        // the softmax threads are past their last TMEM read
   uint32_t* tmem_slot = (uint32_t*)(bar + 8);
-  float* red_m = (float*)(bar + 16);   // [2 halves][128 rows] partial row max
-  float* red_l = red_m + 2 * 128;      // [2 halves][128 rows] partial row sum
+  float* red_m = (float*)(bar + 16);   // [kAttnG][128 rows] partial row max
+  float* red_l = red_m + kAttnG * 128; // [kAttnG][128 rows] partial row sum
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, kvh = blockIdx.y;
@@ -541,9 +543,9 @@ __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_cons
     mbar_init(q_full, 1);
     mbar_init(kv_full, 1);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 256);
+    mbar_init(p_full, 128 * kAttnG);
     mbar_init(o_full, 1);
-    mbar_init(epi_done, 256);
+    mbar_init(epi_done, 128 * kAttnG);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
@@ -612,89 +614,86 @@ __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_cons
     __syncwarp();
     tmem_dealloc(tmem, 256);
   } else {
-    // softmax / output warps: two warpgroups over the same 128 TMEM lanes.  Thread (h, r) owns
-    // MMA row r = (token qt*32 + r/4, head 4*kvh + r%4) for keys 64h .. 64h+63 of every chunk
-    // and output dims 64h .. 64h+63; the row's max and sum meet in shared memory.
+    // softmax / output warps: kAttnG warpgroups over the same 128 TMEM lanes.  Thread (h, r) owns
+    // MMA row r = (token qt*32 + r/4, head 4*kvh + r%4) for keys kAttnKpt*h .. of every chunk and
+    // the same output dims; the row's max and sum meet in shared memory.  More warpgroups shorten
+    // the per-chunk softmax, which sits between the two MMAs of every chunk.
     const int h = (threadIdx.x - 64) >> 7;
     const int r = ((warp & 3) << 5) | lane;
     const int tok = qt * kAQ + (r >> 2);
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const float scale = 0.08838834764831845f;  // 1/sqrt(128)
-    float o[64];
+    float o[kAttnKpt];
 #pragma unroll
-    for (int j = 0; j < 64; j++) o[j] = 0.f;
+    for (int j = 0; j < kAttnKpt; j++) o[j] = 0.f;
     float m = -INFINITY, l = 0.f;
     uint8_t* prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
     for (int c = 0; c < nchunk; c++) {
       if (!mbar_wait(s_full, (uint32_t)c & 1u, ST_EPI_WAIT, &g_status_prefill)) break;
       __syncwarp();
       tc_fence_after();
+      float v[kAttnKpt];
+      tmem_ld_32x32b_x32(tS + lane_base + h * kAttnKpt, v);
       float cm = -INFINITY;
 #pragma unroll
-      for (int qq = 0; qq < 2; qq++) {
-        float v[32];
-        tmem_ld_32x32b_x32(tS + lane_base + h * 64 + qq * 32, v);
-#pragma unroll
-        for (int j = 0; j < 32; j++)
-          if (c * kAK + h * 64 + qq * 32 + j <= tok) cm = fmaxf(cm, v[j] * scale);
-      }
+      for (int j = 0; j < kAttnKpt; j++)
+        if (c * kAK + h * kAttnKpt + j <= tok) cm = fmaxf(cm, v[j] * scale);
       red_m[h * 128 + r] = cm;
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      const float mnew = fmaxf(m, fmaxf(red_m[r], red_m[128 + r]));
+      asm volatile("bar.sync 1, %0;" ::"n"(128 * kAttnG) : "memory");
+      float mx = red_m[r];
+#pragma unroll
+      for (int g2 = 1; g2 < kAttnG; g2++) mx = fmaxf(mx, red_m[g2 * 128 + r]);
+      const float mnew = fmaxf(m, mx);
       const float corr = m == -INFINITY ? 0.f : expf(m - mnew);
       float lsum = 0.f;
 #pragma unroll
-      for (int qq = 0; qq < 2; qq++) {
-        float v[32];
-        tmem_ld_32x32b_x32(tS + lane_base + h * 64 + qq * 32, v);
+      for (int g8 = 0; g8 < kAttnKpt / 8; g8++) {  // 8 keys = one 16-byte chunk of the swizzled row
+        uint32_t hw[4], lw[4];
 #pragma unroll
-        for (int g8 = 0; g8 < 4; g8++) {  // 8 keys = one 16-byte chunk of the swizzled row
-          uint32_t hw[4], lw[4];
+        for (int e = 0; e < 8; e += 2) {
+          float pp[2];
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            float pp[2];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-              const int j = g8 * 8 + e + u;
-              pp[u] = c * kAK + h * 64 + qq * 32 + j <= tok ? expf(v[j] * scale - mnew) : 0.f;
-              lsum += pp[u];
-            }
-            const uint16_t h0 = f2bf_bits(pp[0]), h1 = f2bf_bits(pp[1]);
-            hw[e / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-            lw[e / 2] = (uint32_t)f2bf_bits(pp[0] - bf2f(h0)) | ((uint32_t)f2bf_bits(pp[1] - bf2f(h1)) << 16);
+          for (int u = 0; u < 2; u++) {
+            const int j = g8 * 8 + e + u;
+            pp[u] = c * kAK + h * kAttnKpt + j <= tok ? expf(v[j] * scale - mnew) : 0.f;
+            lsum += pp[u];
           }
-          const int key16 = qq * 4 + g8;  // 16-byte chunk index within this half's 128-byte box row
-          const int ch = key16 ^ (r & 7);
-          *reinterpret_cast<uint4*>(prow + h * kABox + (ch << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4*>(prow + (2 + h) * kABox + (ch << 4)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          const uint16_t h0 = f2bf_bits(pp[0]), h1 = f2bf_bits(pp[1]);
+          hw[e / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+          lw[e / 2] = (uint32_t)f2bf_bits(pp[0] - bf2f(h0)) | ((uint32_t)f2bf_bits(pp[1] - bf2f(h1)) << 16);
         }
+        const int key = h * kAttnKpt + g8 * 8;        // first key of these 8 within the chunk
+        const int box = key >> 6;                      // 64 keys per 128-byte-wide box
+        const int ch = ((key & 63) >> 3) ^ (r & 7);   // its swizzled 16-byte chunk in the row
+        *reinterpret_cast<uint4*>(prow + box * kABox + (ch << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(prow + (2 + box) * kABox + (ch << 4)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
       red_l[h * 128 + r] = lsum;
       fence_proxy_async_smem();  // P is read by the tensor cores
       tc_fence_before();
       pf_arrive(p_full);
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      l = l * corr + (red_l[r] + red_l[128 + r]);
+      asm volatile("bar.sync 1, %0;" ::"n"(128 * kAttnG) : "memory");
+      float ls = red_l[r];
+#pragma unroll
+      for (int g2 = 1; g2 < kAttnG; g2++) ls += red_l[g2 * 128 + r];
+      l = l * corr + ls;
       m = mnew;
       if (!mbar_wait(o_full, (uint32_t)c & 1u, ST_EPI_WAIT, &g_status_prefill)) break;
       __syncwarp();
       tc_fence_after();
+      float w[kAttnKpt];
+      tmem_ld_32x32b_x32(tO + lane_base + h * kAttnKpt, w);
 #pragma unroll
-      for (int qq = 0; qq < 2; qq++) {
-        float v[32];
-        tmem_ld_32x32b_x32(tO + lane_base + h * 64 + qq * 32, v);
-#pragma unroll
-        for (int j = 0; j < 32; j++) o[qq * 32 + j] = fmaf(o[qq * 32 + j], corr, v[j]);
-      }
+      for (int j = 0; j < kAttnKpt; j++) o[j] = fmaf(o[j], corr, w[j]);
     }
     tc_fence_before();
     pf_arrive(epi_done);
     const float inv_l = 1.0f / l;
     const int head = kvh * 4 + (r & 3);
-    uint16_t* dh = act_o + (size_t)tok * ld_act + (size_t)head * 128 + h * 64;
-    uint16_t* dl = act_o + (size_t)(C + tok) * ld_act + (size_t)head * 128 + h * 64;
+    uint16_t* dh = act_o + (size_t)tok * ld_act + (size_t)head * 128 + h * kAttnKpt;
+    uint16_t* dl = act_o + (size_t)(C + tok) * ld_act + (size_t)head * 128 + h * kAttnKpt;
 #pragma unroll
-    for (int d8 = 0; d8 < 8; d8++) {
+    for (int d8 = 0; d8 < kAttnKpt / 8; d8++) {
       uint32_t hw[4], lw[4];
 #pragma unroll
       for (int e = 0; e < 8; e += 2) {
