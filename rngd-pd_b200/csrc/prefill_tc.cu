@@ -37,7 +37,8 @@ constexpr int P_GROUPS = 4;    // epilogue warpgroups, each a quarter of every 3
 constexpr int P_EPI = 128 * P_GROUPS;  // epilogue threads
 constexpr int P_HALF = 32 / P_GROUPS;  // tokens of a chunk per warpgroup
 constexpr int P_YS_LD = P_HALF + 1;    // smem pitch (odd) of a warpgroup's [128][P_HALF] exchange buffer
-constexpr int P_MAXPIECE = 4;  // split-unit pieces whose loads are issued together
+constexpr int P_MAXPIECE = 2;  // split-unit pieces whose loads are issued together (4 spills at
+                               // the 96-register cap of the four-warpgroup epilogue and ran slower)
 
 // MT weight tiles (128 rows each) share every token tile: with MT = 2 a 64 KB stage
 // carries 32 KB of weights and 32 KB of activations (hi + lo) for twice the MMA work of
