@@ -53,6 +53,36 @@ def test_small_prefill_matches_numpy_oracle(small, P):
     assert eng.last_C == (128 if P <= 128 else 256)
 
 
+WIDE = R.Dims(H=512, M=4864, NH=8, NKV=2, HD=128, L=2, V=1000)
+
+
+@pytest.fixture(scope="module")
+def wide():
+    """A 512-token bucket over a model whose gate/up GEMM has 76 weight tiles: at C=512 it takes
+    two weight tiles per work unit (the MT=2 epilogue) and every other GEMM one, the
+    attention's last query tiles read four key chunks, and the O and down GEMMs (16 units over
+    148 CTAs) cut units into up to ten pieces."""
+    from rngd_pd.engines.prefill_full import FullPrefillEngine
+    from rngd_pd.synth import SyntheticState
+    cfg = _cfg(WIDE)
+    return FullPrefillEngine(cfg, SyntheticState(cfg, seed=0), C=512, group=1, S=512), R.SynthModel(WIDE, seed=0)
+
+
+@pytest.mark.parametrize("P", [300, 512])
+def test_wide_512_token_bucket_matches_numpy_oracle(wide, P):
+    eng, m = wide
+    toks = [(13 * i + 7) % WIDE.V for i in range(P)]
+    K, V, nxt = eng.prefill(toks)
+    Kr, Vr, lgr = R.prefill(m, toks, eng.S, kv_bf16=True)
+    np.testing.assert_allclose(K, Kr, rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(V, Vr, rtol=1e-2, atol=1e-2)
+    assert not K[..., P:].any() and not V[:, :, P:].any()
+    lg = eng.logits().cpu().numpy()
+    np.testing.assert_allclose(lg, lgr, rtol=1e-3, atol=2e-3)
+    assert nxt == int(np.argmax(lgr))
+    assert eng.last_C == 512
+
+
 def test_stage_stream_and_device_paths_agree(small):
     eng, _ = small
     toks = [(11 * i + 5) % SMALL.V for i in range(150)]
