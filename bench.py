@@ -545,6 +545,7 @@ def prefill_timeline(eng, layers=2):
     finally:
         _lib.call("rngd_trace_decode_gemms", None, 0)
     out = []
+    prev_end = None
     for i in range(n):
         t = tr[i].cpu().double()
         t = t[t[:, 0] > 0]
@@ -560,6 +561,11 @@ def prefill_timeline(eng, layers=2):
         row["last_unit_epi_by_owners"] = {int(k): round(float(((t[own & (t[:, 8] == k), 6] - t[own & (t[:, 8] == k), 5])
                                                                 / 1e3).median()), 1)
                                           for k in sorted(set(t[own, 8].long().tolist()))}
+        # from the previous traced GEMM's last epilogue to this launch's dependency release: the
+        # kernels in between (for O, the attention) and the boundary
+        row["dep_after_prev_end"] = (round(float((t[:, 1].median() - prev_end) / 1e3), 1)
+                                     if prev_end is not None else None)
+        prev_end = float(t[:, 6].max())
         out.append(row)
     del pf
     return out

@@ -526,7 +526,8 @@ __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_cons
   uint8_t* sP = sV + 2 * kABox;        // [hi keys 0-63, hi keys 64-127, lo keys 0-63, lo keys 64-127]
   uint64_t* bar = (uint64_t*)(sP + 4 * kABox);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;
+  uint64_t* k_full = bar + 1;          // the chunk's K boxes
+  uint64_t* v_full = bar + 6;          // the chunk's V^T boxes
   uint64_t* s_full = bar + 2;
   uint64_t* p_full = bar + 3;
   uint64_t* o_full = bar + 4;
@@ -542,7 +543,8 @@ __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(kv_full, 1);
+    mbar_init(k_full, 1);
+    mbar_init(v_full, 1);
     mbar_init(s_full, 1);
     mbar_init(p_full, 128 * kAttnG);
     mbar_init(o_full, 1);
@@ -569,13 +571,15 @@ __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_cons
       for (int hl = 0; hl < 2; hl++)
         for (int bx = 0; bx < 2; bx++)
           tma_load_3d(sQ + (hl * 2 + bx) * kABox, &tmQ, q_full, bx * 64, kvh * 4, hl * C + qt * kAQ);
+      // K of chunk c is loaded once S of chunk c-1 is done (during its softmax), V once P V of
+      // chunk c-1 is done
       for (int c = 0; c < nchunk; c++) {
+        if (c > 0 && !mbar_wait(s_full, (uint32_t)(c - 1) & 1u, ST_TMA_WAIT, &g_status_prefill)) break;
+        mbar_arrive_expect_tx(k_full, 2 * kABox);
+        for (int bx = 0; bx < 2; bx++) tma_load_3d(sK + bx * kABox, &tmK, k_full, bx * 64, c * kAK, kvh);
         if (c > 0 && !mbar_wait(o_full, (uint32_t)(c - 1) & 1u, ST_TMA_WAIT, &g_status_prefill)) break;
-        mbar_arrive_expect_tx(kv_full, 4 * kABox);
-        for (int bx = 0; bx < 2; bx++) {
-          tma_load_3d(sK + bx * kABox, &tmK, kv_full, bx * 64, c * kAK, kvh);
-          tma_load_3d(sV + bx * kABox, &tmV, kv_full, c * kAK + bx * 64, 0, kvh);
-        }
+        mbar_arrive_expect_tx(v_full, 2 * kABox);
+        for (int bx = 0; bx < 2; bx++) tma_load_3d(sV + bx * kABox, &tmV, v_full, c * kAK + bx * 64, 0, kvh);
       }
       grid_dep_launch();
     }
@@ -585,7 +589,7 @@ __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_cons
       const uint32_t idesc = idesc_bf16_f32(128, 128);
       bool ok = mbar_wait(q_full, 0, ST_MMA_WAIT, &g_status_prefill);
       for (int c = 0; c < nchunk && ok; c++) {
-        ok = mbar_wait(kv_full, (uint32_t)c & 1u, ST_MMA_WAIT, &g_status_prefill);
+        ok = mbar_wait(k_full, (uint32_t)c & 1u, ST_MMA_WAIT, &g_status_prefill);
         if (!ok) break;
         tc_fence_after();
         // S = (Qhi + Qlo) K^T over HD = 2 boxes x 4 K-steps
@@ -596,7 +600,8 @@ __global__ void __launch_bounds__(kAttnT, 1) pf_attn_tc_kernel(const __grid_cons
           umma_bf16(tS, sw128_kmajor_desc(smem_u32(sQ) + 2 * kABox + off), kd, idesc, 1u);
         }
         umma_commit(s_full);
-        ok = mbar_wait(p_full, (uint32_t)c & 1u, ST_MMA_WAIT, &g_status_prefill);
+        ok = mbar_wait(p_full, (uint32_t)c & 1u, ST_MMA_WAIT, &g_status_prefill) &&
+             mbar_wait(v_full, (uint32_t)c & 1u, ST_MMA_WAIT, &g_status_prefill);
         if (!ok) break;
         tc_fence_after();
         // O_c = (Phi + Plo) V over the chunk's 128 keys = 2 boxes x 4 K-steps
