@@ -612,7 +612,9 @@ def prefill_chunk_measure(eng, reps=3, warmup=1):
 def handoff_pairs(rank, world, dev, reps, warmup):
     """Config 3 across processes: GPU 2i prefills (seeded caches) and pushes into GPU 2i+1's
     decode cache, mapped through CUDA IPC; 1/4/16 requests per batch.  Returns, on every rank,
-    {requests: max-over-senders ms} and whether every receiver's lanes were byte-exact."""
+    {requests: max-over-senders ms} of the handoff kernel, of a copy-engine peer copy and of NCCL
+    send/recv moving the same requests (the two comparators), and whether every receiver's lanes
+    were byte-exact."""
     import ctypes
     import torch
     import torch.distributed as dist
@@ -635,7 +637,7 @@ def handoff_pairs(rank, world, dev, reps, warmup):
     dist.all_gather_object(metas, None if sender else t.handshake_metadata())
     key = t.set_remote_handshake(metas[partner]) if sender else None
     s = torch.cuda.Stream(device=dev)
-    out, copies, exact = {}, {}, True
+    out, copies, nccl, exact = {}, {}, {}, True
     pdev = torch.device("cuda", partner)
     for n in HANDOFF_BATCHES:
         times = []
@@ -694,12 +696,36 @@ def handoff_pairs(rank, world, dev, reps, warmup):
         cm = torch.tensor([statistics.median(cms) if cms else 0.0], device=dev)
         dist.all_reduce(cm, op=dist.ReduceOp.MAX)
         copies[n] = float(cm.item())
+        # NCCL point-to-point moving the same requests (send on GPU 2i, recv on GPU 2i+1): the
+        # library comparator.  Every rank posts its side of the batch; device time of the batch on
+        # each rank, max over ranks
+        rbuf = None if sender else torch.empty((n, L, 2, NKV, S, HD), dtype=torch.bfloat16, device=dev)
+        nms = []
+        for rep in range(warmup + reps):
+            if sender:
+                ops = [dist.P2POp(dist.isend, kvs[(rep * n + b) % B].contiguous(), partner) for b in range(n)]
+            else:
+                ops = [dist.P2POp(dist.irecv, rbuf[b], partner) for b in range(n)]
+            dist.barrier()
+            cur = torch.cuda.current_stream(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+            e1.record(cur)
+            e1.synchronize()
+            if rep >= warmup:
+                nms.append(e0.elapsed_time(e1))
+        del rbuf
+        nm = torch.tensor([statistics.median(nms)], device=dev)
+        dist.all_reduce(nm, op=dist.ReduceOp.MAX)
+        nccl[n] = float(nm.item())
     ok = torch.tensor([1 if exact else 0], device=dev)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     t.close()                      # senders unmap before receivers free
     dist.barrier()
     del K, V, kvs
-    return out, copies, bool(ok.item())
+    return out, copies, nccl, bool(ok.item())
 
 
 def run_micro_step_small(args):
@@ -1139,7 +1165,7 @@ def run_ours(args):
     per_req = handoff_bytes(_MC.llama31_8b())
     hreps = 10
     if world >= 2 and world % 2 == 0:
-        hms, hcopy, hexact = handoff_pairs(rank, world, dev, hreps, 3)
+        hms, hcopy, hnccl, hexact = handoff_pairs(rank, world, dev, hreps, 3)
         pairs = world // 2
         handoff = {"unit": "GB/s", "pairs": pairs, "per_request_bytes": per_req, "byte_exact": hexact,
                    "path": "GPU 2i -> GPU 2i+1, separate processes, CUDA IPC + NVLink P2P stores",
@@ -1148,7 +1174,9 @@ def run_ours(args):
                                 "peak": n * per_req / hcopy[n] / 1e6, "peak_kind": "peer copy of the same bytes, "
                                 "measured here (max over pairs)",
                                 "frac": hcopy[n] / ms, "frac_of_nominal": n * per_req / ms / 1e6 / NVLINK_NOMINAL_GBS,
-                                "nominal_gbs": NVLINK_NOMINAL_GBS, "bound": "nvlink"} for n, ms in hms.items()]}
+                                "nominal_gbs": NVLINK_NOMINAL_GBS, "bound": "nvlink",
+                                "nccl_ms": hnccl[n], "nccl_gbs_per_pair": n * per_req / hnccl[n] / 1e6}
+                               for n, ms in hms.items()]}
     elif rank == 0:
         rows = handoff_one_process([local], hreps, 3)
         handoff = {"unit": "GB/s", "pairs": 0, "per_request_bytes": per_req,
